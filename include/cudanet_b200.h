@@ -1,0 +1,122 @@
+/* The C ABI of libcudanet_b200.so, the B200 (sm_100a) evaluator of MayFly's network.
+ *
+ * The first seven entry points are the reference backend's C ABI, same names, arguments, meaning and error
+ * behaviour: mayfly/chess/cudanet/cudanet_capi.h:15-37 (implementation cudanet/cudanet_capi.cpp:31-124). A
+ * caller of cudanet.dll (cudanet/cudanet_py.py, cudanet/cudanet_backend.cpp) binds these unchanged. Everything
+ * after them is additive.
+ *
+ * Conventions (as in the reference): C++ exceptions never cross this boundary; a failing call returns NULL or
+ * -1 and writes a NUL-terminated reason, cut to err_len bytes, into err. The caller owns every host buffer; the
+ * library copies inputs into its own pinned staging and copies outputs out before returning. A handle owns
+ * the weights, buffers, stream and CUDA graphs on one device. Calls on one handle are serialised by a mutex;
+ * any thread may call (the device is made current on each call).
+ *
+ * Sizes: B positions (1..max_batch), wide legal-move slots per row (1..256). ids [B*64] piece ids 0..12 in
+ * the side to move's frame, cast [B*4], hm [B] halfmove bucket 0..101, ep [B] en passant square + 1 or 0,
+ * I [B*wide] policy indices 0..4161 of the legal moves, M [B*wide] nonzero on legal slots. Outputs: pol
+ * [B*wide] raw policy logits at the legal moves (0 on padding), val [B] in [-1, 1], qv [B*wide] 2*sigmoid(q)-1
+ * (0 on padding).
+ */
+#ifndef CUDANET_B200_H
+#define CUDANET_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CUDANET_API __attribute__((visibility("default")))
+#else
+#define CUDANET_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- the reference's ABI (cudanet_capi.h) */
+
+/* cudanet_capi.h:16. Load a weight file (MFCNW001: version 1 with f16 matrices, or version 2 with bf16
+ * matrices) onto `device`. Returns a handle, or NULL with the reason in err. The largest batch is 1024, or env
+ * MAYFLY_CUDANET_MAX_BATCH (1..16384) read here. */
+CUDANET_API void* cudanet_create(const char* weights_path, int device, char* err, int err_len);
+
+/* cudanet_capi.h:20-22. One batch, synchronous. Returns 0, or -1 with the reason in err. */
+CUDANET_API int cudanet_evaluate(void* handle, int B, int wide, const int64_t* ids, const float* cast,
+                                 const int64_t* hm, const int64_t* ep, const int64_t* I, const uint8_t* M,
+                                 float* pol, float* val, float* qv, char* err, int err_len);
+
+/* cudanet_capi.h:25. The weight file's fingerprint (mcts_cpp.fingerprint of the model), copied into buf.
+ * Returns its length, or -1 on a null handle. */
+CUDANET_API int cudanet_fingerprint(void* handle, char* buf, int buf_len);
+
+/* cudanet_capi.h:28. The largest B the handle takes, -1 on a null handle. */
+CUDANET_API int cudanet_max_batch(void* handle);
+
+/* cudanet_capi.h:32. Milliseconds a pass takes by step at batch B (the mean of reps eager passes with an
+ * event after each step, every row an empty board), then last the whole pass as a CUDA graph, into ms (n
+ * slots). Returns how many were written, or -1 with the reason in err. */
+CUDANET_API int cudanet_profile(void* handle, int B, int reps, double* ms, int n, char* err, int err_len);
+
+/* cudanet_capi.h:35. The step names of cudanet_profile, comma separated, copied into buf. Returns their
+ * length. */
+CUDANET_API int cudanet_profile_names(char* buf, int buf_len);
+
+/* cudanet_capi.h:37. Never fails; a null handle is ignored. */
+CUDANET_API void cudanet_destroy(void* handle);
+
+/* ---------------------------------------------------------------- additive entry points */
+
+/* cudanet_evaluate, and also the full logits [B * 2*4162] f32 (policy logits, then qvalue logits) of every
+ * row, for parity tests against the reference model's raw heads. */
+CUDANET_API int cudanet_evaluate_logits(void* handle, int B, int wide, const int64_t* ids, const float* cast,
+                                        const int64_t* hm, const int64_t* ep, const int64_t* I,
+                                        const uint8_t* M, float* pol, float* val, float* qv, float* logits,
+                                        char* err, int err_len);
+
+/* The reference CudaNet::begin / CudaNet::end pair (cudanet/cudanet.h:31-37): begin copies the inputs and
+ * queues the whole pass, end waits for the oldest batch begun and copies its outputs out. At most two batches
+ * are in flight. Both return 0, or -1 with the reason in err. */
+CUDANET_API int cudanet_begin(void* handle, int B, int wide, const int64_t* ids, const float* cast,
+                              const int64_t* hm, const int64_t* ep, const int64_t* I, const uint8_t* M,
+                              char* err, int err_len);
+CUDANET_API int cudanet_end(void* handle, float* pol, float* val, float* qv, char* err, int err_len);
+
+/* The arithmetic the handle runs its products in: "f16" or "bf16". Returns the length, -1 on a null handle. */
+CUDANET_API int cudanet_precision(void* handle, char* buf, int buf_len);
+
+/* One batch whose inputs and outputs are already in device memory of the handle's device, queued on `stream`
+ * (a cudaStream_t, NULL for the legacy default stream) without waiting for it. The arrays are as for
+ * cudanet_evaluate. Device-side failures (a bounded wait that timed out) are reported by the next
+ * cudanet_check. Returns 0, or -1 with the reason in err. */
+CUDANET_API int cudanet_evaluate_device(void* handle, int B, int wide, const int64_t* ids, const float* cast,
+                                        const int64_t* hm, const int64_t* ep, const int64_t* I,
+                                        const uint8_t* M, float* pol, float* val, float* qv, void* stream,
+                                        char* err, int err_len);
+
+/* Wait for the handle's work, including work queued by cudanet_evaluate_device on `stream`, and report a
+ * device-side failure recorded since the last check. Returns 0, or -1 with the reason in err. */
+CUDANET_API int cudanet_check(void* handle, void* stream, char* err, int err_len);
+
+/* ---------------------------------------------------------------- single kernels, for unit tests
+ * Device pointers on the current device, queued on `stream`, synchronous (the call waits for the stream).
+ * dtype: 0 = f16, 1 = bf16. */
+
+/* C = A[M, K] * W[N, K]^T + epilogue, with epi 0: C 16-bit = acc + bias; 1: C 16-bit = gelu(acc + bias);
+ * 2: C f32 += acc + bias; 3: C f32 = acc + bias. C has leading dimension ldc (elements). K must be a multiple
+ * of 64 and A's, W's row pitch K elements. bn 0 picks the tile width, else 64, 128 or 256. */
+CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const void* W, const float* bias,
+                               void* C, int M, int N, int K, int ldc, void* stream, char* err, int err_len);
+
+/* att[rows, d] = per (board, head) softmax(q k^T / sqrt(d/heads)) v over the 65 tokens of each board, qkv
+ * [B*65, 3d]. */
+CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,
+                                    char* err, int err_len);
+
+/* h[i] = LayerNorm(x[i * row_stride]) (f32 in, 16-bit out), i < n, eps 1e-5. */
+CUDANET_API int cudanet_k_layernorm(int dtype, const float* x, const float* g, const float* b, void* h, int n,
+                                    int d, int row_stride, void* stream, char* err, int err_len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUDANET_B200_H */

@@ -1,0 +1,1116 @@
+// The evaluator's host runtime and its C ABI (include/cudanet_b200.h).
+//
+// One Net owns, on one device: the weights (one allocation, tensors at their 256-aligned file offsets), every
+// activation buffer for max_batch positions, one stream, a CUDA graph of the whole forward per batch size
+// (captured on its first use), pinned host staging for two batches in flight, and a device error word that
+// the kernels' bounded waits write. This is the role of the reference's CudaNet
+// (mayfly/chess/cudanet/cudanet.h:15-59, cudanet/cudanet.cpp:144-770), re-designed for sm_100a:
+//   * the products are this library's tcgen05 GEMMs (gemm.cuh), not cuBLASLt, fed by TMA tensor maps made
+//     once per buffer;
+//   * GELU and the residual adds are GEMM epilogues, the first LayerNorm is fused into the embedding;
+//   * kernels are compiled ahead of time for sm_100a (no NVRTC, no runtime library loading).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/cudanet_b200.h"
+#include "json_min.h"
+#include "trunk.cuh"
+
+namespace mf {
+
+// ------------------------------------------------------------------------------------------------ errors
+static void check_rt(cudaError_t e, const char* what, int line)
+{
+    if (e != cudaSuccess)
+        throw std::runtime_error(std::string("cudanet_b200: ") + what + " failed (line " + std::to_string(line) +
+                                 "): " + cudaGetErrorString(e));
+}
+#define RT(call) check_rt((call), #call, __LINE__)
+
+static const char* err_site_name(uint32_t site)
+{
+    switch (site) {
+        case kErrTmaFull: return "a tensor-core product waited too long for a TMA tile";
+        case kErrSmemEmpty: return "a TMA load waited too long for a free shared-memory stage";
+        case kErrTmemFull: return "an epilogue waited too long for its accumulator";
+        case kErrTmemEmpty: return "a tensor-core product waited too long for a free accumulator";
+        case kErrArgs: return "a kernel was launched with arguments it cannot handle";
+        default: return "unknown device error";
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ TMA maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    if (!fn) throw std::runtime_error("cudanet_b200: the driver has no cuTensorMapEncodeTiled");
+    return fn;
+}
+
+// A K-major 16-bit matrix [outer, inner] with row pitch `inner` elements, tiles of 64 x box_outer, 128-byte
+// swizzle (the layout sdesc_sw128 describes). Rows past `outer` read as zero.
+static CUtensorMap make_map(const void* base, bool bf16, uint64_t inner, uint64_t outer, uint32_t box_outer)
+{
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner * 2) % 16)
+        throw std::runtime_error("cudanet_b200: a TMA operand is not 16-byte aligned");
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {inner * 2};
+    const cuuint32_t box[2] = {64, box_outer};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = encode_tiled()(&m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                      2, const_cast<void*>(base), dims, strides, box, es,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        throw std::runtime_error("cudanet_b200: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return m;
+}
+
+// ------------------------------------------------------------------------------------------------ launchers
+template <typename T, int BN, int EPI>
+static void launch_gemm_bn(const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K, const float* bias,
+                           void* out, int ldc, uint32_t* err, int num_sms, cudaStream_t s)
+{
+    using C = GemmCfg<BN>;
+    // the shared-memory opt-in, once per instantiation and device (the first launch of a batch size is eager,
+    // never inside a graph capture)
+    static bool attr[64] = {};
+    int dev = 0;
+    RT(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw std::runtime_error("cudanet_b200: device index out of range");
+    if (!attr[dev]) {
+        RT(cudaFuncSetAttribute(gemm_tc_kernel<T, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)C::SMEM));
+        attr[dev] = true;
+    }
+    const int tiles = ((M + C::BM - 1) / C::BM) * ((N + BN - 1) / BN);
+    const int grid = std::min(tiles, num_sms);
+    gemm_tc_kernel<T, BN, EPI><<<grid, C::THREADS, C::SMEM, s>>>(ma, mb, M, N, K, bias, out, ldc, err);
+    RT(cudaGetLastError());
+}
+
+template <typename T, int BN>
+static void launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K,
+                            const float* bias, void* out, int ldc, uint32_t* err, int num_sms, cudaStream_t s)
+{
+    switch (epi) {
+        case kEpiBias: launch_gemm_bn<T, BN, kEpiBias>(ma, mb, M, N, K, bias, out, ldc, err, num_sms, s); break;
+        case kEpiBiasGelu:
+            launch_gemm_bn<T, BN, kEpiBiasGelu>(ma, mb, M, N, K, bias, out, ldc, err, num_sms, s);
+            break;
+        case kEpiResidual:
+            launch_gemm_bn<T, BN, kEpiResidual>(ma, mb, M, N, K, bias, out, ldc, err, num_sms, s);
+            break;
+        case kEpiF32: launch_gemm_bn<T, BN, kEpiF32>(ma, mb, M, N, K, bias, out, ldc, err, num_sms, s); break;
+        default: throw std::runtime_error("cudanet_b200: unknown epilogue");
+    }
+}
+
+// The widest tile that still gives every SM a tile (weights stream through fewer SMs otherwise).
+static int pick_bn(int M, int N, int num_sms)
+{
+    const int m_tiles = (M + 127) / 128;
+    for (int bn : {256, 128})
+        if (m_tiles * ((N + bn - 1) / bn) >= num_sms) return bn;
+    return 64;
+}
+
+template <typename T>
+static void launch_gemm(int epi, int bn, const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K,
+                        const float* bias, void* out, int ldc, uint32_t* err, int num_sms, cudaStream_t s)
+{
+    if (K % 64 || K <= 0) throw std::runtime_error("cudanet_b200: GEMM K must be a positive multiple of 64");
+    if (bn == 256) launch_gemm_epi<T, 256>(epi, ma, mb, M, N, K, bias, out, ldc, err, num_sms, s);
+    else if (bn == 128) launch_gemm_epi<T, 128>(epi, ma, mb, M, N, K, bias, out, ldc, err, num_sms, s);
+    else if (bn == 64) launch_gemm_epi<T, 64>(epi, ma, mb, M, N, K, bias, out, ldc, err, num_sms, s);
+    else throw std::runtime_error("cudanet_b200: tile width must be 64, 128 or 256");
+}
+
+template <typename T>
+static void launch_layernorm(const float* x, const float* g, const float* b, T* h, int n, int d, int row_stride,
+                             cudaStream_t s)
+{
+    const dim3 grid((n + 7) / 8), block(256);
+    switch (d) {
+        case 256: layernorm_kernel<T, 2><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f); break;
+        case 512: layernorm_kernel<T, 4><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f); break;
+        case 1024: layernorm_kernel<T, 8><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f); break;
+        default: throw std::runtime_error("cudanet_b200: width must be 256, 512 or 1024");
+    }
+    RT(cudaGetLastError());
+}
+
+template <typename T>
+static void launch_attention(const T* qkv, T* att, int B, int d, int heads, cudaStream_t s)
+{
+    const int dh = d / heads;
+    const dim3 grid(heads, B), block(kAttWarps * 32);
+    const float scale = 1.0f / std::sqrt(static_cast<float>(dh));
+    if (dh == 64) attention_kernel<T, 64><<<grid, block, 0, s>>>(qkv, att, d, scale);
+    else if (dh == 32) attention_kernel<T, 32><<<grid, block, 0, s>>>(qkv, att, d, scale);
+    else throw std::runtime_error("cudanet_b200: head width must be 32 or 64");
+    RT(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------------------------------------ weights
+struct Arch {
+    int d = 0, layers = 0, heads = 0, ff = 0, tokens = 0, moves = 0;
+};
+
+enum class Prec { F16, BF16 };
+
+struct TensorEntry {
+    std::string dtype;
+    std::vector<long long> shape;
+    size_t offset = 0, nbytes = 0;
+};
+
+// The weight file (mayfly/chess/cudanet/cudanet_spec.h:35-55; version 2 adds bf16 matrices), parsed,
+// checked (magic, version, numbers, every tensor with its dtype, shape, offset and size) and uploaded in one
+// device allocation (cudanet/weights.cpp:264 is the reference's reader).
+struct Weights {
+    Arch a;
+    Prec prec = Prec::BF16;
+    std::string fingerprint, source;
+    void* base = nullptr;
+    size_t bytes = 0;
+    std::map<std::string, TensorEntry> t;
+
+    ~Weights()
+    {
+        if (base) cudaFree(base);
+    }
+
+    [[noreturn]] static void fail(const std::string& path, const std::string& why)
+    {
+        throw std::runtime_error("cudanet_b200 weights " + path + ": " + why);
+    }
+
+    static int whole(const std::string& path, const JVal* v, const char* what)
+    {
+        if (!v || v->kind != JVal::Num || v->num != std::floor(v->num)) fail(path, std::string("no integer ") + what);
+        return static_cast<int>(v->num);
+    }
+
+    void load(const std::string& path)
+    {
+        std::ifstream f(path, std::ios::binary);
+        if (!f) fail(path, "cannot open");
+        std::vector<char> raw((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+        if (raw.size() < 12 || std::memcmp(raw.data(), "MFCNW001", 8) != 0) fail(path, "bad magic (not MFCNW001)");
+        uint32_t n = 0;
+        std::memcpy(&n, raw.data() + 8, 4);
+        if (12ull + n > raw.size()) fail(path, "header runs past the end");
+        const std::string js(raw.data() + 12, n);
+        const JVal h = JParser(js).parse();
+        const int version = whole(path, h.get("version"), "version");
+        if (version != 1 && version != 2) fail(path, "unknown version (this reader knows 1 and 2)");
+        a.d = whole(path, h.get("d"), "d");
+        a.layers = whole(path, h.get("layers"), "layers");
+        a.heads = whole(path, h.get("heads"), "heads");
+        a.ff = whole(path, h.get("ff"), "ff");
+        a.tokens = whole(path, h.get("tokens"), "tokens");
+        a.moves = whole(path, h.get("moves"), "moves");
+        if (const JVal* fp = h.get("fingerprint")) fingerprint = fp->str;
+        if (const JVal* src = h.get("source")) source = src->str;
+        std::string prec_name = version == 1 ? "f16" : "bf16";
+        if (const JVal* p = h.get("precision")) prec_name = p->str;
+        if (prec_name == "f16") prec = Prec::F16;
+        else if (prec_name == "bf16") prec = Prec::BF16;
+        else fail(path, "precision " + prec_name + " is not supported by this build (f16, bf16)");
+        check_arch(path);
+
+        const JVal* ts = h.get("tensors");
+        if (!ts || ts->kind != JVal::Arr) fail(path, "no tensor list");
+        const size_t start = (12ull + n + 255) / 256 * 256;
+        size_t end = 0;
+        for (const JVal& e : ts->arr) {
+            const JVal* nm = e.get("name");
+            if (!nm || nm->kind != JVal::Str) fail(path, "a tensor without a name");
+            TensorEntry te;
+            const JVal* dt = e.get("dtype");
+            te.dtype = dt ? dt->str : "";
+            const JVal* sh = e.get("shape");
+            if (!sh || sh->kind != JVal::Arr) fail(path, nm->str + ": no shape");
+            size_t count = 1;
+            for (const JVal& s : sh->arr) {
+                if (s.kind != JVal::Num || s.num < 0) fail(path, nm->str + ": bad shape");
+                te.shape.push_back(static_cast<long long>(s.num));
+                count *= static_cast<size_t>(s.num);
+            }
+            const JVal* off = e.get("offset");
+            const JVal* nb = e.get("nbytes");
+            if (!off || !nb) fail(path, nm->str + ": no offset or nbytes");
+            te.offset = static_cast<size_t>(off->num);
+            te.nbytes = static_cast<size_t>(nb->num);
+            size_t es = 0;
+            if (te.dtype == "f16" || te.dtype == "bf16") es = 2;
+            else if (te.dtype == "f32") es = 4;
+            else fail(path, nm->str + ": dtype " + te.dtype + " (f16, bf16 or f32 only)");
+            if (te.offset % 256) fail(path, nm->str + ": offset not 256-aligned");
+            if (te.nbytes != count * es) fail(path, nm->str + ": nbytes does not match dtype and shape");
+            if (start + te.offset + te.nbytes > raw.size()) fail(path, nm->str + ": runs past the end of the file");
+            end = std::max(end, te.offset + te.nbytes);
+            t[nm->str] = te;
+        }
+        check_tensors(path);
+        bytes = (end + 255) / 256 * 256;
+        RT(cudaMalloc(&base, bytes));
+        RT(cudaMemcpy(base, raw.data() + start, std::min(bytes, raw.size() - start), cudaMemcpyHostToDevice));
+    }
+
+    void check_arch(const std::string& path) const
+    {
+        char msg[256];
+        std::snprintf(msg, sizeof msg, "d=%d layers=%d heads=%d ff=%d tokens=%d moves=%d", a.d, a.layers, a.heads,
+                      a.ff, a.tokens, a.moves);
+        const bool ok = (a.d == 256 || a.d == 512 || a.d == 1024) && a.layers >= 1 && a.heads >= 1 &&
+                        a.d % a.heads == 0 && (a.d / a.heads == 32 || a.d / a.heads == 64) && a.ff >= 64 &&
+                        a.ff % 64 == 0 && a.tokens == kTokens && a.moves >= 1;
+        if (!ok)
+            fail(path, std::string(msg) +
+                           ": this build needs d in {256, 512, 1024}, head width 32 or 64, ff a multiple of 64 and "
+                           "65 tokens");
+    }
+
+    void check_tensors(const std::string& path) const
+    {
+        const std::string m16 = prec == Prec::F16 ? "f16" : "bf16";
+        const long long d = a.d, ff = a.ff, mv = a.moves;
+        std::vector<std::pair<std::string, std::pair<std::string, std::vector<long long>>>> want = {
+            {"piece", {"f32", {13, d}}}, {"pos", {"f32", {64, d}}},   {"cls", {"f32", {d}}},
+            {"cast_w", {"f32", {d, 4}}}, {"cast_b", {"f32", {d}}},    {"hm", {"f32", {102, d}}},
+            {"ep_mark", {"f32", {d}}},   {"ln_g", {"f32", {d}}},      {"ln_b", {"f32", {d}}},
+            {"heads_w", {m16, {2 * mv, d}}}, {"heads_b", {"f32", {2 * mv}}}};
+        for (int i = 0; i < a.layers; ++i) {
+            const std::string p = "L" + std::to_string(i) + ".";
+            want.push_back({p + "n1_g", {"f32", {d}}});
+            want.push_back({p + "n1_b", {"f32", {d}}});
+            want.push_back({p + "qkv_w", {m16, {3 * d, d}}});
+            want.push_back({p + "qkv_b", {"f32", {3 * d}}});
+            want.push_back({p + "out_w", {m16, {d, d}}});
+            want.push_back({p + "out_b", {"f32", {d}}});
+            want.push_back({p + "n2_g", {"f32", {d}}});
+            want.push_back({p + "n2_b", {"f32", {d}}});
+            want.push_back({p + "ff1_w", {m16, {ff, d}}});
+            want.push_back({p + "ff1_b", {"f32", {ff}}});
+            want.push_back({p + "ff2_w", {m16, {d, ff}}});
+            want.push_back({p + "ff2_b", {"f32", {d}}});
+        }
+        for (const auto& w : want) {
+            auto it = t.find(w.first);
+            if (it == t.end()) fail(path, w.first + " missing");
+            if (it->second.dtype != w.second.first) fail(path, w.first + ": dtype " + it->second.dtype + ", needs " + w.second.first);
+            if (it->second.shape != w.second.second) fail(path, w.first + ": shape differs from the architecture");
+        }
+    }
+
+    template <typename P = void> const P* ptr(const std::string& name) const
+    {
+        auto it = t.find(name);
+        if (it == t.end()) throw std::runtime_error("cudanet_b200 weights: no tensor named " + name);
+        return reinterpret_cast<const P*>(static_cast<const char*>(base) + it->second.offset);
+    }
+};
+
+// ------------------------------------------------------------------------------------------------ the net
+constexpr int kMaxWide = 256;              // widest I / M row (chess has at most 218 legal moves)
+constexpr int kDefaultMaxBatch = 1024;
+constexpr int kMaxBatchLimit = 16384;
+constexpr size_t kOutHeader = 256;         // the error word, then the outputs at this offset
+
+enum ProfOp { kPEmbed, kPLn1, kPQkv, kPAtt, kPOut, kPLn2, kPFf1, kPGelu, kPFf2, kPCls, kPHeads, kProfOps };
+static const char* const kProfNames = "embed,ln1,qkv,attention,out,ln2,ff1,gelu,ff2,cls_ln,heads,graph_pass";
+
+struct InLayout {
+    size_t ids, hm, ep, cast, I, M, total;
+};
+
+// Offsets of the inputs in the staging block: ids, hm, ep and cast depend on B alone, so a graph per B stays
+// valid whatever wide is (cudanet/cudanet.cpp:107-119 in_layout).
+static InLayout in_layout(int B, int wide)
+{
+    const size_t b = static_cast<size_t>(B), w = static_cast<size_t>(wide);
+    InLayout l;
+    l.ids = 0;
+    l.hm = l.ids + 8 * b * 64;
+    l.ep = l.hm + 8 * b;
+    l.cast = l.ep + 8 * b;
+    l.I = l.cast + 4 * b * 4;
+    l.M = l.I + 8 * b * w;
+    l.total = l.M + b * w;
+    return l;
+}
+
+struct LayerW {
+    const float *n1_g, *n1_b, *qkv_b, *out_b, *n2_g, *n2_b, *ff1_b, *ff2_b;
+    const void *qkv_w, *out_w, *ff1_w, *ff2_w;
+};
+
+class Net {
+public:
+    Net(const std::string& path, int device) { init(path, device); }
+    ~Net() { release(); }
+
+    std::mutex mu;
+
+    int max_batch() const { return max_batch_; }
+    const std::string& fingerprint() const { return w_.fingerprint; }
+    const char* precision() const { return w_.prec == Prec::F16 ? "f16" : "bf16"; }
+
+    void begin(int B, int wide, const int64_t* ids, const float* cast, const int64_t* hm, const int64_t* ep,
+               const int64_t* I, const uint8_t* M, bool queued, bool want_logits);
+    void end(float* pol, float* val, float* qv, float* logits);
+    void evaluate_device(int B, int wide, const int64_t* ids, const float* cast, const int64_t* hm,
+                         const int64_t* ep, const int64_t* I, const uint8_t* M, float* pol, float* val, float* qv,
+                         cudaStream_t s);
+    void check(cudaStream_t s);
+    std::vector<double> profile(int B, int reps);
+
+private:
+    int device_ = 0;
+    int max_batch_ = 0;
+    int num_sms_ = 148;
+    Weights w_;
+    std::vector<LayerW> L_;
+    size_t rows_pad_ = 0, cls_pad_ = 0;
+    float* x_ = nullptr;
+    void *h_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *ff_ = nullptr, *cls_ = nullptr;
+    float* logits_ = nullptr;
+    uint8_t* d_in_ = nullptr;
+    uint8_t* d_out_ = nullptr;
+    uint8_t* h_in_[2] = {nullptr, nullptr};
+    uint8_t* h_out_[2] = {nullptr, nullptr};
+    float* h_logits_[2] = {nullptr, nullptr};
+    cudaStream_t stream_ = nullptr;
+    cudaEvent_t done_[2] = {nullptr, nullptr};
+    std::map<int, cudaGraphExec_t> graphs_;
+    bool use_graph_ = true;
+    CUtensorMap map_h_, map_att_, map_ff_, map_cls_;
+    std::map<std::pair<const void*, int>, CUtensorMap> wmaps_;
+
+    struct Fly {
+        int B, wide, slot;
+        bool queued, logits;
+    };
+    Fly fly_[2];
+    int fly_n_ = 0;
+
+    // profiling marks
+    bool prof_on_ = false;
+    std::vector<cudaEvent_t> prof_ev_;
+    std::vector<int> prof_op_;
+    size_t prof_n_ = 0;
+
+    uint32_t* err_word() const { return reinterpret_cast<uint32_t*>(d_out_); }
+    bool bf16() const { return w_.prec == Prec::BF16; }
+
+    void init(const std::string& path, int device);
+    void release();
+    const CUtensorMap& wmap(const void* W, int N, int K, int bn);
+    void gemm(int epi, const CUtensorMap& ma, const void* W, int M, int N, int K, const float* bias, void* out,
+              int ldc, cudaStream_t s);
+    void forward_kernels(int B, cudaStream_t s);
+    void forward(int B, cudaStream_t s);
+    void capture(int B);
+    void mark(int op, cudaStream_t s);
+    void check_batch(int B) const
+    {
+        if (B >= 1 && B <= max_batch_) return;
+        std::string msg = "cudanet_b200: batch size " + std::to_string(B) + " outside 1.." + std::to_string(max_batch_);
+        if (B > max_batch_ && max_batch_ < kMaxBatchLimit) msg += " (env MAYFLY_CUDANET_MAX_BATCH sets the limit)";
+        throw std::runtime_error(msg);
+    }
+    template <typename T> void forward_t(int B, cudaStream_t s);
+};
+
+static int pick_max_batch()
+{
+    const char* e = std::getenv("MAYFLY_CUDANET_MAX_BATCH");
+    if (!e || !*e) return kDefaultMaxBatch;
+    char* end = nullptr;
+    const long v = std::strtol(e, &end, 10);
+    if (*end || v < 1 || v > kMaxBatchLimit)
+        throw std::runtime_error(std::string("cudanet_b200: MAYFLY_CUDANET_MAX_BATCH=") + e + " is not in 1.." +
+                                 std::to_string(kMaxBatchLimit));
+    return static_cast<int>(v);
+}
+
+void Net::init(const std::string& path, int device)
+{
+    device_ = device;
+    max_batch_ = pick_max_batch();
+    int ndev = 0;
+    RT(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev)
+        throw std::runtime_error("cudanet_b200: device " + std::to_string(device) + " not present (" +
+                                 std::to_string(ndev) + " devices)");
+    RT(cudaSetDevice(device_));
+    cudaDeviceProp prop;
+    RT(cudaGetDeviceProperties(&prop, device_));
+    if (prop.major != 10)
+        throw std::runtime_error(std::string("cudanet_b200: device ") + prop.name + " is sm_" +
+                                 std::to_string(prop.major) + std::to_string(prop.minor) +
+                                 "; this library is built for sm_100a (B200)");
+    num_sms_ = prop.multiProcessorCount;
+    try {
+        w_.load(path);
+        const Arch& a = w_.a;
+        for (int i = 0; i < a.layers; ++i) {
+            const std::string p = "L" + std::to_string(i) + ".";
+            LayerW l;
+            l.n1_g = w_.ptr<float>(p + "n1_g");
+            l.n1_b = w_.ptr<float>(p + "n1_b");
+            l.qkv_w = w_.ptr(p + "qkv_w");
+            l.qkv_b = w_.ptr<float>(p + "qkv_b");
+            l.out_w = w_.ptr(p + "out_w");
+            l.out_b = w_.ptr<float>(p + "out_b");
+            l.n2_g = w_.ptr<float>(p + "n2_g");
+            l.n2_b = w_.ptr<float>(p + "n2_b");
+            l.ff1_w = w_.ptr(p + "ff1_w");
+            l.ff1_b = w_.ptr<float>(p + "ff1_b");
+            l.ff2_w = w_.ptr(p + "ff2_w");
+            l.ff2_b = w_.ptr<float>(p + "ff2_b");
+            L_.push_back(l);
+        }
+        const size_t d = a.d, ff = a.ff;
+        rows_pad_ = (static_cast<size_t>(max_batch_) * kTokens + 127) / 128 * 128;
+        cls_pad_ = (static_cast<size_t>(max_batch_) + 127) / 128 * 128;
+        RT(cudaMalloc(&x_, rows_pad_ * d * 4));
+        RT(cudaMalloc(&h_, rows_pad_ * d * 2));
+        RT(cudaMalloc(&qkv_, rows_pad_ * 3 * d * 2));
+        RT(cudaMalloc(&att_, rows_pad_ * d * 2));
+        RT(cudaMalloc(&ff_, rows_pad_ * ff * 2));
+        RT(cudaMalloc(&cls_, cls_pad_ * d * 2));
+        RT(cudaMalloc(&logits_, cls_pad_ * 2 * a.moves * 4));
+        RT(cudaMemset(x_, 0, rows_pad_ * d * 4));
+        RT(cudaMemset(h_, 0, rows_pad_ * d * 2));
+        RT(cudaMemset(qkv_, 0, rows_pad_ * 3 * d * 2));
+        RT(cudaMemset(att_, 0, rows_pad_ * d * 2));
+        RT(cudaMemset(ff_, 0, rows_pad_ * ff * 2));
+        RT(cudaMemset(cls_, 0, cls_pad_ * d * 2));
+        const size_t in_bytes = in_layout(max_batch_, kMaxWide).total;
+        const size_t out_bytes = kOutHeader + 4 * static_cast<size_t>(max_batch_) * (2 * kMaxWide + 1);
+        RT(cudaMalloc(&d_in_, in_bytes));
+        RT(cudaMalloc(&d_out_, out_bytes));
+        RT(cudaMemset(d_in_, 0, in_bytes));
+        RT(cudaMemset(d_out_, 0, out_bytes));
+        for (int s = 0; s < 2; ++s) {
+            RT(cudaMallocHost(&h_in_[s], in_bytes));
+            RT(cudaMallocHost(&h_out_[s], out_bytes));
+            RT(cudaMallocHost(&h_logits_[s], static_cast<size_t>(max_batch_) * 2 * a.moves * 4));
+            RT(cudaEventCreateWithFlags(&done_[s], cudaEventDisableTiming));
+        }
+        RT(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+        const bool b = bf16();
+        map_h_ = make_map(h_, b, d, rows_pad_, 128);
+        map_att_ = make_map(att_, b, d, rows_pad_, 128);
+        map_ff_ = make_map(ff_, b, ff, rows_pad_, 128);
+        map_cls_ = make_map(cls_, b, d, cls_pad_, 128);
+        const char* g = std::getenv("MAYFLY_CUDANET_GRAPH");
+        use_graph_ = !(g && std::strcmp(g, "0") == 0);
+        RT(cudaStreamSynchronize(stream_));
+    } catch (...) {
+        release();
+        throw;
+    }
+}
+
+void Net::release()
+{
+    cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
+    graphs_.clear();
+    for (cudaEvent_t e : prof_ev_) cudaEventDestroy(e);
+    prof_ev_.clear();
+    void* dev[] = {x_, h_, qkv_, att_, ff_, cls_, logits_, d_in_, d_out_};
+    for (void* p : dev)
+        if (p) cudaFree(p);
+    x_ = nullptr;
+    h_ = qkv_ = att_ = ff_ = cls_ = nullptr;
+    logits_ = nullptr;
+    d_in_ = d_out_ = nullptr;
+    for (int s = 0; s < 2; ++s) {
+        if (h_in_[s]) cudaFreeHost(h_in_[s]);
+        if (h_out_[s]) cudaFreeHost(h_out_[s]);
+        if (h_logits_[s]) cudaFreeHost(h_logits_[s]);
+        if (done_[s]) cudaEventDestroy(done_[s]);
+        h_in_[s] = h_out_[s] = nullptr;
+        h_logits_[s] = nullptr;
+        done_[s] = nullptr;
+    }
+    if (stream_) cudaStreamDestroy(stream_);
+    stream_ = nullptr;
+}
+
+const CUtensorMap& Net::wmap(const void* W, int N, int K, int bn)
+{
+    const auto key = std::make_pair(W, bn);
+    auto it = wmaps_.find(key);
+    if (it != wmaps_.end()) return it->second;
+    return wmaps_[key] = make_map(W, bf16(), static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                                  static_cast<uint32_t>(bn));
+}
+
+void Net::gemm(int epi, const CUtensorMap& ma, const void* W, int M, int N, int K, const float* bias, void* out,
+               int ldc, cudaStream_t s)
+{
+    const int bn = pick_bn(M, N, num_sms_);
+    const CUtensorMap& mb = wmap(W, N, K, bn);
+    if (bf16())
+        launch_gemm<__nv_bfloat16>(epi, bn, ma, mb, M, N, K, bias, out, ldc, err_word(), num_sms_, s);
+    else
+        launch_gemm<__half>(epi, bn, ma, mb, M, N, K, bias, out, ldc, err_word(), num_sms_, s);
+}
+
+void Net::mark(int op, cudaStream_t s)
+{
+    if (!prof_on_) return;
+    if (prof_n_ >= prof_ev_.size()) {
+        cudaEvent_t e;
+        RT(cudaEventCreate(&e));
+        prof_ev_.push_back(e);
+        prof_op_.push_back(0);
+    }
+    RT(cudaEventRecord(prof_ev_[prof_n_], s));
+    prof_op_[prof_n_] = op;
+    ++prof_n_;
+}
+
+template <typename T> void Net::forward_t(int B, cudaStream_t s)
+{
+    const Arch& a = w_.a;
+    const int rows = B * kTokens, d = a.d, ff = a.ff;
+    const InLayout lay = in_layout(B, 1);
+    const int64_t* ids = reinterpret_cast<const int64_t*>(d_in_ + lay.ids);
+    const int64_t* hm = reinterpret_cast<const int64_t*>(d_in_ + lay.hm);
+    const int64_t* ep = reinterpret_cast<const int64_t*>(d_in_ + lay.ep);
+    const float* cast = reinterpret_cast<const float*>(d_in_ + lay.cast);
+    T* h = static_cast<T*>(h_);
+    mark(kPEmbed, s);
+    {
+        const dim3 grid((rows + 7) / 8), block(256);
+        const float* args_f[] = {w_.ptr<float>("piece"), w_.ptr<float>("pos"), w_.ptr<float>("cls"),
+                                 w_.ptr<float>("cast_w"), w_.ptr<float>("cast_b"), w_.ptr<float>("hm"),
+                                 w_.ptr<float>("ep_mark")};
+        switch (d) {
+            case 256:
+                embed_ln_kernel<T, 2><<<grid, block, 0, s>>>(ids, cast, hm, ep, args_f[0], args_f[1], args_f[2],
+                                                              args_f[3], args_f[4], args_f[5], args_f[6], L_[0].n1_g,
+                                                              L_[0].n1_b, x_, h, rows, 1e-5f);
+                break;
+            case 512:
+                embed_ln_kernel<T, 4><<<grid, block, 0, s>>>(ids, cast, hm, ep, args_f[0], args_f[1], args_f[2],
+                                                              args_f[3], args_f[4], args_f[5], args_f[6], L_[0].n1_g,
+                                                              L_[0].n1_b, x_, h, rows, 1e-5f);
+                break;
+            default:
+                embed_ln_kernel<T, 8><<<grid, block, 0, s>>>(ids, cast, hm, ep, args_f[0], args_f[1], args_f[2],
+                                                              args_f[3], args_f[4], args_f[5], args_f[6], L_[0].n1_g,
+                                                              L_[0].n1_b, x_, h, rows, 1e-5f);
+        }
+        RT(cudaGetLastError());
+    }
+    for (int i = 0; i < a.layers; ++i) {
+        const LayerW& l = L_[static_cast<size_t>(i)];
+        mark(kPLn1, s);
+        if (i > 0) launch_layernorm<T>(x_, l.n1_g, l.n1_b, h, rows, d, 1, s);
+        mark(kPQkv, s);
+        gemm(kEpiBias, map_h_, l.qkv_w, rows, 3 * d, d, l.qkv_b, qkv_, 3 * d, s);
+        mark(kPAtt, s);
+        launch_attention<T>(static_cast<const T*>(qkv_), static_cast<T*>(att_), B, d, a.heads, s);
+        mark(kPOut, s);
+        gemm(kEpiResidual, map_att_, l.out_w, rows, d, d, l.out_b, x_, d, s);
+        mark(kPLn2, s);
+        launch_layernorm<T>(x_, l.n2_g, l.n2_b, h, rows, d, 1, s);
+        mark(kPFf1, s);
+        gemm(kEpiBiasGelu, map_h_, l.ff1_w, rows, ff, d, l.ff1_b, ff_, ff, s);
+        mark(kPFf2, s);
+        gemm(kEpiResidual, map_ff_, l.ff2_w, rows, d, ff, l.ff2_b, x_, d, s);
+    }
+    mark(kPCls, s);
+    launch_layernorm<T>(x_, w_.ptr<float>("ln_g"), w_.ptr<float>("ln_b"), static_cast<T*>(cls_), B, d, kTokens, s);
+    mark(kPHeads, s);
+    gemm(kEpiF32, map_cls_, w_.ptr("heads_w"), B, 2 * a.moves, d, w_.ptr<float>("heads_b"), logits_, 2 * a.moves, s);
+    mark(kPHeads, s);
+}
+
+void Net::forward_kernels(int B, cudaStream_t s)
+{
+    if (bf16()) forward_t<__nv_bfloat16>(B, s);
+    else forward_t<__half>(B, s);
+}
+
+void Net::capture(int B)
+{
+    RT(cudaStreamSynchronize(stream_));
+    RT(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    cudaGraph_t g = nullptr;
+    try {
+        forward_kernels(B, stream_);
+    } catch (...) {
+        cudaStreamEndCapture(stream_, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    RT(cudaStreamEndCapture(stream_, &g));
+    cudaGraphExec_t e = nullptr;
+    const cudaError_t err = cudaGraphInstantiate(&e, g, 0);
+    cudaGraphDestroy(g);
+    check_rt(err, "cudaGraphInstantiate", __LINE__);
+    graphs_[B] = e;
+}
+
+// The whole pass for B rows on stream s: the graph when there is one, else eager (the first use of B runs
+// eager, which also makes every launch's one-time set-up happen outside a capture, then captures).
+void Net::forward(int B, cudaStream_t s)
+{
+    auto it = graphs_.find(B);
+    if (it != graphs_.end()) {
+        RT(cudaGraphLaunch(it->second, s));
+        return;
+    }
+    forward_kernels(B, s);
+    if (!use_graph_) return;
+    RT(cudaStreamSynchronize(s));
+    try {
+        capture(B);
+    } catch (const std::exception& ex) {
+        std::fprintf(stderr, "cudanet_b200: CUDA graph capture failed at B=%d, eager from now on: %.300s\n", B,
+                     ex.what());
+        use_graph_ = false;
+        cudaGetLastError();
+    }
+}
+
+void Net::begin(int B, int wide, const int64_t* ids, const float* cast, const int64_t* hm, const int64_t* ep,
+                const int64_t* I, const uint8_t* M, bool queued, bool want_logits)
+{
+    check_batch(B);
+    if (wide < 1 || wide > kMaxWide)
+        throw std::runtime_error("cudanet_b200: wide " + std::to_string(wide) + " outside 1.." +
+                                 std::to_string(kMaxWide));
+    if (!ids || !cast || !hm || !ep || !I || !M) throw std::runtime_error("cudanet_b200: a null input pointer");
+    if (fly_n_ == 2) throw std::runtime_error("cudanet_b200: begin with two batches already in flight");
+    if (fly_n_ && !queued) throw std::runtime_error("cudanet_b200: evaluate while a batch is in flight");
+    const int slot = fly_n_ ? 1 - fly_[0].slot : 0;
+    RT(cudaSetDevice(device_));
+    const size_t b = static_cast<size_t>(B), wd = static_cast<size_t>(wide);
+    const InLayout lay = in_layout(B, wide);
+    uint8_t* hin = h_in_[slot];
+    std::memcpy(hin + lay.ids, ids, 8 * b * 64);
+    std::memcpy(hin + lay.hm, hm, 8 * b);
+    std::memcpy(hin + lay.ep, ep, 8 * b);
+    std::memcpy(hin + lay.cast, cast, 4 * b * 4);
+    std::memcpy(hin + lay.I, I, 8 * b * wd);
+    std::memcpy(hin + lay.M, M, b * wd);
+    RT(cudaMemcpyAsync(d_in_, hin, lay.total, cudaMemcpyHostToDevice, stream_));
+    forward(B, stream_);
+    const int64_t* I_d = reinterpret_cast<const int64_t*>(d_in_ + lay.I);
+    const uint8_t* M_d = d_in_ + lay.M;
+    float* pol_d = reinterpret_cast<float*>(d_out_ + kOutHeader);
+    float* val_d = pol_d + b * wd;
+    float* qv_d = val_d + b;
+    heads_post_kernel<<<(B + 7) / 8, 256, 0, stream_>>>(logits_, I_d, M_d, B, wide, w_.a.moves, pol_d, val_d, qv_d);
+    RT(cudaGetLastError());
+    RT(cudaMemcpyAsync(h_out_[slot], d_out_, kOutHeader + 4 * b * (2 * wd + 1), cudaMemcpyDeviceToHost, stream_));
+    if (want_logits)
+        RT(cudaMemcpyAsync(h_logits_[slot], logits_, 4 * b * 2 * w_.a.moves, cudaMemcpyDeviceToHost, stream_));
+    RT(cudaEventRecord(done_[slot], stream_));
+    fly_[fly_n_++] = Fly{B, wide, slot, queued, want_logits};
+}
+
+void Net::end(float* pol, float* val, float* qv, float* logits)
+{
+    if (!fly_n_) throw std::runtime_error("cudanet_b200: end with no batch in flight");
+    const Fly f = fly_[0];
+    fly_[0] = fly_[1];
+    fly_n_--;
+    RT(cudaSetDevice(device_));
+    RT(cudaEventSynchronize(done_[f.slot]));
+    const uint8_t* hout = h_out_[f.slot];
+    uint32_t errw = 0;
+    std::memcpy(&errw, hout, 4);
+    if (errw) {
+        // the context is still usable: clear the word for the next batch and report this one as failed
+        RT(cudaMemsetAsync(d_out_, 0, 4, stream_));
+        RT(cudaStreamSynchronize(stream_));
+        throw std::runtime_error(std::string("cudanet_b200: device error: ") + err_site_name(errw >> 8));
+    }
+    const size_t b = static_cast<size_t>(f.B), wd = static_cast<size_t>(f.wide);
+    const float* o = reinterpret_cast<const float*>(hout + kOutHeader);
+    if (pol) std::memcpy(pol, o, 4 * b * wd);
+    if (val) std::memcpy(val, o + b * wd, 4 * b);
+    if (qv) std::memcpy(qv, o + b * wd + b, 4 * b * wd);
+    if (logits && f.logits) std::memcpy(logits, h_logits_[f.slot], 4 * b * 2 * w_.a.moves);
+}
+
+void Net::evaluate_device(int B, int wide, const int64_t* ids, const float* cast, const int64_t* hm,
+                          const int64_t* ep, const int64_t* I, const uint8_t* M, float* pol, float* val, float* qv,
+                          cudaStream_t s)
+{
+    check_batch(B);
+    if (wide < 1 || wide > kMaxWide)
+        throw std::runtime_error("cudanet_b200: wide " + std::to_string(wide) + " outside 1.." +
+                                 std::to_string(kMaxWide));
+    if (fly_n_) throw std::runtime_error("cudanet_b200: evaluate_device while a batch is in flight");
+    RT(cudaSetDevice(device_));
+    const size_t b = static_cast<size_t>(B);
+    const InLayout lay = in_layout(B, 1);
+    RT(cudaMemcpyAsync(d_in_ + lay.ids, ids, 8 * b * 64, cudaMemcpyDeviceToDevice, s));
+    RT(cudaMemcpyAsync(d_in_ + lay.hm, hm, 8 * b, cudaMemcpyDeviceToDevice, s));
+    RT(cudaMemcpyAsync(d_in_ + lay.ep, ep, 8 * b, cudaMemcpyDeviceToDevice, s));
+    RT(cudaMemcpyAsync(d_in_ + lay.cast, cast, 16 * b, cudaMemcpyDeviceToDevice, s));
+    if (graphs_.find(B) == graphs_.end() && use_graph_) {
+        // the first use of B: make the graph on the handle's stream, ordered after the copies above
+        cudaEvent_t ev;
+        RT(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        RT(cudaEventRecord(ev, s));
+        RT(cudaStreamWaitEvent(stream_, ev, 0));
+        forward(B, stream_);
+        RT(cudaEventRecord(ev, stream_));
+        RT(cudaStreamWaitEvent(s, ev, 0));
+        RT(cudaEventDestroy(ev));
+    } else {
+        forward(B, s);
+    }
+    heads_post_kernel<<<(B + 7) / 8, 256, 0, s>>>(logits_, I, M, B, wide, w_.a.moves, pol, val, qv);
+    RT(cudaGetLastError());
+}
+
+void Net::check(cudaStream_t s)
+{
+    RT(cudaSetDevice(device_));
+    if (s) RT(cudaStreamSynchronize(s));
+    RT(cudaStreamSynchronize(stream_));
+    RT(cudaDeviceSynchronize());
+    uint32_t errw = 0;
+    RT(cudaMemcpy(&errw, d_out_, 4, cudaMemcpyDeviceToHost));
+    if (errw) {
+        RT(cudaMemset(d_out_, 0, 4));
+        throw std::runtime_error(std::string("cudanet_b200: device error: ") + err_site_name(errw >> 8));
+    }
+}
+
+std::vector<double> Net::profile(int B, int reps)
+{
+    check_batch(B);
+    if (reps < 1) reps = 1;
+    if (fly_n_) throw std::runtime_error("cudanet_b200: profile while a batch is in flight");
+    RT(cudaSetDevice(device_));
+    // an empty board in every row: ids, hm, ep and cast all zero
+    RT(cudaMemsetAsync(d_in_, 0, in_layout(B, 1).I, stream_));
+    forward_kernels(B, stream_);   // warm-up
+    std::vector<double> ms(kProfOps + 1, 0.0);
+    for (int r = 0; r < reps; ++r) {
+        prof_n_ = 0;
+        prof_on_ = true;
+        try {
+            forward_kernels(B, stream_);
+        } catch (...) {
+            prof_on_ = false;
+            throw;
+        }
+        prof_on_ = false;
+        RT(cudaEventSynchronize(prof_ev_[prof_n_ - 1]));
+        for (size_t i = 1; i < prof_n_; ++i) {
+            float t = 0.f;
+            RT(cudaEventElapsedTime(&t, prof_ev_[i - 1], prof_ev_[i]));
+            ms[static_cast<size_t>(prof_op_[i - 1])] += t;
+        }
+    }
+    forward(B, stream_);   // makes the graph if there is none yet
+    cudaEvent_t e0, e1;
+    RT(cudaEventCreate(&e0));
+    RT(cudaEventCreate(&e1));
+    for (int r = 0; r < reps; ++r) {
+        RT(cudaEventRecord(e0, stream_));
+        forward(B, stream_);
+        RT(cudaEventRecord(e1, stream_));
+        RT(cudaEventSynchronize(e1));
+        float t = 0.f;
+        RT(cudaEventElapsedTime(&t, e0, e1));
+        ms[kProfOps] += t;
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    for (double& v : ms) v /= reps;
+    check(nullptr);
+    return ms;
+}
+
+// ------------------------------------------------------------------------------------------------ C ABI glue
+static void put(char* err, int err_len, const char* msg)
+{
+    if (!err || err_len <= 0) return;
+    size_t n = std::strlen(msg);
+    if (n > static_cast<size_t>(err_len - 1)) n = static_cast<size_t>(err_len - 1);
+    std::memcpy(err, msg, n);
+    err[n] = 0;
+}
+
+template <typename F> static int guarded(char* err, int err_len, const char* what, F&& fn)
+{
+    put(err, err_len, "");
+    try {
+        return fn();
+    } catch (const std::exception& e) {
+        put(err, err_len, e.what());
+    } catch (...) {
+        put(err, err_len, what);
+    }
+    return -1;
+}
+
+}  // namespace mf
+
+using mf::Net;
+
+extern "C" {
+
+CUDANET_API void* cudanet_create(const char* weights_path, int device, char* err, int err_len)
+{
+    mf::put(err, err_len, "");
+    if (!weights_path) {
+        mf::put(err, err_len, "cudanet_create: no weights path");
+        return nullptr;
+    }
+    try {
+        return new Net(std::string(weights_path), device);
+    } catch (const std::exception& e) {
+        mf::put(err, err_len, e.what());
+    } catch (...) {
+        mf::put(err, err_len, "cudanet_create: unknown exception");
+    }
+    return nullptr;
+}
+
+CUDANET_API int cudanet_evaluate(void* handle, int B, int wide, const int64_t* ids, const float* cast,
+                                 const int64_t* hm, const int64_t* ep, const int64_t* I, const uint8_t* M,
+                                 float* pol, float* val, float* qv, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_evaluate: unknown exception", [&] {
+        if (!handle) throw std::runtime_error("cudanet_evaluate: null handle");
+        Net* n = static_cast<Net*>(handle);
+        std::lock_guard<std::mutex> lock(n->mu);
+        n->begin(B, wide, ids, cast, hm, ep, I, M, false, false);
+        n->end(pol, val, qv, nullptr);
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_evaluate_logits(void* handle, int B, int wide, const int64_t* ids, const float* cast,
+                                        const int64_t* hm, const int64_t* ep, const int64_t* I,
+                                        const uint8_t* M, float* pol, float* val, float* qv, float* logits,
+                                        char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_evaluate_logits: unknown exception", [&] {
+        if (!handle) throw std::runtime_error("cudanet_evaluate_logits: null handle");
+        Net* n = static_cast<Net*>(handle);
+        std::lock_guard<std::mutex> lock(n->mu);
+        n->begin(B, wide, ids, cast, hm, ep, I, M, false, true);
+        n->end(pol, val, qv, logits);
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_begin(void* handle, int B, int wide, const int64_t* ids, const float* cast,
+                              const int64_t* hm, const int64_t* ep, const int64_t* I, const uint8_t* M, char* err,
+                              int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_begin: unknown exception", [&] {
+        if (!handle) throw std::runtime_error("cudanet_begin: null handle");
+        Net* n = static_cast<Net*>(handle);
+        std::lock_guard<std::mutex> lock(n->mu);
+        n->begin(B, wide, ids, cast, hm, ep, I, M, true, false);
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_end(void* handle, float* pol, float* val, float* qv, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_end: unknown exception", [&] {
+        if (!handle) throw std::runtime_error("cudanet_end: null handle");
+        Net* n = static_cast<Net*>(handle);
+        std::lock_guard<std::mutex> lock(n->mu);
+        n->end(pol, val, qv, nullptr);
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_fingerprint(void* handle, char* buf, int buf_len)
+{
+    if (!handle) {
+        mf::put(buf, buf_len, "");
+        return -1;
+    }
+    const std::string& fp = static_cast<Net*>(handle)->fingerprint();
+    mf::put(buf, buf_len, fp.c_str());
+    return static_cast<int>(fp.size());
+}
+
+CUDANET_API int cudanet_max_batch(void* handle) { return handle ? static_cast<Net*>(handle)->max_batch() : -1; }
+
+CUDANET_API int cudanet_precision(void* handle, char* buf, int buf_len)
+{
+    if (!handle) {
+        mf::put(buf, buf_len, "");
+        return -1;
+    }
+    const char* p = static_cast<Net*>(handle)->precision();
+    mf::put(buf, buf_len, p);
+    return static_cast<int>(std::strlen(p));
+}
+
+CUDANET_API int cudanet_profile(void* handle, int B, int reps, double* ms, int n, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_profile: unknown exception", [&] {
+        if (!handle || !ms) throw std::runtime_error("cudanet_profile: null handle or output");
+        Net* net = static_cast<Net*>(handle);
+        std::lock_guard<std::mutex> lock(net->mu);
+        const std::vector<double> got = net->profile(B, reps);
+        const int k = static_cast<int>(got.size()) < n ? static_cast<int>(got.size()) : n;
+        for (int i = 0; i < k; ++i) ms[i] = got[static_cast<size_t>(i)];
+        return k;
+    });
+}
+
+CUDANET_API int cudanet_profile_names(char* buf, int buf_len)
+{
+    mf::put(buf, buf_len, mf::kProfNames);
+    return static_cast<int>(std::strlen(mf::kProfNames));
+}
+
+CUDANET_API void cudanet_destroy(void* handle)
+{
+    try {
+        delete static_cast<Net*>(handle);
+    } catch (...) {
+    }
+}
+
+CUDANET_API int cudanet_evaluate_device(void* handle, int B, int wide, const int64_t* ids, const float* cast,
+                                        const int64_t* hm, const int64_t* ep, const int64_t* I,
+                                        const uint8_t* M, float* pol, float* val, float* qv, void* stream,
+                                        char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_evaluate_device: unknown exception", [&] {
+        if (!handle) throw std::runtime_error("cudanet_evaluate_device: null handle");
+        if (!ids || !cast || !hm || !ep || !I || !M || !pol || !val || !qv)
+            throw std::runtime_error("cudanet_evaluate_device: a null pointer");
+        Net* n = static_cast<Net*>(handle);
+        std::lock_guard<std::mutex> lock(n->mu);
+        n->evaluate_device(B, wide, ids, cast, hm, ep, I, M, pol, val, qv, static_cast<cudaStream_t>(stream));
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_check(void* handle, void* stream, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_check: unknown exception", [&] {
+        if (!handle) throw std::runtime_error("cudanet_check: null handle");
+        Net* n = static_cast<Net*>(handle);
+        std::lock_guard<std::mutex> lock(n->mu);
+        n->check(static_cast<cudaStream_t>(stream));
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const void* W, const float* bias, void* C,
+                               int M, int N, int K, int ldc, void* stream, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_k_gemm: unknown exception", [&] {
+        if (dtype != 0 && dtype != 1) throw std::runtime_error("cudanet_k_gemm: dtype must be 0 (f16) or 1 (bf16)");
+        if (M < 1 || N < 1 || K < 64) throw std::runtime_error("cudanet_k_gemm: bad sizes");
+        int dev = 0;
+        mf::RT(cudaGetDevice(&dev));
+        int sms = 0;
+        mf::RT(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        if (bn == 0) bn = mf::pick_bn(M, N, sms);
+        if ((reinterpret_cast<uintptr_t>(C) | reinterpret_cast<uintptr_t>(bias)) & 15)
+            throw std::runtime_error("cudanet_k_gemm: C and bias must be 16-byte aligned");
+        if (ldc < N) throw std::runtime_error("cudanet_k_gemm: ldc < N");
+        const bool b16 = dtype == 1;
+        const CUtensorMap ma = mf::make_map(A, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
+        const CUtensorMap mb = mf::make_map(W, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                                            static_cast<uint32_t>(bn));
+        uint32_t* errw = nullptr;
+        mf::RT(cudaMalloc(&errw, 4));
+        mf::RT(cudaMemset(errw, 0, 4));
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        try {
+            if (b16) mf::launch_gemm<__nv_bfloat16>(epi, bn, ma, mb, M, N, K, bias, C, ldc, errw, sms, s);
+            else mf::launch_gemm<__half>(epi, bn, ma, mb, M, N, K, bias, C, ldc, errw, sms, s);
+            mf::RT(cudaStreamSynchronize(s));
+        } catch (...) {
+            cudaFree(errw);
+            throw;
+        }
+        uint32_t e = 0;
+        mf::RT(cudaMemcpy(&e, errw, 4, cudaMemcpyDeviceToHost));
+        cudaFree(errw);
+        if (e) throw std::runtime_error(std::string("cudanet_k_gemm: device error: ") + mf::err_site_name(e >> 8));
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,
+                                    char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_k_attention: unknown exception", [&] {
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (B < 1 || heads < 1 || d % heads) throw std::runtime_error("cudanet_k_attention: bad sizes");
+        if (dtype == 1)
+            mf::launch_attention<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(qkv),
+                                                static_cast<__nv_bfloat16*>(att), B, d, heads, s);
+        else if (dtype == 0)
+            mf::launch_attention<__half>(static_cast<const __half*>(qkv), static_cast<__half*>(att), B, d, heads, s);
+        else
+            throw std::runtime_error("cudanet_k_attention: dtype must be 0 (f16) or 1 (bf16)");
+        mf::RT(cudaStreamSynchronize(s));
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_k_layernorm(int dtype, const float* x, const float* g, const float* b, void* h, int n,
+                                    int d, int row_stride, void* stream, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_k_layernorm: unknown exception", [&] {
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (n < 1 || row_stride < 1) throw std::runtime_error("cudanet_k_layernorm: bad sizes");
+        if (dtype == 1) mf::launch_layernorm<__nv_bfloat16>(x, g, b, static_cast<__nv_bfloat16*>(h), n, d, row_stride, s);
+        else if (dtype == 0) mf::launch_layernorm<__half>(x, g, b, static_cast<__half*>(h), n, d, row_stride, s);
+        else throw std::runtime_error("cudanet_k_layernorm: dtype must be 0 (f16) or 1 (bf16)");
+        mf::RT(cudaStreamSynchronize(s));
+        return 0;
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,208 @@
+// Thin inline-PTX wrappers for sm_100a: mbarriers, TMA tile loads, and the tcgen05 tensor-core / tensor-memory
+// instructions. Every wait here is bounded: it gives up after a time limit, records where it gave up in the
+// device error word, and returns false so the caller can unwind (no kernel of this library can spin forever).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace mf {
+
+// ------------------------------------------------------------------------------------------------ error word
+// One 32-bit word in device memory per evaluator. 0 means no error. A kernel that gives up on a wait writes
+// (site << 8) | 1 with an atomic CAS so the first error is kept. The host reads it after each batch.
+enum ErrSite : uint32_t {
+    kErrTmaFull = 1,     // MMA warp waiting for a TMA stage
+    kErrSmemEmpty = 2,   // TMA warp waiting for the MMA to release a stage
+    kErrTmemFull = 3,    // epilogue waiting for an accumulator
+    kErrTmemEmpty = 4,   // MMA warp waiting for the epilogue to drain an accumulator
+    kErrArgs = 5,        // a kernel was launched with arguments it cannot handle
+};
+
+__device__ __forceinline__ void set_error(uint32_t* err, uint32_t site)
+{
+    if (err) atomicCAS(err, 0u, (site << 8) | 1u);
+}
+
+__device__ __forceinline__ uint64_t globaltimer()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// a wait longer than this (nanoseconds of %globaltimer) is a failure: the whole pass takes milliseconds
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------------------------------------ mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait until the barrier's phase with this parity has completed. False (and the error word set) on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t site)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 1023u) == 1023u && globaltimer() - t0 > kWaitLimitNs) {
+            set_error(err, site);
+            return false;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ TMA
+// A 2D tile load into shared memory that completes `bytes` of transaction on the barrier. x is the innermost
+// coordinate (elements); callers keep x a multiple of 16 bytes / element size.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map)
+{
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ------------------------------------------------------------------------------------------------ tcgen05
+// Tensor memory: 128 lanes x 512 columns of 32 bits per SM. An address is (lane << 16) | column.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish()
+{
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem]^T, one instruction of kind::f16 (f16 or bf16 inputs, f32 accumulator).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// The same for 8-bit float inputs (kind::f8f6f4; e4m3 x e4m3 here), f32 accumulator.
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive once on the barrier when every tcgen05.mma this thread issued before has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 lanes x 32 columns of 32 bits: thread t of the warp gets lane (base lane + t), columns col..col+31.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major tile stored with the 128-byte swizzle (what a TMA load with
+// CU_TENSOR_MAP_SWIZZLE_128B writes): rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte offset),
+// version 1 (bits 46-47), layout type 2 = SWIZZLE_128B (bits 61-63). The tile base must be 1024-byte aligned;
+// advancing the start address by 32 bytes steps 16 elements of 16-bit type along K inside the swizzle atom.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr)
+{
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3FFFF) >> 4);          // start address, bits 0-13
+    d |= static_cast<uint64_t>(1) << 16;                              // leading byte offset (unused here)
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;                      // stride byte offset, bits 32-45
+    d |= static_cast<uint64_t>(1) << 46;                              // descriptor version
+    d |= static_cast<uint64_t>(2) << 61;                              // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor of kind::f16 with an f32 accumulator, both operands K-major.
+// a/b format: 0 = f16, 1 = bf16. M in {64, 128}, N a multiple of 16 up to 256.
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_format, uint32_t M, uint32_t N)
+{
+    return (1u << 4)                 // D format f32
+           | (ab_format << 7)        // A format
+           | (ab_format << 10)       // B format
+           | ((N >> 3) << 17)        // N / 8
+           | ((M >> 4) << 24);       // M / 16
+}
+
+// Instruction descriptor of kind::f8f6f4, A and B e4m3 (format 0), f32 accumulator, K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3(uint32_t M, uint32_t N)
+{
+    return (1u << 4) | (0u << 7) | (0u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+}  // namespace mf

@@ -1,0 +1,383 @@
+// The bandwidth-bound kernels of the forward pass: the embedding fused with the first LayerNorm, LayerNorm,
+// attention per (board, head), the final LayerNorm of the CLS rows, and the search's reduction of the heads.
+// Row r of every activation is token r % 65 of board r / 65 (token 0 is CLS), as in
+// mayfly/chess/cudanet/cudanet_spec.h:68-80.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "gemm.cuh"
+
+namespace mf {
+
+constexpr int kTokens = 65;
+constexpr int kPieces = 13;
+constexpr int kHmBuckets = 102;
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+template <typename T> __device__ __forceinline__ void store4(T* p, float a, float b, float c, float d)
+{
+    uint2 q;
+    q.x = pack2<T>(a, b);
+    q.y = pack2<T>(c, d);
+    *reinterpret_cast<uint2*>(p) = q;
+}
+
+// LayerNorm of one row held by one warp (V float4 per lane, lane owns float4s lane, lane+32, ...): biased
+// variance from a second pass over (x - mean) in registers, rstd = rsqrt(var + eps), as F.layer_norm in fp32.
+template <typename T, int V>
+__device__ __forceinline__ void ln_row_store(const float4 (&v)[V], int d, const float* __restrict__ g,
+                                             const float* __restrict__ b, T* __restrict__ y, float eps)
+{
+    const int lane = threadIdx.x & 31;
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    const float mean = warp_sum(s) / static_cast<float>(d);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, e = v[i].w - mean;
+        q += (a * a + bb * bb) + (c * c + e * e);
+    }
+    const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(d) + eps);
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int c4 = lane + 32 * i;
+        const float4 gg = __ldg(g4 + c4), bb = __ldg(b4 + c4);
+        store4<T>(y + 4 * c4, (v[i].x - mean) * rstd * gg.x + bb.x, (v[i].y - mean) * rstd * gg.y + bb.y,
+                  (v[i].z - mean) * rstd * gg.z + bb.z, (v[i].w - mean) * rstd * gg.w + bb.w);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ embed + LN1
+// mayfly/chess/chess_net.py:182-192 (cudanet/kernels_trunk.cu:74-122 embed), then layer 0's norm1:
+//   x[b*65]     = cls + (cast_b + cast_w . cast[b]) + hm_emb[hm[b]]
+//   x[b*65+1+s] = piece[ids[b*64+s]] + pos[s] (+ ep_mark when ep[b] > 0 and s == ep[b] - 1)
+//   h = LN(x; g, beta)
+// One warp per row, rows = B * 65. ids and hm are clamped to their tables (a bad input cannot read out of
+// bounds), as the reference kernel does. d = 128 * V.
+template <typename T, int V>
+__global__ void __launch_bounds__(256) embed_ln_kernel(
+    const int64_t* __restrict__ ids, const float* __restrict__ cast, const int64_t* __restrict__ hm,
+    const int64_t* __restrict__ ep, const float* __restrict__ piece, const float* __restrict__ pos,
+    const float* __restrict__ cls, const float* __restrict__ cast_w, const float* __restrict__ cast_b,
+    const float* __restrict__ hm_emb, const float* __restrict__ ep_mark, const float* __restrict__ g,
+    const float* __restrict__ beta, float* __restrict__ x, T* __restrict__ h, int rows, float eps)
+{
+    constexpr int d = 128 * V;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;   // whole warp
+    const int lane = threadIdx.x & 31;
+    const int b = row / kTokens, t = row % kTokens;
+    float4 v[V];
+    if (t == 0) {
+        const float c0 = cast[4 * b + 0], c1 = cast[4 * b + 1], c2 = cast[4 * b + 2], c3 = cast[4 * b + 3];
+        long long hi = hm[b];
+        hi = hi < 0 ? 0 : (hi >= kHmBuckets ? kHmBuckets - 1 : hi);
+        const float4* cl4 = reinterpret_cast<const float4*>(cls);
+        const float4* cb4 = reinterpret_cast<const float4*>(cast_b);
+        const float4* he4 = reinterpret_cast<const float4*>(hm_emb + (size_t)hi * d);
+        const float4* cw4 = reinterpret_cast<const float4*>(cast_w);   // row c of cast_w [d, 4] is cw4[c]
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            const int c4 = lane + 32 * i;
+            const float4 w0 = __ldg(cw4 + 4 * c4 + 0), w1 = __ldg(cw4 + 4 * c4 + 1);
+            const float4 w2 = __ldg(cw4 + 4 * c4 + 2), w3 = __ldg(cw4 + 4 * c4 + 3);
+            const float4 bb = __ldg(cb4 + c4), cl = __ldg(cl4 + c4), he = __ldg(he4 + c4);
+            const float l0 = bb.x + (w0.x * c0 + w0.y * c1 + w0.z * c2 + w0.w * c3);
+            const float l1 = bb.y + (w1.x * c0 + w1.y * c1 + w1.z * c2 + w1.w * c3);
+            const float l2 = bb.z + (w2.x * c0 + w2.y * c1 + w2.z * c2 + w2.w * c3);
+            const float l3 = bb.w + (w3.x * c0 + w3.y * c1 + w3.z * c2 + w3.w * c3);
+            v[i] = make_float4(cl.x + l0 + he.x, cl.y + l1 + he.y, cl.z + l2 + he.z, cl.w + l3 + he.w);
+        }
+    } else {
+        const int s = t - 1;
+        long long p = ids[(size_t)b * 64 + s];
+        p = p < 0 ? 0 : (p >= kPieces ? kPieces - 1 : p);
+        const long long e = ep[b];
+        const bool mark = e > 0 && (long long)s == e - 1;
+        const float4* pc4 = reinterpret_cast<const float4*>(piece + (size_t)p * d);
+        const float4* ps4 = reinterpret_cast<const float4*>(pos + (size_t)s * d);
+        const float4* em4 = reinterpret_cast<const float4*>(ep_mark);
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            const int c4 = lane + 32 * i;
+            const float4 a = __ldg(pc4 + c4), q = __ldg(ps4 + c4);
+            float4 r = make_float4(a.x + q.x, a.y + q.y, a.z + q.z, a.w + q.w);
+            if (mark) {
+                const float4 m = __ldg(em4 + c4);
+                r = make_float4(r.x + m.x, r.y + m.y, r.z + m.z, r.w + m.w);
+            }
+            v[i] = r;
+        }
+    }
+    float4* xr = reinterpret_cast<float4*>(x + (size_t)row * d);
+#pragma unroll
+    for (int i = 0; i < V; ++i) xr[lane + 32 * i] = v[i];
+    ln_row_store<T, V>(v, d, g, beta, h + (size_t)row * d, eps);
+}
+
+// ------------------------------------------------------------------------------------------------ LayerNorm
+// h[r] = LN(x[r]) for rows r = row0 + i * row_stride, i < n (row_stride 65 picks the CLS rows for the final
+// norm, chess_net.py:194 / cudanet/kernels_heads.cu:64-86). Output rows are dense: h row i. One warp per row.
+template <typename T, int V>
+__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                                                        const float* __restrict__ b, T* __restrict__ h, int n,
+                                                        int row_stride, float eps)
+{
+    constexpr int d = 128 * V;
+    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (i >= n) return;
+    const int lane = threadIdx.x & 31;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)i * row_stride * d);
+    float4 v[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) v[k] = xr[lane + 32 * k];
+    ln_row_store<T, V>(v, d, g, b, h + (size_t)i * d, eps);
+}
+
+// ------------------------------------------------------------------------------------------------ attention
+// softmax(q k^T / sqrt(DH)) v over all 65 tokens of one board for one head (chess_net.py:159-161 SDPA, no
+// mask; cudanet/kernels_trunk.cu:385-509 attention_mma). qkv [rows, 3*d] holds q, k, v column blocks; head j
+// owns columns j*DH..j*DH+DH-1 of each. att [rows, d] gets the heads concatenated.
+//
+// One CTA per (head, board), 5 warps; warp w owns query rows 16w..16w+15 (tokens padded 65 -> 80 with zero
+// rows, padded keys masked to -inf). Q, K, V are staged in shared memory (row pitch DH+8 elements, so
+// ldmatrix rows fall in distinct banks); S = Q K^T and O = P V run on mma.sync m16n8k16 with f32 accumulation;
+// the softmax runs on the S fragments in registers (row max and sum across the 4 lanes of a quad by shuffles);
+// P is rounded to the 16-bit type for the second product and O is divided by the f32 row sum at the end.
+template <typename T> struct MmaName;
+template <> struct MmaName<__half> {
+    static __device__ __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+    {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+template <> struct MmaName<__nv_bfloat16> {
+    static __device__ __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+    {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+constexpr int kAttRows = 80;     // 65 tokens padded to 5 tiles of 16
+constexpr int kAttWarps = 5;
+
+template <typename T, int DH>
+__global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const T* __restrict__ qkv, T* __restrict__ att,
+                                                                   int d, float scale)
+{
+    constexpr int P = DH + 8;                 // smem row pitch in elements (16-byte multiple)
+    constexpr int CH = DH * 2 / 16;           // 16-byte chunks per row
+    constexpr int NT = kAttRows / 8;          // 10 key tiles of 8
+    constexpr int DT = DH / 8;                // output column tiles of 8
+    __shared__ __align__(16) T sQ[kAttRows * P];
+    __shared__ __align__(16) T sK[kAttRows * P];
+    __shared__ __align__(16) T sV[kAttRows * P];
+
+    const int head = blockIdx.x, b = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t row0 = (size_t)b * kTokens;
+    const size_t ld = 3 * (size_t)d;
+
+    // stage Q, K, V (rows 65..79 zero)
+    for (int i = tid; i < kAttRows * CH * 3; i += blockDim.x) {
+        const int which = i / (kAttRows * CH);
+        const int rem = i % (kAttRows * CH);
+        const int r = rem / CH, c = rem % CH;
+        T* dst = (which == 0 ? sQ : which == 1 ? sK : sV) + r * P + c * 8;
+        uint4 val = make_uint4(0, 0, 0, 0);
+        if (r < kTokens)
+            val = __ldg(reinterpret_cast<const uint4*>(qkv + (row0 + r) * ld + (size_t)which * d +
+                                                       (size_t)head * DH) + c);
+        *reinterpret_cast<uint4*>(dst) = val;
+    }
+    __syncthreads();
+
+    const int g = lane >> 2, t = lane & 3;
+    const int q0 = warp * 16;
+
+    // S = Q K^T for this warp's 16 rows and all 80 keys
+    float s[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int k0 = 0; k0 < DH; k0 += 16) {
+        uint32_t a[4];
+        ldsm_x4(smem_u32(sQ + (q0 + (lane & 15)) * P + k0 + (lane >> 4) * 8), a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int n = 0; n < NT; n += 2) {
+            // keys n*8 .. n*8+15: matrices (keys 0-7, k0), (keys 0-7, k0+8), (keys 8-15, k0), (keys 8-15, k0+8)
+            const int key = n * 8 + (lane & 7) + ((lane >> 4) << 3);
+            const int kk = k0 + ((lane >> 3) & 1) * 8;
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(smem_u32(sK + key * P + kk), b0, b1, b2, b3);
+            MmaName<T>::mma(s[n], a, b0, b1);
+            MmaName<T>::mma(s[n + 1], a, b2, b3);
+        }
+    }
+
+    // softmax over keys 0..64 of rows g and g+8 (each row spread over the quad's 4 lanes)
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int key = n * 8 + 2 * t + j;
+            const bool live = key < kTokens;
+            s[n][j] = live ? s[n][j] * scale : -INFINITY;
+            s[n][2 + j] = live ? s[n][2 + j] * scale : -INFINITY;
+            mx0 = fmaxf(mx0, s[n][j]);
+            mx1 = fmaxf(mx1, s[n][2 + j]);
+        }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            s[n][j] = expf(s[n][j] - mx0);
+            s[n][2 + j] = expf(s[n][2 + j] - mx1);
+            sum0 += s[n][j];
+            sum1 += s[n][2 + j];
+        }
+    }
+    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+
+    // O = P V: P's fragments are S's accumulators (keys 16kk..16kk+15 = key tiles 2kk, 2kk+1)
+    float o[DT][4];
+#pragma unroll
+    for (int n = 0; n < DT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < kAttRows / 16; ++kk) {
+        uint32_t a[4];
+        a[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
+        a[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
+        a[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        a[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+        for (int n = 0; n < DT; n += 2) {
+            // V rows (keys) 16kk.., transposed: matrices (keys 0-7, cols n*8), (keys 8-15, cols n*8),
+            // (keys 0-7, cols n*8+8), (keys 8-15, cols n*8+8)
+            const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            const int col = n * 8 + (lane >> 4) * 8;
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(smem_u32(sV + key * P + col), b0, b1, b2, b3);
+            MmaName<T>::mma(o[n], a, b0, b1);
+            MmaName<T>::mma(o[n + 1], a, b2, b3);
+        }
+    }
+
+    // normalise, stage this warp's rows in sQ (its own rows only: no other warp reads them any more), store
+    const float inv0 = 1.f / sum0, inv1 = 1.f / sum1;
+    __syncwarp();
+#pragma unroll
+    for (int n = 0; n < DT; ++n) {
+        *reinterpret_cast<uint32_t*>(sQ + (q0 + g) * P + n * 8 + 2 * t) = pack2<T>(o[n][0] * inv0, o[n][1] * inv0);
+        *reinterpret_cast<uint32_t*>(sQ + (q0 + g + 8) * P + n * 8 + 2 * t) =
+            pack2<T>(o[n][2] * inv1, o[n][3] * inv1);
+    }
+    __syncwarp();
+    for (int i = lane; i < 16 * CH; i += 32) {
+        const int r = q0 + i / CH, c = i % CH;
+        if (r < kTokens)
+            *(reinterpret_cast<uint4*>(att + (row0 + r) * d + (size_t)head * DH) + c) =
+                *reinterpret_cast<const uint4*>(sQ + r * P + c * 8);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ heads_post
+// The search's reduction of the two heads at each row's legal moves (mcts.py:1152-1164 _collect,
+// cpp/export_ts.py:147-156 post, cudanet/kernels_heads.cu:88-143 heads_post):
+//   p_k = policy[I_k], q_k = sigmoid(qvalue[I_k]); w = softmax(p over legal k)
+//   val = 2 * sum_k w_k q_k - 1;  pol_k = p_k, qv_k = 2 q_k - 1 on legal slots, 0 on padding
+// A row with no legal slot gets val = -1. logits [B, 2*moves] f32 (policy, then qvalue). One warp per board.
+// Policy indices outside 0..moves-1 are clamped (a bad input cannot read out of bounds).
+__global__ void __launch_bounds__(256) heads_post_kernel(const float* __restrict__ logits,
+                                                         const int64_t* __restrict__ I,
+                                                         const uint8_t* __restrict__ Mk, int B, int wide,
+                                                         int moves, float* __restrict__ pol,
+                                                         float* __restrict__ val, float* __restrict__ qv)
+{
+    const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (b >= B) return;
+    const int lane = threadIdx.x & 31;
+    const float* lp = logits + (size_t)b * 2 * moves;
+    const float* lq = lp + moves;
+    const size_t base = (size_t)b * wide;
+    float mx = -INFINITY;
+    for (int k = lane; k < wide; k += 32) {
+        if (Mk[base + k]) {
+            long long j = I[base + k];
+            j = j < 0 ? 0 : (j >= moves ? moves - 1 : j);
+            const float p = lp[j];
+            pol[base + k] = p;
+            qv[base + k] = (1.0f / (1.0f + expf(-lq[j]))) * 2.0f - 1.0f;
+            mx = fmaxf(mx, p);
+        } else {
+            pol[base + k] = 0.0f;
+            qv[base + k] = 0.0f;
+        }
+    }
+    mx = warp_max(mx);
+    float s = 0.f, acc = 0.f;
+    for (int k = lane; k < wide; k += 32) {
+        if (Mk[base + k]) {
+            long long j = I[base + k];
+            j = j < 0 ? 0 : (j >= moves ? moves - 1 : j);
+            const float e = expf(lp[j] - mx);
+            s += e;
+            acc += e * (1.0f / (1.0f + expf(-lq[j])));
+        }
+    }
+    s = warp_sum(s);
+    acc = warp_sum(acc);
+    if (lane == 0) val[b] = s > 0.f ? (acc / s) * 2.0f - 1.0f : -1.0f;
+}
+
+}  // namespace mf

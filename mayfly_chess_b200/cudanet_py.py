@@ -1,0 +1,320 @@
+"""libcudanet_b200.so from Python through ctypes: the reference backend's Python interface, unchanged.
+
+    net = CudaNet("net.cnw")
+    pol, val, qv = net.evaluate(ids, cast, hm, ep, I, M)
+
+This mirrors mayfly/chess/cudanet/cudanet_py.py:87-178 (class CudaNet): the same constructor
+(weights_path, device=0, dll=None), the same evaluate(ids, cast, hm, ep, I, M) -> (pol, val, qv) with the same
+shape and dtype checks (bool M is taken too), fingerprint(), profile(B, reps), close() and the context
+manager, the same exceptions (ValueError for bad shapes or batch sizes, RuntimeError with the library's reason
+for a failed call). The inputs are what MCTS._prepare builds: ids (B, 64) int64, cast (B, 4) float32, hm (B,)
+int64, ep (B,) int64, I (B, wide) int64 and M (B, wide) uint8. The outputs are float32 pol (B, wide) (raw policy
+logits at each row's legal moves, 0 on padding), val (B,) and qv (B, wide).
+
+Additions: evaluate_logits (also the full (B, 8324) logits), begin/end (two batches in flight),
+evaluate_device (torch CUDA tensors in and out, queued on a stream), precision, check, and k_* single-kernel
+entry points for unit tests.
+
+The library is MAYFLY_CUDANET_DLL, else libcudanet_b200.so beside this file. There is no fallback: if the
+library is missing the constructor raises.
+"""
+import ctypes
+import os
+import threading
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+MAX_BATCH = 1024        # the library's default (env MAYFLY_CUDANET_MAX_BATCH when a net is made)
+MAX_WIDE = 256
+N_MOVES = 4162
+ERR_LEN = 2048
+
+_libs = {}
+_load_lock = threading.Lock()
+
+
+def dll_path(dll=None):
+    return dll or os.environ.get("MAYFLY_CUDANET_DLL") or os.path.join(HERE, "libcudanet_b200.so")
+
+
+def load(dll=None):
+    """The library, loaded once per path, with every entry point's signature declared."""
+    path = os.path.abspath(dll_path(dll))
+    with _load_lock:
+        if path in _libs:
+            return _libs[path]
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"no libcudanet_b200.so at {path} (build it: python -m mayfly_chess_b200.build)")
+        lib = ctypes.CDLL(path)
+        vp, i32, cp = ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p
+        lib.cudanet_create.argtypes = [cp, i32, cp, i32]
+        lib.cudanet_create.restype = vp
+        lib.cudanet_evaluate.argtypes = [vp, i32, i32] + [vp] * 9 + [cp, i32]
+        lib.cudanet_evaluate.restype = i32
+        lib.cudanet_evaluate_logits.argtypes = [vp, i32, i32] + [vp] * 10 + [cp, i32]
+        lib.cudanet_evaluate_logits.restype = i32
+        lib.cudanet_begin.argtypes = [vp, i32, i32] + [vp] * 6 + [cp, i32]
+        lib.cudanet_begin.restype = i32
+        lib.cudanet_end.argtypes = [vp, vp, vp, vp, cp, i32]
+        lib.cudanet_end.restype = i32
+        lib.cudanet_fingerprint.argtypes = [vp, cp, i32]
+        lib.cudanet_fingerprint.restype = i32
+        lib.cudanet_precision.argtypes = [vp, cp, i32]
+        lib.cudanet_precision.restype = i32
+        lib.cudanet_max_batch.argtypes = [vp]
+        lib.cudanet_max_batch.restype = i32
+        lib.cudanet_profile.argtypes = [vp, i32, i32, ctypes.POINTER(ctypes.c_double), i32, cp, i32]
+        lib.cudanet_profile.restype = i32
+        lib.cudanet_profile_names.argtypes = [cp, i32]
+        lib.cudanet_profile_names.restype = i32
+        lib.cudanet_destroy.argtypes = [vp]
+        lib.cudanet_destroy.restype = None
+        lib.cudanet_evaluate_device.argtypes = [vp, i32, i32] + [vp] * 10 + [cp, i32]
+        lib.cudanet_evaluate_device.restype = i32
+        lib.cudanet_check.argtypes = [vp, vp, cp, i32]
+        lib.cudanet_check.restype = i32
+        lib.cudanet_k_gemm.argtypes = [i32, i32, i32, vp, vp, vp, vp, i32, i32, i32, i32, vp, cp, i32]
+        lib.cudanet_k_gemm.restype = i32
+        lib.cudanet_k_attention.argtypes = [i32, vp, vp, i32, i32, i32, vp, cp, i32]
+        lib.cudanet_k_attention.restype = i32
+        lib.cudanet_k_layernorm.argtypes = [i32, vp, vp, vp, vp, i32, i32, i32, vp, cp, i32]
+        lib.cudanet_k_layernorm.restype = i32
+        _libs[path] = lib
+        return lib
+
+
+def _arr(a, dtype, shape, name):
+    """A C-contiguous array of exactly this dtype and shape (copied only when it has to be)."""
+    a = np.asarray(a)
+    if dtype is np.uint8 and a.dtype == np.bool_:
+        a = a.view(np.uint8)
+    a = np.ascontiguousarray(a, dtype=dtype)
+    if a.shape != shape:
+        raise ValueError(f"{name}: shape {a.shape}, expected {shape}")
+    return a
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _msg(err):
+    return err.value.decode("utf-8", "replace")
+
+
+class CudaNet:
+    """One evaluator handle: the weights on one B200, a CUDA graph per batch size. One call at a time."""
+
+    def __init__(self, weights_path, device=0, dll=None):
+        self.path = os.path.abspath(weights_path)
+        self.device = int(device)
+        self.dll = dll_path(dll)
+        self._lib = load(self.dll)
+        self._lock = threading.Lock()
+        self._h = None
+        err = ctypes.create_string_buffer(ERR_LEN)
+        h = self._lib.cudanet_create(self.path.encode("utf-8"), self.device, err, ERR_LEN)
+        if not h:
+            raise RuntimeError(f"cudanet_create({self.path}): {_msg(err)}")
+        self._h = ctypes.c_void_p(h)
+        self.max_batch = int(self._lib.cudanet_max_batch(self._h))
+
+    def _inputs(self, ids, cast, hm, ep, I, M):
+        if self._h is None:
+            raise RuntimeError("CudaNet is closed")
+        I = np.asarray(I)
+        if I.ndim != 2:
+            raise ValueError(f"I: shape {I.shape}, expected (B, wide)")
+        B, wide = I.shape
+        if not 1 <= B <= self.max_batch:
+            raise ValueError(f"batch {B}: cudanet takes 1 to {self.max_batch} (env MAYFLY_CUDANET_MAX_BATCH)")
+        if wide < 1:
+            raise ValueError("wide must be at least 1")
+        return (B, wide, _arr(ids, np.int64, (B, 64), "ids"), _arr(cast, np.float32, (B, 4), "cast"),
+                _arr(hm, np.int64, (B,), "hm"), _arr(ep, np.int64, (B,), "ep"), _arr(I, np.int64, (B, wide), "I"),
+                _arr(M, np.uint8, (B, wide), "M"))
+
+    def evaluate(self, ids, cast, hm, ep, I, M):
+        """One batch. Returns (pol (B, wide), val (B,), qv (B, wide)) float32."""
+        B, wide, ids, cast, hm, ep, I, M = self._inputs(ids, cast, hm, ep, I, M)
+        pol = np.zeros((B, wide), np.float32)
+        val = np.zeros(B, np.float32)
+        qv = np.zeros((B, wide), np.float32)
+        err = ctypes.create_string_buffer(ERR_LEN)
+        with self._lock:
+            rc = self._lib.cudanet_evaluate(self._h, B, wide, _p(ids), _p(cast), _p(hm), _p(ep), _p(I), _p(M),
+                                            _p(pol), _p(val), _p(qv), err, ERR_LEN)
+        if rc != 0:
+            raise RuntimeError(f"cudanet_evaluate: {_msg(err)}")
+        return pol, val, qv
+
+    def evaluate_logits(self, ids, cast, hm, ep, I, M):
+        """evaluate, plus the full logits (B, 2 * 4162) float32: policy, then qvalue."""
+        B, wide, ids, cast, hm, ep, I, M = self._inputs(ids, cast, hm, ep, I, M)
+        pol = np.zeros((B, wide), np.float32)
+        val = np.zeros(B, np.float32)
+        qv = np.zeros((B, wide), np.float32)
+        logits = np.zeros((B, 2 * N_MOVES), np.float32)
+        err = ctypes.create_string_buffer(ERR_LEN)
+        with self._lock:
+            rc = self._lib.cudanet_evaluate_logits(self._h, B, wide, _p(ids), _p(cast), _p(hm), _p(ep), _p(I),
+                                                   _p(M), _p(pol), _p(val), _p(qv), _p(logits), err, ERR_LEN)
+        if rc != 0:
+            raise RuntimeError(f"cudanet_evaluate_logits: {_msg(err)}")
+        return pol, val, qv, logits
+
+    def begin(self, ids, cast, hm, ep, I, M):
+        """Queue one batch (at most two in flight); end() returns the oldest one's outputs."""
+        B, wide, ids, cast, hm, ep, I, M = self._inputs(ids, cast, hm, ep, I, M)
+        err = ctypes.create_string_buffer(ERR_LEN)
+        with self._lock:
+            rc = self._lib.cudanet_begin(self._h, B, wide, _p(ids), _p(cast), _p(hm), _p(ep), _p(I), _p(M), err,
+                                         ERR_LEN)
+            if rc == 0:
+                self._fly = getattr(self, "_fly", []) + [(B, wide)]
+        if rc != 0:
+            raise RuntimeError(f"cudanet_begin: {_msg(err)}")
+
+    def end(self):
+        fly = getattr(self, "_fly", [])
+        if not fly:
+            raise RuntimeError("cudanet_end: no batch in flight")
+        B, wide = fly[0]
+        pol = np.zeros((B, wide), np.float32)
+        val = np.zeros(B, np.float32)
+        qv = np.zeros((B, wide), np.float32)
+        err = ctypes.create_string_buffer(ERR_LEN)
+        with self._lock:
+            self._fly = fly[1:]
+            rc = self._lib.cudanet_end(self._h, _p(pol), _p(val), _p(qv), err, ERR_LEN)
+        if rc != 0:
+            raise RuntimeError(f"cudanet_end: {_msg(err)}")
+        return pol, val, qv
+
+    def evaluate_device(self, ids, cast, hm, ep, I, M, pol, val, qv, stream=None):
+        """One batch on torch CUDA tensors of the handle's device (outputs preallocated float32), queued on
+        `stream` (a torch.cuda.Stream, default the current stream) without waiting."""
+        import torch
+        if self._h is None:
+            raise RuntimeError("CudaNet is closed")
+        B, wide = I.shape
+        for name, t, dt in (("ids", ids, torch.int64), ("cast", cast, torch.float32), ("hm", hm, torch.int64),
+                            ("ep", ep, torch.int64), ("I", I, torch.int64), ("M", M, torch.uint8),
+                            ("pol", pol, torch.float32), ("val", val, torch.float32), ("qv", qv, torch.float32)):
+            if not t.is_cuda or t.dtype != dt or not t.is_contiguous():
+                raise ValueError(f"{name}: needs a contiguous CUDA {dt} tensor")
+        s = stream if stream is not None else torch.cuda.current_stream()
+        err = ctypes.create_string_buffer(ERR_LEN)
+        with self._lock:
+            rc = self._lib.cudanet_evaluate_device(self._h, B, wide, ids.data_ptr(), cast.data_ptr(),
+                                                   hm.data_ptr(), ep.data_ptr(), I.data_ptr(), M.data_ptr(),
+                                                   pol.data_ptr(), val.data_ptr(), qv.data_ptr(),
+                                                   ctypes.c_void_p(s.cuda_stream), err, ERR_LEN)
+        if rc != 0:
+            raise RuntimeError(f"cudanet_evaluate_device: {_msg(err)}")
+
+    def check(self, stream=None):
+        """Wait for the handle's work (and `stream`) and raise if a device-side wait failed."""
+        err = ctypes.create_string_buffer(ERR_LEN)
+        sp = ctypes.c_void_p(stream.cuda_stream) if stream is not None else None
+        with self._lock:
+            rc = self._lib.cudanet_check(self._h, sp, err, ERR_LEN)
+        if rc != 0:
+            raise RuntimeError(f"cudanet_check: {_msg(err)}")
+
+    def fingerprint(self):
+        """The weight file's fingerprint, as mcts_cpp.fingerprint computes it for the checkpoint."""
+        if self._h is None:
+            raise RuntimeError("CudaNet is closed")
+        buf = ctypes.create_string_buffer(256)
+        if self._lib.cudanet_fingerprint(self._h, buf, len(buf)) < 0:
+            raise RuntimeError("cudanet_fingerprint failed")
+        return buf.value.decode("utf-8", "replace")
+
+    def precision(self):
+        buf = ctypes.create_string_buffer(32)
+        if self._lib.cudanet_precision(self._h, buf, len(buf)) < 0:
+            raise RuntimeError("cudanet_precision failed")
+        return buf.value.decode()
+
+    def profile(self, B, reps=20):
+        """Milliseconds a pass by step at batch B (an empty board, eager, an event after each step), the mean of
+        reps passes, and last graph_pass, the whole pass as a CUDA graph. A dict in pass order."""
+        if self._h is None:
+            raise RuntimeError("CudaNet is closed")
+        buf = ctypes.create_string_buffer(512)
+        self._lib.cudanet_profile_names(buf, len(buf))
+        names = buf.value.decode("utf-8").split(",")
+        ms = (ctypes.c_double * len(names))()
+        err = ctypes.create_string_buffer(ERR_LEN)
+        with self._lock:
+            k = self._lib.cudanet_profile(self._h, int(B), int(reps), ms, len(names), err, ERR_LEN)
+        if k < 0:
+            raise RuntimeError(f"cudanet_profile: {_msg(err)}")
+        return dict(zip(names[:k], list(ms)[:k]))
+
+    def close(self):
+        if getattr(self, "_h", None) is not None:
+            self._lib.cudanet_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------------------------------------ kernels
+def _dtype_code(t):
+    import torch
+    if t.dtype == torch.float16:
+        return 0
+    if t.dtype == torch.bfloat16:
+        return 1
+    raise ValueError(f"16-bit float tensors only, got {t.dtype}")
+
+
+def _stream():
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def k_gemm(A, W, bias, C, epi, bn=0, dll=None):
+    """C = A W^T + epilogue on the tensor cores (epi 0 bias, 1 bias+GELU, 2 C += (f32), 3 f32 out)."""
+    lib = load(dll)
+    M, K = A.shape
+    N = W.shape[0]
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_k_gemm(_dtype_code(A), int(epi), int(bn), A.data_ptr(), W.data_ptr(), bias.data_ptr(),
+                            C.data_ptr(), M, N, K, C.stride(0), _stream(), err, ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_k_gemm: {_msg(err)}")
+    return C
+
+
+def k_attention(qkv, att, B, d, heads, dll=None):
+    lib = load(dll)
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_k_attention(_dtype_code(qkv), qkv.data_ptr(), att.data_ptr(), B, d, heads, _stream(), err,
+                                 ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_k_attention: {_msg(err)}")
+    return att
+
+
+def k_layernorm(x, g, b, h, n, d, row_stride=1, dll=None):
+    lib = load(dll)
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_k_layernorm(_dtype_code(h), x.data_ptr(), g.data_ptr(), b.data_ptr(), h.data_ptr(), n, d,
+                                 row_stride, _stream(), err, ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_k_layernorm: {_msg(err)}")
+    return h

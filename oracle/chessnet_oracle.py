@@ -1,0 +1,90 @@
+"""TEST INFRASTRUCTURE ONLY: the CPU fp32 oracle of MayFly's batched network evaluation.
+
+A plain-torch restatement, on the CPU in float32, of the forward the search calls per leaf batch and of the
+search's reduction of the two heads. Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use
+it, as the checker; the product never imports it. It is pinned against the reference's own ChessNet (imported
+from the reference checkout) through the committed fixtures under tests/golden/ (make_golden.py).
+
+  forward(state, arch, ids, cast, hm, ep) -> (policy [B, 4162], qvalue [B, 4162])
+      mayfly/chess/chess_net.py:176-204 ChessNet.forward, with the encoder layer written out as
+      chess_net.py:148-165 _encode_sdpa writes it (pre-norm nn.TransformerEncoderLayer, exact erf GELU, LN eps
+      1e-5, no final encoder norm), then the final LayerNorm on the CLS row (chess_net.py:194) and the policy
+      and qvalue heads (chess_net.py:199-204). cpp/export_ts.py:241-248 Export returns the same pair.
+  post(policy, qvalue, I, M) -> (pol [B, wide], val [B], qv [B, wide])
+      cpp/export_ts.py:325-334 post (= mcts.py:1152-1164 _collect) with the evaluator's padding convention
+      (cudanet/kernels_heads.cu:88-143): pol and qv are 0 on padding, a row with no legal move gets val = -1.
+"""
+import math
+
+import torch
+import torch.nn.functional as F
+
+LN_EPS = 1e-5
+
+
+def embed(state, arch, ids, cast, hm, ep):
+    """chess_net.py:182-192: piece + square embeddings, the en passant mark, and the CLS token."""
+    d = arch.d
+    B = ids.shape[0]
+    x = state["piece.weight"][ids] + state["pos.weight"][None]                 # (B, 64, d)
+    has = (ep > 0).to(x.dtype)[:, None]
+    rows = torch.arange(B)
+    sq = (ep - 1).clamp(min=0)
+    x[rows, sq] = x[rows, sq] + state["ep_mark"] * has
+    cls = (state["cls"].reshape(1, 1, d) + F.linear(cast, state["cast.weight"], state["cast.bias"])[:, None, :]
+           + state["hm.weight"][hm][:, None, :])
+    return torch.cat([cls, x], dim=1)                                            # (B, 65, d)
+
+
+def layer(state, arch, i, x):
+    """One pre-norm encoder layer (chess_net.py:154-164)."""
+    B, L, d = x.shape
+    H, dh = arch.heads, arch.dh
+    p = f"enc.layers.{i}."
+    h = F.layer_norm(x, (d,), state[p + "norm1.weight"], state[p + "norm1.bias"], LN_EPS)
+    qkv = F.linear(h, state[p + "self_attn.in_proj_weight"], state[p + "self_attn.in_proj_bias"])
+    q, k, v = qkv.view(B, L, 3, H, dh).permute(2, 0, 3, 1, 4).unbind(0)         # each (B, H, L, dh)
+    s = torch.matmul(q, k.transpose(-1, -2)) * (1.0 / math.sqrt(dh))
+    o = torch.matmul(torch.softmax(s, dim=-1), v).transpose(1, 2).reshape(B, L, d)
+    x = x + F.linear(o, state[p + "self_attn.out_proj.weight"], state[p + "self_attn.out_proj.bias"])
+    h = F.layer_norm(x, (d,), state[p + "norm2.weight"], state[p + "norm2.bias"], LN_EPS)
+    f = F.gelu(F.linear(h, state[p + "linear1.weight"], state[p + "linear1.bias"]))
+    return x + F.linear(f, state[p + "linear2.weight"], state[p + "linear2.bias"])
+
+
+@torch.no_grad()
+def forward(state, arch, ids, cast, hm, ep):
+    ids = torch.as_tensor(ids, dtype=torch.long)
+    cast = torch.as_tensor(cast, dtype=torch.float32)
+    hm = torch.as_tensor(hm, dtype=torch.long)
+    ep = torch.as_tensor(ep, dtype=torch.long)
+    x = embed(state, arch, ids, cast, hm, ep)
+    for i in range(arch.layers):
+        x = layer(state, arch, i, x)
+    hc = F.layer_norm(x[:, 0], (arch.d,), state["ln.weight"], state["ln.bias"], LN_EPS)
+    return (F.linear(hc, state["policy.weight"], state["policy.bias"]),
+            F.linear(hc, state["qvalue.weight"], state["qvalue.bias"]))
+
+
+@torch.no_grad()
+def post(policy, qvalue, I, M):
+    """_collect's arithmetic at the legal moves (module docstring)."""
+    It = torch.as_tensor(I, dtype=torch.long)
+    Mt = torch.as_tensor(M).to(torch.bool)
+    q = torch.sigmoid(qvalue.float())
+    lg = torch.gather(policy.float(), 1, It)
+    w = torch.softmax(lg.masked_fill(~Mt, float("-inf")), -1)
+    qg = torch.gather(q, 1, It)
+    val = (w * qg).sum(1) * 2.0 - 1.0
+    val = torch.where(Mt.any(1), val, torch.full_like(val, -1.0))
+    pol = lg.masked_fill(~Mt, 0.0)
+    qv = (qg * 2.0 - 1.0).masked_fill(~Mt, 0.0)
+    return pol.numpy(), val.numpy(), qv.numpy()
+
+
+def evaluate(state, arch, b):
+    """The oracle's answer for one batch dict (ids, cast, hm, ep, I, M): (pol, val, qv) as the evaluator
+    returns them, plus the full (policy, qvalue) logits."""
+    policy, qvalue = forward(state, arch, b["ids"], b["cast"], b["hm"], b["ep"])
+    pol, val, qv = post(policy, qvalue, b["I"], b["M"])
+    return pol, val, qv, policy.numpy(), qvalue.numpy()

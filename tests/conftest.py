@@ -1,0 +1,46 @@
+"""Shared fixtures. GPU tests are marked `gpu` and need a B200; everything else runs on the CPU."""
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(REPO, "tests", "golden")
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
+
+
+@pytest.fixture(scope="session")
+def meta():
+    with open(os.path.join(GOLDEN, "meta.json")) as f:
+        return json.load(f)
+
+
+def golden_case(name):
+    """(batch dict, reference outputs dict) of a committed fixture."""
+    from mayfly_chess_b200.inputs import PositionSet
+    path = os.path.join(GOLDEN, name + ".npz")
+    ps = PositionSet(path)
+    z = np.load(path)
+    ref = {k: z[k] for k in ("pol", "val", "qv", "policy_rows", "qvalue_rows")}
+    return ps.batch(0, len(ps)), ref
+
+
+@pytest.fixture(scope="session")
+def chesscore():
+    """The reference's chess core (oracle/_ref), built by oracle/Makefile from the reference checkout when it is
+    missing (where there is no checkout the build fails and the tests that need it are skipped)."""
+    lib = os.path.join(REPO, "oracle", "_ref", "libchesscore.so")
+    if not os.path.exists(lib):
+        subprocess.run(["make", "-C", os.path.join(REPO, "oracle")], capture_output=True)
+    if not os.path.exists(lib):
+        pytest.skip("oracle/_ref/libchesscore.so not built and no reference checkout to build it from")
+    from oracle import positions
+    return positions

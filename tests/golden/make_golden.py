@@ -1,0 +1,197 @@
+"""Generates the committed golden fixtures from the REFERENCE itself, in a container that has the reference
+checkout (it is not needed, and not present, where the tests and the bench run).
+
+    python tests/golden/make_golden.py [--ref /root/reference]
+
+What it does:
+  1. Builds the reference's own C++ chess core (make -C oracle) and uses it, through oracle/positions.py, for
+     every position: seeded random playouts (numpy PCG64; seed 0 with 0..80 plies for the CPU correctness
+     config, seed 1 with 0..120 plies for the 146M configs) and the reference's fixed edge-case positions, read
+     as text from mayfly/chess/cudanet/test_cudanet.py (FIXED, :68-103) and mayfly/chess/cpp/positions.json.
+     python-chess is not installed, so the SAN lines of test_cudanet.py (:106-118) are not used.
+  2. Imports the reference's ChessNet (mayfly/chess/chess_net.py) and export_ts (Export, post) with a stub
+     `chess` module of constants (the forward never calls python-chess), loads the seeded random-init state
+     (mayfly_chess_b200.weights.random_state) with load_state_dict(strict=True), which pins the state dict's
+     names and shapes, and runs the reference in float32 on the CPU with the MHA fast path off, as
+     cudanet/test_cudanet.py:177-194 reference() does.
+  3. Writes, per case, the inputs and the reference outputs at the legal moves (pol with 0 on padding, val, qv
+     with 0 on padding) plus the full logits of a few rows, and the 8,192-position seed-1 set the bench uses.
+
+Fixtures (all small .npz):
+  positions_seed1.npz         8,192 seed-1 positions, compact (mayfly_chess_b200/inputs.py PositionSet)
+  small_seed0_b256.npz        config 1: d 256, 4 layers, 8 heads, FFN 1024, seed-0 weights, 256 seed-0 positions
+  small_seed0_fixed.npz       the same net on the reference's fixed edge-case positions
+  full_seed1_b64.npz          the 146M net (d 1024, 16 layers, 16 heads, FFN 2048), seed-1 weights, the first 64
+                              seed-1 positions
+  full_seed1_fixed.npz        the 146M net on the fixed edge-case positions
+  meta.json                   fingerprints, state dict names and shapes, how each case was made
+"""
+import argparse
+import ast
+import json
+import os
+import subprocess
+import sys
+import time
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+from mayfly_chess_b200 import weights as W   # noqa: E402
+from mayfly_chess_b200.inputs import pack    # noqa: E402
+
+
+def chess_stub():
+    """The constants chess_net.py, moves.py and encode.py read at import (python-chess values)."""
+    m = types.ModuleType("chess")
+    m.PAWN, m.KNIGHT, m.BISHOP, m.ROOK, m.QUEEN, m.KING = 1, 2, 3, 4, 5, 6
+    m.WHITE, m.BLACK = True, False
+    m.square_mirror = lambda sq: sq ^ 0x38
+    m.square_rank = lambda sq: sq >> 3
+    m.STARTING_FEN = "rnbqkbnr/pppppppp/8/8/8/8/PPPPPPPP/RNBQKBNR w KQkq - 0 1"
+    return m
+
+
+def import_reference(ref):
+    chess_dir = os.path.join(ref, "mayfly", "chess")
+    sys.modules.setdefault("chess", chess_stub())
+    for d in (chess_dir, os.path.join(chess_dir, "cpp")):
+        if d not in sys.path:
+            sys.path.insert(0, d)
+    import chess_net   # noqa: E402
+    import export_ts   # noqa: E402
+    return chess_net, export_ts
+
+
+def fixed_fens(ref):
+    """FIXED from test_cudanet.py (parsed, not executed) and every FEN of cpp/positions.json with its history."""
+    from oracle import positions as P
+    src = open(os.path.join(ref, "mayfly", "chess", "cudanet", "test_cudanet.py"), encoding="utf-8").read()
+    fens = []
+    for node in ast.walk(ast.parse(src)):
+        if isinstance(node, ast.Assign) and any(getattr(t, "id", None) == "FIXED" for t in node.targets):
+            for e in node.value.elts:
+                fens.append(P.START_FEN if isinstance(e, ast.Attribute) else e.value)
+    out = []
+    for f in fens:
+        p = P.Position(f)
+        if p.legal()[0]:
+            out.append(("test_cudanet.FIXED", f, p))
+    for e in json.load(open(os.path.join(ref, "mayfly", "chess", "cpp", "positions.json"))):
+        p = P.Position(e["fen"])
+        for u in e["hist"]:
+            codes, _ = p.legal()
+            match = [c for c in codes if uci(c) == u]
+            if len(match) != 1:
+                raise RuntimeError(f"{e['name']}: history move {u} not legal")
+            p.push(match[0])
+        if p.legal()[0]:
+            out.append(("positions.json:" + e["name"], e["fen"], p))
+    return out
+
+
+def uci(code):
+    f, t, promo = (code >> 6) & 63, code & 63, code >> 12
+    s = "abcdefgh"[f & 7] + "12345678"[f >> 3] + "abcdefgh"[t & 7] + "12345678"[t >> 3]
+    return s + (" pnbrqk"[promo] if promo else "")
+
+
+def reference_outputs(chess_net, export_ts, arch, state, batch):
+    """ChessNet float32 on the CPU through export_ts.Export and export_ts.post (test_cudanet.py:177-194), with
+    pol cut to the legal moves (test_cudanet.py:167-173 cut) and qv set to 0 on padding."""
+    m = chess_net.ChessNet(d=arch.d, nhead=arch.heads, layers=arch.layers, dim_ff=arch.ff, qhead=True)
+    m.load_state_dict({**state, "posidx": torch.arange(64)}, strict=True)
+    m = m.float().eval()
+    mha = torch.backends.mha
+    fast = mha.get_fastpath_enabled()
+    mha.set_fastpath_enabled(False)
+    try:
+        with torch.no_grad():
+            exp = export_ts.Export(m).eval()
+            pol, qval = exp(*export_ts.inputs(batch, "cpu"))
+            r = export_ts.post(pol, qval, batch, "cpu")
+    finally:
+        mha.set_fastpath_enabled(fast)
+    B, wide = batch["I"].shape
+    P = np.zeros((B, wide), np.float32)
+    Q = np.array(r["qv"], np.float32)
+    for i, k in enumerate(batch["widths"]):
+        P[i, :k] = r["policy"][i, batch["I"][i, :k]]
+        Q[i, k:] = 0.0
+    return P, r["val"].astype(np.float32), Q, pol.numpy(), qval.numpy()
+
+
+def check_state_spec(chess_net, arch):
+    m = chess_net.ChessNet(d=arch.d, nhead=arch.heads, layers=arch.layers, dim_ff=arch.ff, qhead=True)
+    ref = [(k, tuple(v.shape)) for k, v in m.state_dict().items() if v.is_floating_point()]
+    mine = [(k, tuple(s)) for k, s in W.state_spec(arch)]
+    if ref != mine:
+        raise SystemExit(f"state_spec differs from ChessNet's state dict for {arch}")
+    return [k for k, _ in ref]
+
+
+def save_case(name, arch, seed, batch, outs, note, meta, full_rows=4):
+    P, V, Q, pol_full, q_full = outs
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), **pack(batch), pol=P, val=V, qv=Q,
+                        policy_rows=pol_full[:full_rows].astype(np.float32),
+                        qvalue_rows=q_full[:full_rows].astype(np.float32))
+    meta["cases"][name] = {"arch": [arch.d, arch.layers, arch.heads, arch.ff], "seed": seed,
+                           "B": int(batch["ids"].shape[0]), "wide": int(batch["I"].shape[1]), "note": note}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    subprocess.run(["make", "-C", os.path.join(REPO, "oracle"), f"REF={args.ref}"], check=True)
+    from oracle import positions as P
+
+    chess_net, export_ts = import_reference(args.ref)
+    meta = {"generator": "tests/golden/make_golden.py", "torch": torch.__version__, "cases": {}}
+    for tag, arch in (("small", W.SMALL), ("full", W.FULL)):
+        meta[f"state_keys_{tag}"] = check_state_spec(chess_net, arch)
+
+    fixed = fixed_fens(args.ref)
+    fixed_batch = P.encode_batch([p for _, _, p in fixed])
+    meta["fixed_sources"] = [s for s, _, _ in fixed]
+    print(f"{len(fixed)} fixed positions, widths {fixed_batch['widths'].min()}..{fixed_batch['widths'].max()}")
+
+    # the bench's position set: 8,192 seed-1 playouts of 0..120 plies
+    t = time.time()
+    seed1_pos = P.random_playouts(8192, seed=1, max_plies=120)
+    seed1 = P.encode_batch(seed1_pos)
+    np.savez_compressed(os.path.join(HERE, "positions_seed1.npz"), **pack(seed1))
+    print(f"positions_seed1: 8192 positions in {time.time() - t:.1f} s, widths "
+          f"{seed1['widths'].min()}..{seed1['widths'].max()}")
+
+    # config 1: the small net, seed 0
+    small0 = P.encode_batch(P.random_playouts(256, seed=0, max_plies=80))
+    st = W.random_state(W.SMALL, 0)
+    meta["fingerprint_small_seed0"] = W.fingerprint(st)
+    save_case("small_seed0_b256", W.SMALL, 0, small0, reference_outputs(chess_net, export_ts, W.SMALL, st, small0),
+              "256 seed-0 playouts of 0..80 plies", meta)
+    save_case("small_seed0_fixed", W.SMALL, 0, fixed_batch,
+              reference_outputs(chess_net, export_ts, W.SMALL, st, fixed_batch), "fixed edge cases", meta)
+
+    # config 2 subsets: the 146M net, seed 1
+    st = W.random_state(W.FULL, 1)
+    meta["fingerprint_full_seed1"] = W.fingerprint(st)
+    b64 = P.encode_batch(seed1_pos[:64])
+    t = time.time()
+    save_case("full_seed1_b64", W.FULL, 1, b64, reference_outputs(chess_net, export_ts, W.FULL, st, b64),
+              "the first 64 seed-1 positions (positions_seed1.npz rows 0..63)", meta)
+    save_case("full_seed1_fixed", W.FULL, 1, fixed_batch,
+              reference_outputs(chess_net, export_ts, W.FULL, st, fixed_batch), "fixed edge cases", meta)
+    print(f"146M reference forward: {time.time() - t:.1f} s")
+    with open(os.path.join(HERE, "meta.json"), "w") as f:
+        json.dump(meta, f, indent=1)
+    print("done")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,95 @@
+"""Single kernels through the C ABI against plain PyTorch fp32 references of the same op (B200 only)."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def k():
+    from mayfly_chess_b200 import build, cudanet_py
+    build.build()
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return cudanet_py
+
+
+def _ref_gemm(A, W, bias, epi, C0=None):
+    y = A.float() @ W.float().t() + bias
+    if epi == 1:
+        y = F.gelu(y)
+    if epi == 2:
+        y = C0 + y
+    return y
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
+@pytest.mark.parametrize("M,N,K,bn", [(195, 1024, 1024, 0), (4160, 3072, 1024, 256), (1300, 1024, 2048, 128),
+                                      (65, 2048, 1024, 64), (300, 8324, 1024, 256), (128, 256, 64, 256)])
+def test_gemm(k, dtype, epi, M, N, K, bn):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K + epi)
+    A = torch.randn(M, K, device="cuda", generator=g).to(dtype)
+    W = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(dtype)
+    bias = torch.randn(N, device="cuda", generator=g) * 0.02
+    if epi in (0, 1):
+        C = torch.full((M, N), float("nan"), device="cuda", dtype=dtype)
+    else:
+        C = torch.randn(M, N, device="cuda", generator=g) if epi == 2 else torch.full((M, N), float("nan"),
+                                                                                     device="cuda")
+    C0 = C.clone()
+    k.k_gemm(A, W, bias, C, epi, bn)
+    torch.cuda.synchronize()
+    ref = _ref_gemm(A, W, bias, epi, C0.float())
+    err = (C.float() - ref).abs().max().item()
+    # f32 accumulation of K products of 16-bit inputs; 16-bit outputs add one rounding of the result
+    tol = 2e-3 if epi in (2, 3) else (8e-3 if dtype == torch.bfloat16 else 1.5e-3)
+    assert math.isfinite(err) and err < tol, err
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gemm_repeatable(k, dtype):
+    A = torch.randn(4160, 1024, device="cuda").to(dtype)
+    W = (torch.randn(2048, 1024, device="cuda") * 0.02).to(dtype)
+    b = torch.zeros(2048, device="cuda")
+    C1 = torch.empty(4160, 2048, device="cuda", dtype=dtype)
+    C2 = torch.empty_like(C1)
+    k.k_gemm(A, W, b, C1, 1)
+    k.k_gemm(A, W, b, C2, 1)
+    assert torch.equal(C1, C2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("d,heads", [(1024, 16), (256, 8)])
+@pytest.mark.parametrize("B", [1, 3, 64])
+def test_attention(k, dtype, d, heads, B):
+    rows = B * 65
+    qkv = torch.randn(rows, 3 * d, device="cuda").to(dtype)
+    att = torch.full((rows, d), float("nan"), device="cuda", dtype=dtype)
+    k.k_attention(qkv, att, B, d, heads)
+    torch.cuda.synchronize()
+    dh = d // heads
+    q, kk, v = qkv.float().view(B, 65, 3, heads, dh).permute(2, 0, 3, 1, 4).unbind(0)
+    o = torch.softmax(q @ kk.transpose(-1, -2) / math.sqrt(dh), -1) @ v
+    ref = o.transpose(1, 2).reshape(rows, d)
+    err = (att.float() - ref).abs().max().item()
+    assert math.isfinite(err) and err < (3e-2 if dtype == torch.bfloat16 else 4e-3), err
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("d", [256, 1024])
+@pytest.mark.parametrize("stride", [1, 65])
+def test_layernorm(k, dtype, d, stride):
+    n = 300
+    x = torch.randn(n * stride, d, device="cuda") * 3 + 0.5
+    g = torch.randn(d, device="cuda")
+    b = torch.randn(d, device="cuda")
+    h = torch.empty(n, d, device="cuda", dtype=dtype)
+    k.k_layernorm(x, g, b, h, n, d, stride)
+    torch.cuda.synchronize()
+    ref = F.layer_norm(x[::stride], (d,), g, b, 1e-5)
+    err = (h.float() - ref).abs().max().item()
+    assert err < (3e-2 if dtype == torch.bfloat16 else 4e-3), err

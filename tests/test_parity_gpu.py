@@ -1,0 +1,179 @@
+"""The evaluator end to end through the C ABI (CudaNet, the reference's Python interface) against golden
+outputs of the reference's own ChessNet (tests/golden, made by make_golden.py), on a B200.
+
+Tolerances (at the legal moves): policy logits max |diff| <= 2e-2 with bf16 products, win probabilities
+sigmoid(q) and (val+1)/2 within 5e-3, the top move agreeing on >= 99.5% of the rows and on every row without a
+near tie; the fp16 path (the reference backend's own precision) is held to 5e-3 on the logits. No non-finite
+value, padding exactly 0, and a second run over the same batches bit-identical (replays of captured graphs)."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import golden_case
+from parity import metrics
+from mayfly_chess_b200 import weights as W
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"bf16": {"pol_max": 2e-2, "q_max": 5e-3, "val_max": 5e-3},
+       "f16": {"pol_max": 5e-3, "q_max": 1e-3, "val_max": 1e-3}}
+TOP1_MIN = 0.995
+
+
+@pytest.fixture(scope="session")
+def nets(tmp_path_factory):
+    import torch
+    from mayfly_chess_b200 import build, cudanet_py
+    build.build()
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    d = tmp_path_factory.mktemp("cnw")
+    out = {}
+    states = {"small": (W.SMALL, W.random_state(W.SMALL, 0)), "full": (W.FULL, W.random_state(W.FULL, 1))}
+    for tag, (arch, st) in states.items():
+        for prec in ("bf16", "f16"):
+            path = os.path.join(d, f"{tag}_{prec}.cnw")
+            W.write_cnw(path, st, arch, prec)
+            out[(tag, prec)] = cudanet_py.CudaNet(path)
+    yield out
+    for n in out.values():
+        n.close()
+
+
+def run(net, b):
+    return net.evaluate(b["ids"], b["cast"], b["hm"], b["ep"], b["I"], b["M"])
+
+
+CASES = {"small": ["small_seed0_b256", "small_seed0_fixed"], "full": ["full_seed1_b64", "full_seed1_fixed"]}
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f16"])
+@pytest.mark.parametrize("tag", ["small", "full"])
+def test_parity_against_reference(nets, tag, prec):
+    net = nets[(tag, prec)]
+    assert net.precision() == prec
+    hits = rows = 0
+    for case in CASES[tag]:
+        b, ref = golden_case(case)
+        got = run(net, b)
+        m = metrics((ref["pol"], ref["val"], ref["qv"]), got, b["widths"])
+        print(case, prec, m)
+        for key, lim in TOL[prec].items():
+            assert m[key] <= lim, (case, key, m[key])
+        assert m["nonfinite"] == 0 and m["pad_nonzero"] == 0
+        assert m["top1_clear"] == 1.0, m
+        hits += m["top1_hits"]
+        rows += m["rows"]
+        again = run(net, b)
+        for x, y in zip(got, again):
+            assert np.array_equal(x, y), "two runs of the same batch differ"
+    assert hits / rows >= TOP1_MIN, (hits, rows)
+
+
+def test_full_logits(nets):
+    """The raw heads of the first rows against the reference's full policy and qvalue logits."""
+    net = nets[("full", "bf16")]
+    b, ref = golden_case("full_seed1_b64")
+    pol, val, qv, logits = net.evaluate_logits(b["ids"], b["cast"], b["hm"], b["ep"], b["I"], b["M"])
+    n = ref["policy_rows"].shape[0]
+    assert np.abs(logits[:n, :4162] - ref["policy_rows"]).max() <= 2e-2
+    q = 1 / (1 + np.exp(-logits[:n, 4162:].astype(np.float64)))
+    qr = 1 / (1 + np.exp(-ref["qvalue_rows"].astype(np.float64)))
+    assert np.abs(q - qr).max() <= 5e-3
+    p2, v2, q2 = run(net, b)
+    assert np.array_equal(pol, p2) and np.array_equal(val, v2) and np.array_equal(qv, q2)
+
+
+@pytest.mark.parametrize("B", [1, 3, 47, 64, 129])
+def test_batch_sizes_and_slices(nets, B):
+    """Odd batch sizes (M tails, one board) give each row the same numbers as the row had in a bigger batch
+    (rows are independent), within the rounding of the pass."""
+    net = nets[("full", "bf16")]
+    from mayfly_chess_b200.inputs import PositionSet
+    from conftest import GOLDEN
+    ps = PositionSet(os.path.join(GOLDEN, "positions_seed1.npz"))
+    big = ps.batch(0, 256)
+    pb, vb, qb = run(net, big)
+    small = ps.batch(0, B)
+    ps_, vs, qs = run(net, small)
+    w = small["I"].shape[1]
+    assert np.abs(ps_ - pb[:B, :w]).max() < 1e-4
+    assert np.abs(vs - vb[:B]).max() < 1e-4
+
+
+def test_begin_end_pipeline(nets):
+    net = nets[("full", "bf16")]
+    b1, _ = golden_case("full_seed1_b64")
+    b2, _ = golden_case("full_seed1_fixed")
+    want1, want2 = run(net, b1), run(net, b2)
+    net.begin(b1["ids"], b1["cast"], b1["hm"], b1["ep"], b1["I"], b1["M"])
+    net.begin(b2["ids"], b2["cast"], b2["hm"], b2["ep"], b2["I"], b2["M"])
+    with pytest.raises(RuntimeError):
+        net.begin(b1["ids"], b1["cast"], b1["hm"], b1["ep"], b1["I"], b1["M"])   # a third is refused
+    got1 = net.end()
+    got2 = net.end()
+    for x, y in zip(want1 + want2, got1 + got2):
+        assert np.array_equal(x, y)
+    with pytest.raises(RuntimeError):
+        net.end()
+
+
+def test_evaluate_device_matches_host(nets):
+    import torch
+    net = nets[("full", "bf16")]
+    b, _ = golden_case("full_seed1_b64")
+    want = run(net, b)
+    t = {k: torch.from_numpy(np.ascontiguousarray(b[k])).cuda() for k in ("ids", "cast", "hm", "ep", "I")}
+    M = torch.from_numpy(b["M"].astype(np.uint8)).cuda()
+    B, wide = b["I"].shape
+    pol = torch.empty(B, wide, device="cuda")
+    val = torch.empty(B, device="cuda")
+    qv = torch.empty(B, wide, device="cuda")
+    net.evaluate_device(t["ids"], t["cast"], t["hm"], t["ep"], t["I"], M, pol, val, qv)
+    net.check(torch.cuda.current_stream())
+    for x, y in zip(want, (pol.cpu().numpy(), val.cpu().numpy(), qv.cpu().numpy())):
+        assert np.array_equal(x, y)
+
+
+def test_errors_come_back_as_exceptions(nets):
+    net = nets[("small", "bf16")]
+    b, _ = golden_case("small_seed0_b256")
+    with pytest.raises(ValueError):
+        net.evaluate(b["ids"][:, :63], b["cast"], b["hm"], b["ep"], b["I"], b["M"])
+    with pytest.raises(ValueError):
+        net.evaluate(b["ids"][:0], b["cast"][:0], b["hm"][:0], b["ep"][:0], b["I"][:0], b["M"][:0])
+    wide = np.zeros((1, 257), np.int64)
+    with pytest.raises(RuntimeError, match="wide"):
+        net.evaluate(b["ids"][:1], b["cast"][:1], b["hm"][:1], b["ep"][:1], wide, wide.astype(bool))
+    # the handle still works afterwards
+    run(net, b)
+
+
+def test_bad_indices_are_clamped(nets):
+    """Out-of-range piece ids, clocks and policy indices read inside their tables (kernels clamp them)."""
+    net = nets[("small", "bf16")]
+    b, _ = golden_case("small_seed0_b256")
+    ids = b["ids"][:4].copy()
+    ids[:, 0] = 99
+    hm = np.array([-5, 500, 101, 0], np.int64)
+    I = b["I"][:4].copy()
+    I[:, 0] = 100000
+    pol, val, qv = net.evaluate(ids, b["cast"][:4], hm, b["ep"][:4], I, b["M"][:4])
+    assert np.isfinite(pol).all() and np.isfinite(val).all() and np.isfinite(qv).all()
+
+
+def test_fingerprint_and_profile(nets, meta):
+    net = nets[("full", "bf16")]
+    assert net.fingerprint() == meta["fingerprint_full_seed1"]
+    prof = net.profile(64, reps=2)
+    assert list(prof)[-1] == "graph_pass" and all(v >= 0 for v in prof.values())
+    assert prof["graph_pass"] > 0
+
+
+def test_bad_weight_file(tmp_path):
+    from mayfly_chess_b200 import cudanet_py
+    p = tmp_path / "bad.cnw"
+    p.write_bytes(b"MFCNW001" + b"\x02\x00\x00\x00{}")
+    with pytest.raises(RuntimeError, match="cudanet_create"):
+        cudanet_py.CudaNet(str(p))

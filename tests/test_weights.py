@@ -1,0 +1,71 @@
+"""The weight file, the seeded random init and the fingerprint (CPU only)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from mayfly_chess_b200 import weights as W
+
+
+@pytest.mark.parametrize("tag,arch", [("small", W.SMALL), ("full", W.FULL)])
+def test_state_spec_is_chessnets(meta, tag, arch):
+    """The parameter list the random init walks is ChessNet's own state dict order (recorded from the reference
+    model by the fixture generator)."""
+    assert [k for k, _ in W.state_spec(arch)] == meta[f"state_keys_{tag}"]
+
+
+def test_fingerprints(meta):
+    assert W.fingerprint(W.random_state(W.SMALL, 0)) == meta["fingerprint_small_seed0"]
+    assert W.fingerprint(W.random_state(W.FULL, 1)) == meta["fingerprint_full_seed1"]
+
+
+def test_random_state_rule():
+    st = W.random_state(W.SMALL, 0)
+    assert torch.equal(st["enc.layers.0.norm1.weight"], torch.ones(256))
+    assert torch.equal(st["ln.bias"], torch.zeros(256))
+    w = st["enc.layers.0.linear1.weight"]
+    assert abs(float(w.std()) - 0.02) < 0.001 and abs(float(w.mean())) < 0.001
+    # same seed, same weights; another seed, other weights
+    assert torch.equal(W.random_state(W.SMALL, 0)["piece.weight"], st["piece.weight"])
+    assert not torch.equal(W.random_state(W.SMALL, 1)["piece.weight"], st["piece.weight"])
+
+
+@pytest.mark.parametrize("precision", ["f16", "bf16", "e4m3"])
+def test_cnw_roundtrip(tmp_path, precision):
+    st = W.random_state(W.SMALL, 0)
+    path = os.path.join(tmp_path, "n.cnw")
+    hdr = W.write_cnw(path, st, W.SMALL, precision)
+    h2, t = W.read_cnw(path)
+    assert h2 == hdr
+    assert h2["version"] == (1 if precision == "f16" else 2)
+    assert h2["fingerprint"] == W.fingerprint(st)
+    for e in h2["tensors"]:
+        assert e["offset"] % 256 == 0
+    np.testing.assert_array_equal(t["piece"], st["piece.weight"].numpy())
+    q = t["L1.ff2_w"]
+    ref = st["enc.layers.1.linear2.weight"]
+    if precision == "f16":
+        np.testing.assert_array_equal(q, ref.half().numpy())
+    elif precision == "bf16":
+        np.testing.assert_array_equal(W.bf16_bits_to_f32(q).numpy(), ref.bfloat16().float().numpy())
+    else:
+        deq = W.e4m3_to_f32(q, t["L1.ff2_w_scale"])
+        rel = (deq - ref).abs().max() / ref.abs().max()
+        assert rel < 2 ** -3      # e4m3 keeps 3 mantissa bits
+    # the heads stay 16-bit in every precision
+    assert t["heads_w"].dtype == (np.float16 if precision == "f16" else np.uint16)
+
+
+def test_cnw_rejects_bad_magic(tmp_path):
+    path = os.path.join(tmp_path, "bad.cnw")
+    with open(path, "wb") as f:
+        f.write(b"NOTCNW01" + b"\0" * 64)
+    with pytest.raises(ValueError):
+        W.read_cnw(path)
+
+
+def test_bf16_rounding_is_nearest_even():
+    x = torch.tensor([1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -2.5e-3], dtype=torch.float32)
+    bits = W.to_bf16_bits(x)
+    assert torch.equal(W.bf16_bits_to_f32(bits), x.bfloat16().float())
