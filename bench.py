@@ -1,0 +1,343 @@
+"""Throughput of MayFly's batched network evaluation on B200s: positions evaluated per second.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch 1024] [--precision bf16|f16] [--impl reference]
+
+Workload (the metric's configuration): the 146M trunk (d 1024, 16 layers, 16 heads, FFN
+2048, 65 tokens, policy + qvalue heads and the search's reduction) with seed-1 random-init weights in bf16,
+evaluating 1,024 seed-1 random-playout positions per GPU per step (tests/golden/positions_seed1.npz; rank r
+takes positions r*1024 .. r*1024+1023, so 8 ranks cover the whole 8,192-position set of config 5). One
+independent evaluator per GPU, no collective on the data path (weak scaling: 1,024 positions per GPU).
+
+  value      positions/s with inputs resident in HBM: K passes through cudanet_evaluate_device, timed with
+             CUDA events on the launching stream between a barrier + synchronize on both sides, max over ranks.
+             The working set (285 MB of weights, ~1.2 GB of activations) is far larger than L2.
+  e2e        the same metric through the reference-facing API, CudaNet.evaluate on host numpy arrays: each step
+             copies the inputs into pinned staging and up, and the outputs down and out (wall clock).
+  roofline   the dominant kernel, the tcgen05 GEMM (all 64 trunk products of a pass): algorithmic FLOPs per
+             launch / mean launch time, from per-step CUDA events of an eager pass (cudanet_profile), against
+             the measured sustained bf16 peak.
+  cpu_baseline  the CPU fp32 restatement of the reference forward (oracle/, test infrastructure) on a bounded
+             sample on this host's cores.
+
+--impl reference times the reference's CPU path (the same fp32 restatement, all host threads) on the same
+metric, rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "NN positions evaluated/sec (146M trunk, bs1024, 1/2/4/8 B200); p50 latency at bs64"
+POSITIONS = os.path.join(REPO, "tests", "golden", "positions_seed1.npz")
+PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def flops_per_position(d=1024, layers=16, heads=16, ff=2048, tokens=65, moves=4162):
+    """Algorithmic FLOPs of one position (multiply-add = 2): the four trunk products, attention, the heads."""
+    gemm = tokens * layers * (3 * d * d + d * d + 2 * d * ff)
+    att = layers * heads * 2 * tokens * tokens * (d // heads)
+    return 2 * (gemm + att + 2 * moves * d), 2 * gemm
+
+
+def rank_env():
+    r = int(os.environ.get("RANK", "0"))
+    w = int(os.environ.get("WORLD_SIZE", "1"))
+    lr = int(os.environ.get("LOCAL_RANK", str(r)))
+    return r, w, lr
+
+
+class Clocks:
+    """nvidia-smi samples of one GPU every 200 ms while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 8:
+                continue
+            try:
+                sm.append(float(p[0]))
+                mx.append(float(p[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, p[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def load_peaks():
+    try:
+        with open(PEAKS) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return FALLBACK_PEAKS, "fallback"
+
+
+def cpu_sample(n_pos, threads):
+    """Positions/s of the CPU fp32 oracle (test infrastructure) on n_pos positions of the workload."""
+    import torch
+    from mayfly_chess_b200 import weights as W
+    from mayfly_chess_b200.inputs import PositionSet
+    from oracle import chessnet_oracle as O
+    torch.set_num_threads(threads)
+    st = W.random_state(W.FULL, 1)
+    b = PositionSet(POSITIONS).batch(0, n_pos)
+    O.evaluate(st, W.FULL, PositionSet(POSITIONS).batch(n_pos, 2))      # warm-up
+    t0 = time.perf_counter()
+    O.evaluate(st, W.FULL, b)
+    return n_pos / (time.perf_counter() - t0)
+
+
+def bench_reference(args):
+    """--impl reference: the reference's CPU implementation of the path (its fp32 forward and _collect
+    arithmetic, restated in oracle/chessnet_oracle.py; the reference's own code cannot travel here) timed with
+    every host thread; each step is a bounded sample of the workload's positions."""
+    rank, world, _ = rank_env()
+    if rank != 0:
+        return
+    import torch
+    from mayfly_chess_b200 import weights as W
+    from mayfly_chess_b200.inputs import PositionSet
+    from oracle import chessnet_oracle as O
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    st = W.random_state(W.FULL, 1)
+    ps = PositionSet(POSITIONS)
+    n = args.ref_sample
+    for i in range(args.warmup):
+        O.evaluate(st, W.FULL, ps.batch(i * n, n))
+    times = []
+    for i in range(args.steps):
+        b = ps.batch((args.warmup + i) * n, n)
+        t0 = time.perf_counter()
+        O.evaluate(st, W.FULL, b)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    v = n * args.steps / total
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "positions/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "146M trunk fp32 on the host CPU (reference forward + _collect), seed-1 weights, "
+                               f"{n} seed-1 positions per step", "batch": n, "parallelism": "host threads"},
+        "cpu_baseline": {"value": v, "unit": "positions/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} steps of {n} positions (fp32 torch restatement of ChessNet + post)"},
+        "e2e": {"value": v, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1024)
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "f16"])
+    ap.add_argument("--impl", default="own", choices=["own", "reference"])
+    ap.add_argument("--ref-sample", type=int, default=16, help="positions per step of the reference arm")
+    ap.add_argument("--cpu-sample", type=int, default=32, help="positions of the cpu_baseline sample")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        return bench_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    from mayfly_chess_b200 import weights as W
+    from mayfly_chess_b200.cudanet_py import CudaNet
+    from mayfly_chess_b200.inputs import PositionSet
+
+    rank, world, local = rank_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    B = args.batch
+    arch = W.FULL
+    st = W.random_state(arch, 1)
+    tmp = tempfile.mkdtemp(prefix="mayfly_b200_")
+    path = os.path.join(tmp, f"net_{args.precision}_{rank}.cnw")
+    W.write_cnw(path, st, arch, args.precision)
+    os.environ.setdefault("MAYFLY_CUDANET_MAX_BATCH", str(max(B, 1024)))
+    net = CudaNet(path, device=local)
+    os.remove(path)
+    ps = PositionSet(POSITIONS)
+    b = ps.batch(rank * B, B)
+    wide = b["I"].shape[1]
+
+    # ---------------------------------------------------------------- value: inputs resident in HBM
+    dev = {k: torch.from_numpy(np.ascontiguousarray(b[k])).cuda() for k in ("ids", "cast", "hm", "ep", "I")}
+    Md = torch.from_numpy(b["M"].astype(np.uint8)).cuda()
+    pol = torch.empty(B, wide, device="cuda")
+    val = torch.empty(B, device="cuda")
+    qv = torch.empty(B, wide, device="cuda")
+
+    def step_dev():
+        net.evaluate_device(dev["ids"], dev["cast"], dev["hm"], dev["ep"], dev["I"], Md, pol, val, qv)
+
+    for _ in range(args.warmup):
+        step_dev()
+    net.check(torch.cuda.current_stream())
+    vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    clocks = Clocks(vis[local] if local < len(vis) else local)   # nvidia-smi counts physical devices
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        step_dev()
+    e1.record(s)
+    barrier()
+    clk = clocks.stop()
+    net.check(s)
+    dev_ms = e0.elapsed_time(e1)
+    dev_ms = max_over_ranks(dev_ms)
+    value = world * B * args.steps / (dev_ms / 1000.0)
+
+    # ---------------------------------------------------------------- e2e: host arrays through the C ABI
+    for _ in range(2):
+        net.evaluate(b["ids"], b["cast"], b["hm"], b["ep"], b["I"], b["M"])
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        p_h, v_h, q_h = net.evaluate(b["ids"], b["cast"], b["hm"], b["ep"], b["I"], b["M"])
+    e2e_s = time.perf_counter() - t0
+    barrier()
+    e2e_s = max_over_ranks(e2e_s)
+    e2e = world * B * args.steps / e2e_s
+    h2d = B * (64 * 8 + 8 + 8 + 16) + B * wide * 9
+    d2h = 256 + 4 * B * (2 * wide + 1)
+
+    # ---------------------------------------------------------------- roofline of the dominant kernel
+    prof = net.profile(B, reps=3)
+    fl_pos, gemm_fl_pos = flops_per_position()
+    trunk_gemm_ms = prof["qkv"] + prof["out"] + prof["ff1"] + prof["ff2"]
+    launches = 4 * arch.layers
+    per_launch_s = trunk_gemm_ms / 1000.0 / launches
+    achieved = gemm_fl_pos * B / launches / per_launch_s / 1e12
+    peaks, peak_kind = load_peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+
+    # ---------------------------------------------------------------- latency (config 3) and CPU baseline
+    sweep = {}
+    if not args.no_sweep:
+        for Bs in (1, 16, 64, 128, 256):
+            bs = ps.batch(rank * B, Bs)
+            for _ in range(5):
+                net.evaluate(bs["ids"], bs["cast"], bs["hm"], bs["ep"], bs["I"], bs["M"])
+            ts = []
+            for _ in range(200):
+                t0 = time.perf_counter()
+                net.evaluate(bs["ids"], bs["cast"], bs["hm"], bs["ep"], bs["I"], bs["M"])
+                ts.append(time.perf_counter() - t0)
+            ts.sort()
+            p50, p99 = ts[len(ts) // 2], ts[int(len(ts) * 0.99)]
+            wbytes = 285483008 + 811008   # bf16 matrices + f32 vectors read once per call
+            sweep[str(Bs)] = {"p50_ms": 1000 * p50, "p99_ms": 1000 * p99, "positions_per_s": Bs / p50,
+                              "weight_stream_gbs": wbytes / p50 / 1e9}
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        v = cpu_sample(args.cpu_sample, cores)
+        cpu = {"value": v, "unit": "positions/s", "cores": cores, "kind": "port",
+               "sample": f"{args.cpu_sample} seed-1 positions of the 146M net, fp32 torch restatement of the "
+                         "reference forward + post (oracle/), one call"}
+
+    net.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    out = {
+        "metric": METRIC, "value": value, "unit": "positions/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
+        "config": {"workload": "config 2: 146M trunk (d1024 L16 H16 FF2048, 65 tokens), seed-1 random-init "
+                               f"weights, {B} seed-1 random-playout positions per GPU per step",
+                   "batch_per_gpu": B, "global_batch": B * world, "wide": wide, "precision": args.precision,
+                   "parallelism": f"replicas x{world} (no collective)",
+                   "l2": "working set larger than L2 (285 MB weights + ~1.2 GB activations per pass)"},
+        "e2e": {"value": e2e, "unit": "positions/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": (1 + 7 * arch.layers - 1 + 2 + 1) * args.steps,
+        "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (qkv, out, ff1, ff2 of every layer)",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} bf16 sustained", "traffic": None,
+                     "flop_per_launch": gemm_fl_pos * B / launches},
+        "pass": {"flop_per_position": fl_pos, "tflops_whole_pass": fl_pos * value / world / 1e12,
+                 "frac_whole_pass": fl_pos * value / world / 1e12 / peak, "profile_ms": prof},
+        "p50_latency_ms_bs64": sweep.get("64", {}).get("p50_ms"),
+        "clocks": clk,
+        "latency_sweep": sweep,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -16,6 +16,9 @@ What it does:
      cudanet/test_cudanet.py:177-194 reference() does.
   3. Writes, per case, the inputs and the reference outputs at the legal moves (pol with 0 on padding, val, qv
      with 0 on padding) plus the full logits of a few rows, and the 8,192-position seed-1 set the bench uses.
+     Each case also holds the outputs of the same reference model with its weight matrices rounded as a bf16
+     or an e4m3 weight file stores them (pol_bf16w, pol_e4m3w, ...), which separates what the prescribed weight
+     rounding costs from what the evaluator's own arithmetic costs.
 
 Fixtures (all small .npz):
   positions_seed1.npz         8,192 seed-1 positions, compact (mayfly_chess_b200/inputs.py PositionSet)
@@ -135,11 +138,16 @@ def check_state_spec(chess_net, arch):
     return [k for k, _ in ref]
 
 
-def save_case(name, arch, seed, batch, outs, note, meta, full_rows=4):
+def save_case(name, arch, seed, batch, outs, note, meta, full_rows=4, rounded=None):
+    """rounded: {tag: outputs} of the same reference model with its weights rounded the way a weight file of
+    that precision stores them (mayfly_chess_b200.weights.dequantised_state), saved as pol_<tag> etc."""
     P, V, Q, pol_full, q_full = outs
+    extra = {}
+    for tag, (p2, v2, q2, _, _) in (rounded or {}).items():
+        extra.update({f"pol_{tag}": p2, f"val_{tag}": v2, f"qv_{tag}": q2})
     np.savez_compressed(os.path.join(HERE, name + ".npz"), **pack(batch), pol=P, val=V, qv=Q,
                         policy_rows=pol_full[:full_rows].astype(np.float32),
-                        qvalue_rows=q_full[:full_rows].astype(np.float32))
+                        qvalue_rows=q_full[:full_rows].astype(np.float32), **extra)
     meta["cases"][name] = {"arch": [arch.d, arch.layers, arch.heads, arch.ff], "seed": seed,
                            "B": int(batch["ids"].shape[0]), "wide": int(batch["I"].shape[1]), "note": note}
 
@@ -173,20 +181,27 @@ def main():
     small0 = P.encode_batch(P.random_playouts(256, seed=0, max_plies=80))
     st = W.random_state(W.SMALL, 0)
     meta["fingerprint_small_seed0"] = W.fingerprint(st)
-    save_case("small_seed0_b256", W.SMALL, 0, small0, reference_outputs(chess_net, export_ts, W.SMALL, st, small0),
-              "256 seed-0 playouts of 0..80 plies", meta)
-    save_case("small_seed0_fixed", W.SMALL, 0, fixed_batch,
-              reference_outputs(chess_net, export_ts, W.SMALL, st, fixed_batch), "fixed edge cases", meta)
+    def run(arch, st, batch):
+        outs = reference_outputs(chess_net, export_ts, arch, st, batch)
+        rounded = {tag: reference_outputs(chess_net, export_ts, arch, W.dequantised_state(st, arch, prec), batch)
+                   for tag, prec in (("bf16w", "bf16"), ("e4m3w", "e4m3"))}
+        return outs, rounded
+
+    o, rd = run(W.SMALL, st, small0)
+    save_case("small_seed0_b256", W.SMALL, 0, small0, o, "256 seed-0 playouts of 0..80 plies", meta, rounded=rd)
+    o, rd = run(W.SMALL, st, fixed_batch)
+    save_case("small_seed0_fixed", W.SMALL, 0, fixed_batch, o, "fixed edge cases", meta, rounded=rd)
 
     # config 2 subsets: the 146M net, seed 1
     st = W.random_state(W.FULL, 1)
     meta["fingerprint_full_seed1"] = W.fingerprint(st)
     b64 = P.encode_batch(seed1_pos[:64])
     t = time.time()
-    save_case("full_seed1_b64", W.FULL, 1, b64, reference_outputs(chess_net, export_ts, W.FULL, st, b64),
-              "the first 64 seed-1 positions (positions_seed1.npz rows 0..63)", meta)
-    save_case("full_seed1_fixed", W.FULL, 1, fixed_batch,
-              reference_outputs(chess_net, export_ts, W.FULL, st, fixed_batch), "fixed edge cases", meta)
+    o, rd = run(W.FULL, st, b64)
+    save_case("full_seed1_b64", W.FULL, 1, b64, o, "the first 64 seed-1 positions (positions_seed1.npz rows 0..63)",
+              meta, rounded=rd)
+    o, rd = run(W.FULL, st, fixed_batch)
+    save_case("full_seed1_fixed", W.FULL, 1, fixed_batch, o, "fixed edge cases", meta, rounded=rd)
     print(f"146M reference forward: {time.time() - t:.1f} s")
     with open(os.path.join(HERE, "meta.json"), "w") as f:
         json.dump(meta, f, indent=1)
