@@ -14,11 +14,19 @@
 //   warp 0      one thread issues TMA tile loads (128-byte swizzle) of A and W into a STAGES-deep ring
 //   warp 1      allocates tensor memory (2 accumulators of BN f32 columns); one thread issues tcgen05.mma
 //               (M=128, N=BN, K=16 per instruction) and tcgen05.commit to release ring stages / accumulators
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31, one row per
-//               thread), bias / GELU / residual, store; then hand the accumulator back to the MMA warp
-// The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1. Tiles run M-block-major
-// (all N blocks of an M block back to back), so an A block is read from HBM once and the weights stay in L2.
-// Out-of-range rows (M tail) and columns (N tail) are zero-filled by TMA and skipped by the epilogue.
+//   warps 2..5  epilogue, one output row per thread: tcgen05.ld of the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+31), bias / GELU / residual, then the row goes into a 128-row x 128-byte staging
+//               chunk in shared memory (128-byte swizzle) and one thread stores the chunk with a TMA tensor
+//               store (coalesced, asynchronous). For the residual the chunk of X is first TMA-loaded into the
+//               same staging buffer, several chunks ahead (also across tiles), so the read-modify-write of the
+//               f32 residual stream is pure bulk traffic.
+// The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1. Tiles run M-block-major (all
+// N blocks of an M block back to back), so an A block is read from HBM once and the weights stay in L2.
+// Out-of-range rows and columns (M and N tails) are zero-filled by TMA loads and clipped by TMA stores.
+//
+// Every wait is bounded (ptx.cuh). Epilogue decisions are made by one thread and broadcast through shared
+// memory at a named barrier, so the four epilogue warps always take the same path and never strand one
+// another at a barrier.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -33,16 +41,26 @@ template <typename T> struct Fmt;
 template <> struct Fmt<__half> { static constexpr uint32_t v = 0; };
 template <> struct Fmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
 
-template <int BN> struct GemmCfg {
+template <int BN, int EPI> struct GemmCfg {
     static constexpr int BM = 128;
     static constexpr int BK = 64;                       // 64 x 16-bit = one 128-byte swizzle row
-    static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr bool RESID = EPI == kEpiResidual;
+    static constexpr int OUT_BYTES = (EPI == kEpiResidual || EPI == kEpiF32) ? 4 : 2;
+    static constexpr int CHUNK_COLS = 128 / OUT_BYTES;   // one staging chunk: 128 rows x 128 bytes
+    static constexpr int NC = BN / CHUNK_COLS;           // staging chunks per tile
+    static constexpr uint32_t CHUNK_BYTES = 128 * 128;
+    static constexpr int NBUF = RESID ? 4 : 2;           // staging buffers
     static constexpr uint32_t A_BYTES = BM * BK * 2;
     static constexpr uint32_t B_BYTES = BN * BK * 2;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES_FIT = (224 * 1024 - NBUF * (int)CHUNK_BYTES) / (int)STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-    static constexpr size_t SMEM = 1024 + STAGES * (size_t)STAGE_BYTES + 256;
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (size_t)NBUF * CHUNK_BYTES + 256;
     static constexpr int THREADS = 192;
+    static_assert(STAGES >= 3, "pipeline too shallow");
+    static_assert(SMEM <= 232448, "shared memory over the per-block limit");
+    static_assert(BN % CHUNK_COLS == 0, "tile width must hold whole staging chunks");
 };
 
 __device__ __forceinline__ float gelu_erf(float x)
@@ -63,104 +81,51 @@ template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, fl
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// The epilogue of 32 consecutive columns col0..col0+31 of one row, r[] holding the raw f32 accumulators.
-// out and bias are 16-byte aligned (checked by the host); vector accesses are used only when every row of
-// out is 16-byte aligned too (ldc a multiple of 16 bytes), scalar ones otherwise and on the N tail.
-template <typename T, int EPI>
-__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int row, int col0, int N, int ldc,
-                                               const float* __restrict__ bias, void* __restrict__ out)
+// v[off + i] += bias[col0 + i], i < 32; vector loads when the whole run is inside N (bias is 16-byte aligned)
+template <int NV>
+__device__ __forceinline__ void add_bias32(float (&v)[NV], int off, const float* __restrict__ bias, int col0, int N)
 {
-    float v[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-    const bool full = col0 + 32 <= N;
-    if (full) {
+    if (col0 + 32 <= N) {
         const float4* b4 = reinterpret_cast<const float4*>(bias + col0);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const float4 b = __ldg(b4 + i);
-            v[4 * i + 0] += b.x;
-            v[4 * i + 1] += b.y;
-            v[4 * i + 2] += b.z;
-            v[4 * i + 3] += b.w;
+            v[off + 4 * i + 0] += b.x;
+            v[off + 4 * i + 1] += b.y;
+            v[off + 4 * i + 2] += b.z;
+            v[off + 4 * i + 3] += b.w;
         }
     } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-            if (col0 + i < N) v[i] += __ldg(bias + col0 + i);
-    }
-    if constexpr (EPI == kEpiBiasGelu) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
-    }
-    if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu) {
-        T* o = reinterpret_cast<T*>(out) + (size_t)row * ldc + col0;
-        if (full && (ldc % 8) == 0) {   // 16-byte stores need 16-byte aligned rows
-            uint4* o4 = reinterpret_cast<uint4*>(o);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                uint4 q;
-                q.x = pack2<T>(v[8 * i + 0], v[8 * i + 1]);
-                q.y = pack2<T>(v[8 * i + 2], v[8 * i + 3]);
-                q.z = pack2<T>(v[8 * i + 4], v[8 * i + 5]);
-                q.w = pack2<T>(v[8 * i + 6], v[8 * i + 7]);
-                o4[i] = q;
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (col0 + i < N) o[i] = static_cast<T>(v[i]);
-        }
-    } else if constexpr (EPI == kEpiResidual) {
-        float* x = reinterpret_cast<float*>(out) + (size_t)row * ldc + col0;
-        if (full && (ldc % 4) == 0) {
-            float4* x4 = reinterpret_cast<float4*>(x);
-            float4 old[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) old[i] = x4[i];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                old[i].x += v[4 * i + 0];
-                old[i].y += v[4 * i + 1];
-                old[i].z += v[4 * i + 2];
-                old[i].w += v[4 * i + 3];
-                x4[i] = old[i];
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (col0 + i < N) x[i] += v[i];
-        }
-    } else {  // kEpiF32
-        float* o = reinterpret_cast<float*>(out) + (size_t)row * ldc + col0;
-        if (full && (ldc % 4) == 0) {
-            float4* o4 = reinterpret_cast<float4*>(o);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (col0 + i < N) o[i] = v[i];
-        }
+            if (col0 + i < N) v[off + i] += __ldg(bias + col0 + i);
     }
 }
 
+// byte offset of 16-byte unit j of row r in a 128-byte-swizzled staging chunk (what a TMA tensor map with
+// CU_TENSOR_MAP_SWIZZLE_128B reads and writes; the chunk base is 1024-byte aligned)
+__device__ __forceinline__ uint32_t swz(int r, int j) { return (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)); }
+
 template <typename T, int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-               int K, const float* __restrict__ bias, void* __restrict__ out, int ldc, uint32_t* err)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmC, int M, int N, int K, const float* __restrict__ bias,
+               uint32_t* err)
 {
-    using C = GemmCfg<BN>;
+    using C = GemmCfg<BN, EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+    uint8_t* sC = sB + C::STAGES * C::B_BYTES;                        // NBUF staging chunks
+    uint64_t* full = reinterpret_cast<uint64_t*>(sC + C::NBUF * C::CHUNK_BYTES);
     uint64_t* empty = full + C::STAGES;
     uint64_t* tfull = empty + C::STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* mma_done = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    uint64_t* xfull = mma_done + 1;                                    // NBUF (residual loads)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + C::NBUF);
+    volatile uint32_t* epi_ok = tmem_slot + 1;                         // the epilogue's broadcast flag
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m_tiles = (M + C::BM - 1) / C::BM;
@@ -178,9 +143,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_init(&tempty[b], 4);
         }
         mbar_init(mma_done, 1);
+        for (int b = 0; b < C::NBUF; ++b) mbar_init(&xfull[b], 1);
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        tma_prefetch_desc(&tmC);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -262,33 +229,141 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             umma_commit(mma_done);
             mbar_wait(mma_done, 0, err, kErrTmemFull);
         }
-    } else {
+    } else if (k_iters > 0) {
         // ---------------------------------------------------------------- epilogue (warps 2..5)
         const int quarter = warp & 3;
-        const int row_in_tile = quarter * 32 + lane;
+        const int row = quarter * 32 + lane;                  // row of the tile this thread owns
+        const bool leader = threadIdx.x == 64;                // issues the epilogue's TMA traffic
+        const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const int my_tiles = (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const int total_chunks = my_tiles * C::NC;
+
+        // chunk h of this CTA: tile blockIdx.x + (h / NC) * gridDim.x, columns (h % NC) * CHUNK_COLS
+        auto chunk_xy = [&](int h, int& x, int& y) {
+            const int tile = (int)blockIdx.x + (h / C::NC) * (int)gridDim.x;
+            x = (tile % n_tiles) * BN + (h % C::NC) * C::CHUNK_COLS;
+            y = (tile / n_tiles) * C::BM;
+        };
+        int loads = 0;    // residual chunks whose load the leader issued
+        if constexpr (C::RESID) {
+            if (leader)
+                for (; loads < C::NBUF && loads < total_chunks; ++loads) {
+                    int x, y;
+                    chunk_xy(loads, x, y);
+                    mbar_arrive_expect_tx(&xfull[loads], C::CHUNK_BYTES);
+                    tma_load_2d(sC + loads * C::CHUNK_BYTES, &tmC, &xfull[loads], x, y);
+                }
+        }
+
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < num_tiles && k_iters > 0; tile += gridDim.x) {
+        bool ok = true;
+        int g = 0;        // chunks done
+        for (int it = 0; it < my_tiles && ok; ++it) {
+            const int tile = (int)blockIdx.x + it * (int)gridDim.x;
             const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
-            if (!mbar_wait(&tfull[acc], acc_phase, err, kErrTmemFull)) break;
+            if (leader) *epi_ok = mbar_wait(&tfull[acc], acc_phase, err, kErrTmemFull) ? 1u : 0u;
+            named_barrier(1, 128);
+            if (!*epi_ok) break;
             tc_fence_after();
-            const int row = m_blk * C::BM + row_in_tile;
-            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                   static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
-                const int col0 = n_blk * BN + c;
-                if (col0 >= N) break;   // whole warp agrees: col0 does not depend on the lane
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c), r);
-                tmem_ld_wait();
-                if (row < M) epilogue_chunk<T, EPI>(r, row, col0, N, ldc, bias, out);
+            const uint32_t t_acc = t_lane + static_cast<uint32_t>(acc * BN);
+            for (int c = 0; c < C::NC; ++c, ++g) {
+                const int b = g % C::NBUF;
+                uint8_t* buf = sC + b * C::CHUNK_BYTES;
+                const int col0 = n_blk * BN + c * C::CHUNK_COLS;
+                // the accumulator columns of this chunk (one or two 32-column loads)
+                float v[C::CHUNK_COLS];
+                {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * C::CHUNK_COLS), r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                    if constexpr (C::CHUNK_COLS == 64) {
+                        tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * C::CHUNK_COLS + 32), r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
+                    }
+                }
+                if (c == C::NC - 1) {
+                    // the accumulator is drained: hand it back to the MMA warp
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[acc]);
+                }
+                add_bias32<C::CHUNK_COLS>(v, 0, bias, col0, N);
+                if constexpr (C::CHUNK_COLS == 64) add_bias32<C::CHUNK_COLS>(v, 32, bias, col0 + 32, N);
+                if constexpr (EPI == kEpiBiasGelu) {
+#pragma unroll
+                    for (int i = 0; i < C::CHUNK_COLS; ++i) v[i] = gelu_erf(v[i]);
+                }
+                // the staging buffer must be ready: loaded (residual) or no longer read by its last store
+                if constexpr (C::RESID) {
+                    if (leader) *epi_ok = mbar_wait(&xfull[b], (g / C::NBUF) & 1u, err, kErrTmaFull) ? 1u : 0u;
+                } else {
+                    if (leader) bulk_wait_read<C::NBUF - 1>();
+                }
+                named_barrier(1, 128);
+                if (!*epi_ok) {
+                    ok = false;
+                    break;
+                }
+                if constexpr (C::RESID) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        float4* p = reinterpret_cast<float4*>(buf + swz(row, j));
+                        float4 x = *p;
+                        x.x += v[4 * j + 0];
+                        x.y += v[4 * j + 1];
+                        x.z += v[4 * j + 2];
+                        x.w += v[4 * j + 3];
+                        *p = x;
+                    }
+                } else if constexpr (C::OUT_BYTES == 4) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        *reinterpret_cast<float4*>(buf + swz(row, j)) =
+                            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        uint4 q;
+                        q.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
+                        q.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
+                        q.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
+                        q.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
+                        *reinterpret_cast<uint4*>(buf + swz(row, j)) = q;
+                    }
+                }
+                fence_proxy_async_smem();
+                named_barrier(1, 128);
+                if (leader) {
+                    tma_store_2d(&tmC, buf, col0, m_blk * C::BM);
+                    bulk_commit();
+                    if constexpr (C::RESID) {
+                        // refill the previous chunk's buffer (its store has been read) NBUF chunks ahead
+                        const int next = g - 1 + C::NBUF;
+                        if (g >= 1 && next < total_chunks && next >= loads) {
+                            bulk_wait_read<1>();
+                            const int nb = next % C::NBUF;
+                            int x, y;
+                            chunk_xy(next, x, y);
+                            mbar_arrive_expect_tx(&xfull[nb], C::CHUNK_BYTES);
+                            tma_load_2d(sC + nb * C::CHUNK_BYTES, &tmC, &xfull[nb], x, y);
+                            loads = next + 1;
+                        }
+                    }
+                }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
             acc ^= 1;
             if (acc == 0) acc_phase ^= 1u;
+        }
+        if (leader) {
+            bulk_wait_all();
+            // residual loads issued but never consumed (only after a failure) land before the CTA leaves
+            if constexpr (C::RESID)
+                for (int h = g; h < loads; ++h) mbar_wait(&xfull[h % C::NBUF], (h / C::NBUF) & 1u, err, kErrTmaFull);
         }
     }
 

@@ -23,6 +23,7 @@
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "../../include/cudanet_b200.h"
@@ -72,19 +73,27 @@ static EncodeTiledFn encode_tiled()
     return fn;
 }
 
-// A K-major 16-bit matrix [outer, inner] with row pitch `inner` elements, tiles of 64 x box_outer, 128-byte
-// swizzle (the layout sdesc_sw128 describes). Rows past `outer` read as zero.
-static CUtensorMap make_map(const void* base, bool bf16, uint64_t inner, uint64_t outer, uint32_t box_outer)
+// A row-major matrix [outer, inner] with row pitch `pitch` elements, tiles of box_inner x box_outer with the
+// 128-byte swizzle (box_inner * element size = 128 bytes: the layout sdesc_sw128 and the epilogue's staging
+// describe). Reads past the extents are zero, writes past them are dropped.
+enum class MapType { F16, BF16, F32 };
+
+static CUtensorMap make_map(const void* base, MapType type, uint64_t inner, uint64_t outer, uint64_t pitch,
+                            uint32_t box_inner, uint32_t box_outer)
 {
-    if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner * 2) % 16)
-        throw std::runtime_error("cudanet_b200: a TMA operand is not 16-byte aligned");
+    const uint64_t es = type == MapType::F32 ? 4 : 2;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch * es) % 16)
+        throw std::runtime_error("cudanet_b200: a TMA operand or its row pitch is not 16-byte aligned");
+    if (box_inner * es != 128) throw std::runtime_error("cudanet_b200: TMA box rows must be 128 bytes");
     CUtensorMap m;
     const cuuint64_t dims[2] = {inner, outer};
-    const cuuint64_t strides[1] = {inner * 2};
-    const cuuint32_t box[2] = {64, box_outer};
-    const cuuint32_t es[2] = {1, 1};
-    const CUresult r = encode_tiled()(&m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                                      2, const_cast<void*>(base), dims, strides, box, es,
+    const cuuint64_t strides[1] = {pitch * es};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt = type == MapType::F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : type == MapType::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const CUresult r = encode_tiled()(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
@@ -92,12 +101,26 @@ static CUtensorMap make_map(const void* base, bool bf16, uint64_t inner, uint64_
     return m;
 }
 
+// A K-major 16-bit operand [rows, K] (tiles of 64 x box_rows).
+static CUtensorMap operand_map(const void* base, bool bf16, uint64_t K, uint64_t rows, uint32_t box_rows)
+{
+    return make_map(base, bf16 ? MapType::BF16 : MapType::F16, K, rows, K, 64, box_rows);
+}
+
+// The output (and, for the residual, the input) of a product: [M, N] with pitch ldc, 16-bit for the kEpiBias /
+// kEpiBiasGelu epilogues, f32 for kEpiResidual / kEpiF32; staging chunks of 128 rows x 128 bytes.
+static CUtensorMap output_map(void* base, int epi, bool bf16, int M, int N, int ldc)
+{
+    if (epi == kEpiResidual || epi == kEpiF32) return make_map(base, MapType::F32, N, M, ldc, 32, 128);
+    return make_map(base, bf16 ? MapType::BF16 : MapType::F16, N, M, ldc, 64, 128);
+}
+
 // ------------------------------------------------------------------------------------------------ launchers
 template <typename T, int BN, int EPI>
-static void launch_gemm_bn(const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K, const float* bias,
-                           void* out, int ldc, uint32_t* err, int num_sms, cudaStream_t s)
+static void launch_gemm_bn(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M, int N, int K,
+                           const float* bias, uint32_t* err, int num_sms, cudaStream_t s)
 {
-    using C = GemmCfg<BN>;
+    using C = GemmCfg<BN, EPI>;
     // the shared-memory opt-in, once per instantiation and device (the first launch of a batch size is eager,
     // never inside a graph capture)
     static bool attr[64] = {};
@@ -111,23 +134,19 @@ static void launch_gemm_bn(const CUtensorMap& ma, const CUtensorMap& mb, int M, 
     }
     const int tiles = ((M + C::BM - 1) / C::BM) * ((N + BN - 1) / BN);
     const int grid = std::min(tiles, num_sms);
-    gemm_tc_kernel<T, BN, EPI><<<grid, C::THREADS, C::SMEM, s>>>(ma, mb, M, N, K, bias, out, ldc, err);
+    gemm_tc_kernel<T, BN, EPI><<<grid, C::THREADS, C::SMEM, s>>>(ma, mb, mc, M, N, K, bias, err);
     RT(cudaGetLastError());
 }
 
 template <typename T, int BN>
-static void launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K,
-                            const float* bias, void* out, int ldc, uint32_t* err, int num_sms, cudaStream_t s)
+static void launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
+                            int N, int K, const float* bias, uint32_t* err, int num_sms, cudaStream_t s)
 {
     switch (epi) {
-        case kEpiBias: launch_gemm_bn<T, BN, kEpiBias>(ma, mb, M, N, K, bias, out, ldc, err, num_sms, s); break;
-        case kEpiBiasGelu:
-            launch_gemm_bn<T, BN, kEpiBiasGelu>(ma, mb, M, N, K, bias, out, ldc, err, num_sms, s);
-            break;
-        case kEpiResidual:
-            launch_gemm_bn<T, BN, kEpiResidual>(ma, mb, M, N, K, bias, out, ldc, err, num_sms, s);
-            break;
-        case kEpiF32: launch_gemm_bn<T, BN, kEpiF32>(ma, mb, M, N, K, bias, out, ldc, err, num_sms, s); break;
+        case kEpiBias: launch_gemm_bn<T, BN, kEpiBias>(ma, mb, mc, M, N, K, bias, err, num_sms, s); break;
+        case kEpiBiasGelu: launch_gemm_bn<T, BN, kEpiBiasGelu>(ma, mb, mc, M, N, K, bias, err, num_sms, s); break;
+        case kEpiResidual: launch_gemm_bn<T, BN, kEpiResidual>(ma, mb, mc, M, N, K, bias, err, num_sms, s); break;
+        case kEpiF32: launch_gemm_bn<T, BN, kEpiF32>(ma, mb, mc, M, N, K, bias, err, num_sms, s); break;
         default: throw std::runtime_error("cudanet_b200: unknown epilogue");
     }
 }
@@ -142,13 +161,15 @@ static int pick_bn(int M, int N, int num_sms)
 }
 
 template <typename T>
-static void launch_gemm(int epi, int bn, const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K,
-                        const float* bias, void* out, int ldc, uint32_t* err, int num_sms, cudaStream_t s)
+static void launch_gemm(int epi, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
+                        int N, int K, const float* bias, uint32_t* err, int num_sms, cudaStream_t s)
 {
     if (K % 64 || K <= 0) throw std::runtime_error("cudanet_b200: GEMM K must be a positive multiple of 64");
-    if (bn == 256) launch_gemm_epi<T, 256>(epi, ma, mb, M, N, K, bias, out, ldc, err, num_sms, s);
-    else if (bn == 128) launch_gemm_epi<T, 128>(epi, ma, mb, M, N, K, bias, out, ldc, err, num_sms, s);
-    else if (bn == 64) launch_gemm_epi<T, 64>(epi, ma, mb, M, N, K, bias, out, ldc, err, num_sms, s);
+    if (M < 1 || N < 1) throw std::runtime_error("cudanet_b200: GEMM with an empty output");
+    if (reinterpret_cast<uintptr_t>(bias) & 15) throw std::runtime_error("cudanet_b200: bias not 16-byte aligned");
+    if (bn == 256) launch_gemm_epi<T, 256>(epi, ma, mb, mc, M, N, K, bias, err, num_sms, s);
+    else if (bn == 128) launch_gemm_epi<T, 128>(epi, ma, mb, mc, M, N, K, bias, err, num_sms, s);
+    else if (bn == 64) launch_gemm_epi<T, 64>(epi, ma, mb, mc, M, N, K, bias, err, num_sms, s);
     else throw std::runtime_error("cudanet_b200: tile width must be 64, 128 or 256");
 }
 
@@ -414,6 +435,7 @@ private:
     bool use_graph_ = true;
     CUtensorMap map_h_, map_att_, map_ff_, map_cls_;
     std::map<std::pair<const void*, int>, CUtensorMap> wmaps_;
+    std::map<std::tuple<const void*, int, int, int>, CUtensorMap> omaps_;   // (out, epi, M, N)
 
     struct Fly {
         int B, wide, slot;
@@ -529,10 +551,10 @@ void Net::init(const std::string& path, int device)
         }
         RT(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
         const bool b = bf16();
-        map_h_ = make_map(h_, b, d, rows_pad_, 128);
-        map_att_ = make_map(att_, b, d, rows_pad_, 128);
-        map_ff_ = make_map(ff_, b, ff, rows_pad_, 128);
-        map_cls_ = make_map(cls_, b, d, cls_pad_, 128);
+        map_h_ = operand_map(h_, b, d, rows_pad_, 128);
+        map_att_ = operand_map(att_, b, d, rows_pad_, 128);
+        map_ff_ = operand_map(ff_, b, ff, rows_pad_, 128);
+        map_cls_ = operand_map(cls_, b, d, cls_pad_, 128);
         const char* g = std::getenv("MAYFLY_CUDANET_GRAPH");
         use_graph_ = !(g && std::strcmp(g, "0") == 0);
         RT(cudaStreamSynchronize(stream_));
@@ -575,8 +597,8 @@ const CUtensorMap& Net::wmap(const void* W, int N, int K, int bn)
     const auto key = std::make_pair(W, bn);
     auto it = wmaps_.find(key);
     if (it != wmaps_.end()) return it->second;
-    return wmaps_[key] = make_map(W, bf16(), static_cast<uint64_t>(K), static_cast<uint64_t>(N),
-                                  static_cast<uint32_t>(bn));
+    return wmaps_[key] = operand_map(W, bf16(), static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                                     static_cast<uint32_t>(bn));
 }
 
 void Net::gemm(int epi, const CUtensorMap& ma, const void* W, int M, int N, int K, const float* bias, void* out,
@@ -584,10 +606,13 @@ void Net::gemm(int epi, const CUtensorMap& ma, const void* W, int M, int N, int 
 {
     const int bn = pick_bn(M, N, num_sms_);
     const CUtensorMap& mb = wmap(W, N, K, bn);
+    const auto okey = std::make_tuple(static_cast<const void*>(out), epi, M, N);
+    auto it = omaps_.find(okey);
+    if (it == omaps_.end()) it = omaps_.emplace(okey, output_map(out, epi, bf16(), M, N, ldc)).first;
     if (bf16())
-        launch_gemm<__nv_bfloat16>(epi, bn, ma, mb, M, N, K, bias, out, ldc, err_word(), num_sms_, s);
+        launch_gemm<__nv_bfloat16>(epi, bn, ma, mb, it->second, M, N, K, bias, err_word(), num_sms_, s);
     else
-        launch_gemm<__half>(epi, bn, ma, mb, M, N, K, bias, out, ldc, err_word(), num_sms_, s);
+        launch_gemm<__half>(epi, bn, ma, mb, it->second, M, N, K, bias, err_word(), num_sms_, s);
 }
 
 void Net::mark(int op, cudaStream_t s)
@@ -1056,18 +1081,23 @@ CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const 
         if (bn == 0) bn = mf::pick_bn(M, N, sms);
         if ((reinterpret_cast<uintptr_t>(C) | reinterpret_cast<uintptr_t>(bias)) & 15)
             throw std::runtime_error("cudanet_k_gemm: C and bias must be 16-byte aligned");
+        const long long ob = (epi == 2 || epi == 3) ? 4 : 2;
+        if ((ldc * ob) % 16 || (N * ob) % 16)
+            throw std::runtime_error("cudanet_k_gemm: C's rows and row pitch must be multiples of 16 bytes");
         if (ldc < N) throw std::runtime_error("cudanet_k_gemm: ldc < N");
         const bool b16 = dtype == 1;
-        const CUtensorMap ma = mf::make_map(A, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
-        const CUtensorMap mb = mf::make_map(W, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
-                                            static_cast<uint32_t>(bn));
+        if (epi < 0 || epi > 3) throw std::runtime_error("cudanet_k_gemm: epi must be 0..3");
+        const CUtensorMap ma = mf::operand_map(A, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
+        const CUtensorMap mb = mf::operand_map(W, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                                               static_cast<uint32_t>(bn));
+        const CUtensorMap mc = mf::output_map(C, epi, b16, M, N, ldc);
         uint32_t* errw = nullptr;
         mf::RT(cudaMalloc(&errw, 4));
         mf::RT(cudaMemset(errw, 0, 4));
         const cudaStream_t s = static_cast<cudaStream_t>(stream);
         try {
-            if (b16) mf::launch_gemm<__nv_bfloat16>(epi, bn, ma, mb, M, N, K, bias, C, ldc, errw, sms, s);
-            else mf::launch_gemm<__half>(epi, bn, ma, mb, M, N, K, bias, C, ldc, errw, sms, s);
+            if (b16) mf::launch_gemm<__nv_bfloat16>(epi, bn, ma, mb, mc, M, N, K, bias, errw, sms, s);
+            else mf::launch_gemm<__half>(epi, bn, ma, mb, mc, M, N, K, bias, errw, sms, s);
             mf::RT(cudaStreamSynchronize(s));
         } catch (...) {
             cudaFree(errw);

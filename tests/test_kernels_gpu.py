@@ -29,21 +29,30 @@ def _ref_gemm(A, W, bias, epi, C0=None):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("epi", [0, 1, 2, 3])
 @pytest.mark.parametrize("M,N,K,bn", [(195, 1024, 1024, 0), (4160, 3072, 1024, 256), (1300, 1024, 2048, 128),
-                                      (65, 2048, 1024, 64), (300, 8324, 1024, 256), (128, 256, 64, 256)])
+                                      (65, 2048, 1024, 64), (300, 8328, 1024, 256), (300, 8324, 1024, 256),
+                                      (128, 256, 64, 256)])
 def test_gemm(k, dtype, epi, M, N, K, bn):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K + epi)
     A = torch.randn(M, K, device="cuda", generator=g).to(dtype)
     W = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(dtype)
     bias = torch.randn(N, device="cuda", generator=g) * 0.02
     if epi in (0, 1):
-        C = torch.full((M, N), float("nan"), device="cuda", dtype=dtype)
+        if N % 8:
+            pytest.skip("16-bit output rows must be whole 16-byte units (the heads' 8,324 columns are f32)")
+        # a padded pitch: the padding must never be written
+        Cfull = torch.full((M, N + 8), float("nan"), device="cuda", dtype=dtype)
+        C = Cfull[:, :N]
+    elif epi == 2:
+        C = torch.randn(M, N, device="cuda", generator=g)
     else:
-        C = torch.randn(M, N, device="cuda", generator=g) if epi == 2 else torch.full((M, N), float("nan"),
-                                                                                     device="cuda")
+        Cfull = torch.full((M, N + 4), float("nan"), device="cuda")
+        C = Cfull[:, :N]
     C0 = C.clone()
     k.k_gemm(A, W, bias, C, epi, bn)
     torch.cuda.synchronize()
     ref = _ref_gemm(A, W, bias, epi, C0.float())
+    if epi != 2:
+        assert torch.isnan(Cfull[:, N:]).all()
     # f32 accumulation of K products of 16-bit inputs (summation order differs from torch's: 1e-3 absolute),
     # and 16-bit outputs add one rounding of the result (half an ulp: 2^-9 relative for bf16, 2^-12 for f16)
     rel = 0.0 if epi in (2, 3) else (2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11)
