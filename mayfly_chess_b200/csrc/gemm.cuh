@@ -14,8 +14,9 @@
 //   warp 0      one thread issues TMA tile loads (128-byte swizzle) of A and W into a STAGES-deep ring
 //   warp 1      allocates tensor memory (2 accumulators of BN f32 columns); one thread issues tcgen05.mma
 //               (M=128, N=BN, K=16 per instruction) and tcgen05.commit to release ring stages / accumulators
-//   warps 2..5  epilogue, one output row per thread: tcgen05.ld of the accumulator (warp w reads TMEM lanes
-//               32*(w%4)..+31), bias / GELU / residual, then the row goes into a 128-row x 128-byte staging
+//   warps 2..   epilogue, 1 or 2 groups of 4 warps (GemmCfg::EG), one output row per thread per group:
+//               tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31; two groups split a tile's
+//               column chunks), bias / GELU / residual, then the row goes into a 128-row x 128-byte staging
 //               chunk in shared memory (128-byte swizzle) and one thread stores the chunk with a TMA tensor
 //               store (coalesced, asynchronous). For the residual the chunk of X is first TMA-loaded into the
 //               same staging buffer, several chunks ahead (also across tiles), so the read-modify-write of the
@@ -49,15 +50,20 @@ template <int BN, int EPI> struct GemmCfg {
     static constexpr int CHUNK_COLS = 128 / OUT_BYTES;   // one staging chunk: 128 rows x 128 bytes
     static constexpr int NC = BN / CHUNK_COLS;           // staging chunks per tile
     static constexpr uint32_t CHUNK_BYTES = 128 * 128;
-    static constexpr int NBUF = RESID ? 4 : 2;           // staging buffers
+    // Epilogue groups: 4 warps each, one per TMEM lane quarter. Two groups split a tile's chunks (even / odd)
+    // where the per-element work is heavy (GELU's erf) or the chunks are many; the residual's bulk traffic
+    // keeps one group with deeper prefetch.
+    static constexpr int EG = (!RESID && NC % 2 == 0) ? 2 : 1;
+    static constexpr int NBUF = RESID ? 4 : (EG == 2 ? 1 : 2);   // staging buffers per group
     static constexpr uint32_t A_BYTES = BM * BK * 2;
     static constexpr uint32_t B_BYTES = BN * BK * 2;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES_FIT = (224 * 1024 - NBUF * (int)CHUNK_BYTES) / (int)STAGE_BYTES;
+    static constexpr int STAGES_FIT = (224 * 1024 - EG * NBUF * (int)CHUNK_BYTES) / (int)STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (size_t)NBUF * CHUNK_BYTES + 256;
-    static constexpr int THREADS = 192;
+    static constexpr size_t SMEM =
+        1024 + (size_t)STAGES * STAGE_BYTES + (size_t)EG * NBUF * CHUNK_BYTES + 256;
+    static constexpr int THREADS = 64 + 128 * EG;
     static_assert(STAGES >= 3, "pipeline too shallow");
     static_assert(SMEM <= 232448, "shared memory over the per-block limit");
     static_assert(BN % CHUNK_COLS == 0, "tile width must hold whole staging chunks");
@@ -107,7 +113,7 @@ __device__ __forceinline__ void add_bias32(float (&v)[NV], int off, const float*
 __device__ __forceinline__ uint32_t swz(int r, int j) { return (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)); }
 
 template <typename T, int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, int M, int N, int K, const float* __restrict__ bias,
                uint32_t* err)
@@ -117,15 +123,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-    uint8_t* sC = sB + C::STAGES * C::B_BYTES;                        // NBUF staging chunks
-    uint64_t* full = reinterpret_cast<uint64_t*>(sC + C::NBUF * C::CHUNK_BYTES);
+    uint8_t* sC = sB + C::STAGES * C::B_BYTES;                        // EG x NBUF staging chunks
+    uint64_t* full = reinterpret_cast<uint64_t*>(sC + C::EG * C::NBUF * C::CHUNK_BYTES);
     uint64_t* empty = full + C::STAGES;
     uint64_t* tfull = empty + C::STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* mma_done = tempty + 2;
     uint64_t* xfull = mma_done + 1;                                    // NBUF (residual loads)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + C::NBUF);
-    volatile uint32_t* epi_ok = tmem_slot + 1;                         // the epilogue's broadcast flag
+    volatile uint32_t* epi_ok = tmem_slot + 1;                         // per group: the leader's broadcast flag
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m_tiles = (M + C::BM - 1) / C::BM;
@@ -140,7 +146,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 4);
+            mbar_init(&tempty[b], 4 * C::EG);
         }
         mbar_init(mma_done, 1);
         for (int b = 0; b < C::NBUF; ++b) mbar_init(&xfull[b], 1);
@@ -230,18 +236,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_wait(mma_done, 0, err, kErrTmemFull);
         }
     } else if (k_iters > 0) {
-        // ---------------------------------------------------------------- epilogue (warps 2..5)
+        // ---------------------------------------------------------------- epilogue (warps 2 .. 2 + 4*EG - 1)
+        const int grp = (warp - 2) >> 2;                      // epilogue group: chunks grp, grp + EG, ...
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;                  // row of the tile this thread owns
-        const bool leader = threadIdx.x == 64;                // issues the epilogue's TMA traffic
+        const bool leader = threadIdx.x == 64 + 128 * grp;    // issues the group's TMA traffic
+        const uint32_t bar_id = 1 + grp;
+        constexpr int CPG = C::NC / C::EG;                    // chunks per tile for one group
         const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
         const int my_tiles = (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-        const int total_chunks = my_tiles * C::NC;
+        const int total_chunks = my_tiles * CPG;              // this group's chunks over all its tiles
+        uint8_t* gbuf = sC + grp * C::NBUF * C::CHUNK_BYTES;
 
-        // chunk h of this CTA: tile blockIdx.x + (h / NC) * gridDim.x, columns (h % NC) * CHUNK_COLS
+        // this group's chunk h: tile blockIdx.x + (h / CPG) * gridDim.x, chunk grp + (h % CPG) * EG of it
         auto chunk_xy = [&](int h, int& x, int& y) {
-            const int tile = (int)blockIdx.x + (h / C::NC) * (int)gridDim.x;
-            x = (tile % n_tiles) * BN + (h % C::NC) * C::CHUNK_COLS;
+            const int tile = (int)blockIdx.x + (h / CPG) * (int)gridDim.x;
+            x = (tile % n_tiles) * BN + (grp + (h % CPG) * C::EG) * C::CHUNK_COLS;
             y = (tile / n_tiles) * C::BM;
         };
         int loads = 0;    // residual chunks whose load the leader issued
@@ -251,25 +261,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     int x, y;
                     chunk_xy(loads, x, y);
                     mbar_arrive_expect_tx(&xfull[loads], C::CHUNK_BYTES);
-                    tma_load_2d(sC + loads * C::CHUNK_BYTES, &tmC, &xfull[loads], x, y);
+                    tma_load_2d(gbuf + loads * C::CHUNK_BYTES, &tmC, &xfull[loads], x, y);
                 }
         }
 
         int acc = 0;
         uint32_t acc_phase = 0;
         bool ok = true;
-        int g = 0;        // chunks done
+        int g = 0;        // this group's chunks done
         for (int it = 0; it < my_tiles && ok; ++it) {
             const int tile = (int)blockIdx.x + it * (int)gridDim.x;
             const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
-            if (leader) *epi_ok = mbar_wait(&tfull[acc], acc_phase, err, kErrTmemFull) ? 1u : 0u;
-            named_barrier(1, 128);
-            if (!*epi_ok) break;
+            if (leader) epi_ok[grp] = mbar_wait(&tfull[acc], acc_phase, err, kErrTmemFull) ? 1u : 0u;
+            named_barrier(bar_id, 128);
+            if (!epi_ok[grp]) break;
             tc_fence_after();
             const uint32_t t_acc = t_lane + static_cast<uint32_t>(acc * BN);
-            for (int c = 0; c < C::NC; ++c, ++g) {
+            for (int ci = 0; ci < CPG; ++ci, ++g) {
+                const int c = grp + ci * C::EG;
                 const int b = g % C::NBUF;
-                uint8_t* buf = sC + b * C::CHUNK_BYTES;
+                uint8_t* buf = gbuf + b * C::CHUNK_BYTES;
                 const int col0 = n_blk * BN + c * C::CHUNK_COLS;
                 // the accumulator columns of this chunk (one or two 32-column loads)
                 float v[C::CHUNK_COLS];
@@ -286,8 +297,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
                     }
                 }
-                if (c == C::NC - 1) {
-                    // the accumulator is drained: hand it back to the MMA warp
+                if (ci == CPG - 1) {
+                    // this warp is done with the accumulator: hand it back to the MMA warp (all 4*EG warps)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -300,12 +311,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
                 // the staging buffer must be ready: loaded (residual) or no longer read by its last store
                 if constexpr (C::RESID) {
-                    if (leader) *epi_ok = mbar_wait(&xfull[b], (g / C::NBUF) & 1u, err, kErrTmaFull) ? 1u : 0u;
+                    if (leader) epi_ok[grp] = mbar_wait(&xfull[b], (g / C::NBUF) & 1u, err, kErrTmaFull) ? 1u : 0u;
                 } else {
                     if (leader) bulk_wait_read<C::NBUF - 1>();
                 }
-                named_barrier(1, 128);
-                if (!*epi_ok) {
+                named_barrier(bar_id, 128);
+                if (!epi_ok[grp]) {
                     ok = false;
                     break;
                 }
@@ -337,7 +348,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     }
                 }
                 fence_proxy_async_smem();
-                named_barrier(1, 128);
+                named_barrier(bar_id, 128);
                 if (leader) {
                     tma_store_2d(&tmC, buf, col0, m_blk * C::BM);
                     bulk_commit();
@@ -350,7 +361,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                             int x, y;
                             chunk_xy(next, x, y);
                             mbar_arrive_expect_tx(&xfull[nb], C::CHUNK_BYTES);
-                            tma_load_2d(sC + nb * C::CHUNK_BYTES, &tmC, &xfull[nb], x, y);
+                            tma_load_2d(gbuf + nb * C::CHUNK_BYTES, &tmC, &xfull[nb], x, y);
                             loads = next + 1;
                         }
                     }
