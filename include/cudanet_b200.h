@@ -107,6 +107,17 @@ CUDANET_API int cudanet_check(void* handle, void* stream, char* err, int err_len
 CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const void* W, const float* bias,
                                void* C, int M, int N, int K, int ldc, void* stream, char* err, int err_len);
 
+/* The same product as cudanet_k_gemm, for callers that cannot call cudaMalloc (a process whose GPU memory is
+ * all reserved up front, or a search thread that must not take the device-wide synchronisation an allocation
+ * costs while other batches are in flight). No counterpart in the reference. It allocates nothing: its only
+ * scratch, the kernel's 4-byte error word, lives in a static 256-byte device array that every GPU loading the
+ * library holds until exit. The first call on a device looks up that array's address (cudaGetSymbolAddress);
+ * make that first call before any stream capture. Calls share the array and it keeps the last call's word
+ * (each call clears it first), so calls that overlap on the GPU race on it. Any M, N, K that cudanet_k_gemm
+ * takes fits: the scratch need does not grow with the product. */
+CUDANET_API int cudanet_k_gemm_noalloc(int dtype, int epi, int bn, const void* A, const void* W, const float* bias,
+                                       void* C, int M, int N, int K, int ldc, void* stream, char* err, int err_len);
+
 /* att[rows, d] = per (board, head) softmax(q k^T / sqrt(d/heads)) v over the 65 tokens of each board, qkv
  * [B*65, 3d]. */
 CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,

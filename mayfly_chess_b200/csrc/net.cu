@@ -914,6 +914,36 @@ template <typename F> static int guarded(char* err, int err_len, const char* wha
     return -1;
 }
 
+// ------------------------------------------------------------------------------------------------ no-alloc product
+// Some callers cannot call cudaMalloc at all: a search thread that has reserved the whole GPU memory budget up
+// front, or code that must not take the implicit device-wide synchronisation a cudaMalloc/cudaFree pair costs
+// while other batches are in flight. cudanet_k_gemm allocates its device error word on every call, so they
+// cannot use it. cudanet_k_gemm_noalloc runs the same product with that scratch in this file-scope array
+// instead: 256 bytes on every GPU that loads the library, held until the process exits. A call uses the first
+// 4-byte word (the kernel's bounded-wait error report), whatever M, N and K are.
+constexpr size_t kNoAllocScratchBytes = 256;
+constexpr size_t kNoAllocBytesPerCall = sizeof(uint32_t);
+static __device__ __align__(256) uint32_t g_noalloc_scratch[kNoAllocScratchBytes / sizeof(uint32_t)];
+
+// The array's device address on the current device, looked up once per device (host code must not hand the
+// symbol itself to a kernel: on the host it is only a stand-in for the device copy).
+static uint32_t* noalloc_scratch(int dev)
+{
+    static std::mutex mu;
+    static uint32_t* addr[64] = {};
+    if (dev < 0 || dev >= 64) throw std::runtime_error("cudanet_k_gemm_noalloc: device index out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            throw std::runtime_error(std::string("cudanet_k_gemm_noalloc: cudaGetSymbolAddress failed: ") +
+                                     cudaGetErrorString(e));
+        addr[dev] = static_cast<uint32_t*>(p);
+    }
+    return addr[dev];
+}
+
 }  // namespace mf
 
 using mf::Net;
@@ -1107,6 +1137,47 @@ CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const 
         mf::RT(cudaMemcpy(&e, errw, 4, cudaMemcpyDeviceToHost));
         cudaFree(errw);
         if (e) throw std::runtime_error(std::string("cudanet_k_gemm: device error: ") + mf::err_site_name(e >> 8));
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_k_gemm_noalloc(int dtype, int epi, int bn, const void* A, const void* W, const float* bias,
+                                       void* C, int M, int N, int K, int ldc, void* stream, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_k_gemm_noalloc: unknown exception", [&] {
+        if (dtype != 0 && dtype != 1)
+            throw std::runtime_error("cudanet_k_gemm_noalloc: dtype must be 0 (f16) or 1 (bf16)");
+        if (M < 1 || N < 1 || K < 64) throw std::runtime_error("cudanet_k_gemm_noalloc: bad sizes");
+        if (epi < 0 || epi > 3) throw std::runtime_error("cudanet_k_gemm_noalloc: epi must be 0..3");
+        if (mf::kNoAllocBytesPerCall > mf::kNoAllocScratchBytes)
+            throw std::runtime_error("cudanet_k_gemm_noalloc: the call needs more scratch than the static " +
+                                     std::to_string(mf::kNoAllocScratchBytes) + " bytes");
+        int dev = 0;
+        mf::RT(cudaGetDevice(&dev));
+        uint32_t* errw = mf::noalloc_scratch(dev);   // the first call on a device looks the address up
+        int sms = 0;
+        mf::RT(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        if (bn == 0) bn = mf::pick_bn(M, N, sms);
+        if ((reinterpret_cast<uintptr_t>(C) | reinterpret_cast<uintptr_t>(bias)) & 15)
+            throw std::runtime_error("cudanet_k_gemm_noalloc: C and bias must be 16-byte aligned");
+        const long long ob = (epi == 2 || epi == 3) ? 4 : 2;
+        if ((ldc * ob) % 16 || (N * ob) % 16)
+            throw std::runtime_error("cudanet_k_gemm_noalloc: C's rows and row pitch must be multiples of 16 bytes");
+        const bool b16 = dtype == 1;
+        const CUtensorMap ma = mf::operand_map(A, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
+        const CUtensorMap mb = mf::operand_map(W, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                                               static_cast<uint32_t>(bn));
+        const CUtensorMap mc = mf::output_map(C, epi, b16, M, N, ldc);
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        // the word keeps the last call's value: clear it for this call, in stream order
+        mf::RT(cudaMemsetAsync(errw, 0, mf::kNoAllocBytesPerCall, s));
+        if (b16) mf::launch_gemm<__nv_bfloat16>(epi, bn, ma, mb, mc, M, N, K, bias, errw, sms, s);
+        else mf::launch_gemm<__half>(epi, bn, ma, mb, mc, M, N, K, bias, errw, sms, s);
+        uint32_t e = 0;
+        mf::RT(cudaMemcpyAsync(&e, errw, sizeof e, cudaMemcpyDeviceToHost, s));
+        mf::RT(cudaStreamSynchronize(s));
+        if (e)
+            throw std::runtime_error(std::string("cudanet_k_gemm_noalloc: device error: ") + mf::err_site_name(e >> 8));
         return 0;
     });
 }

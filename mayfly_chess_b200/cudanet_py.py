@@ -76,6 +76,8 @@ def load(dll=None):
         lib.cudanet_check.restype = i32
         lib.cudanet_k_gemm.argtypes = [i32, i32, i32, vp, vp, vp, vp, i32, i32, i32, i32, vp, cp, i32]
         lib.cudanet_k_gemm.restype = i32
+        lib.cudanet_k_gemm_noalloc.argtypes = [i32, i32, i32, vp, vp, vp, vp, i32, i32, i32, i32, vp, cp, i32]
+        lib.cudanet_k_gemm_noalloc.restype = i32
         lib.cudanet_k_attention.argtypes = [i32, vp, vp, i32, i32, i32, vp, cp, i32]
         lib.cudanet_k_attention.restype = i32
         lib.cudanet_k_layernorm.argtypes = [i32, vp, vp, vp, vp, i32, i32, i32, vp, cp, i32]
@@ -297,6 +299,21 @@ def k_gemm(A, W, bias, C, epi, bn=0, dll=None):
                             C.data_ptr(), M, N, K, C.stride(0), _stream(), err, ERR_LEN)
     if rc != 0:
         raise RuntimeError(f"cudanet_k_gemm: {_msg(err)}")
+    return C
+
+
+def k_gemm_noalloc(A, W, bias, C, epi, bn=0, dll=None):
+    """k_gemm without any device allocation: for callers that cannot call cudaMalloc (their GPU memory is
+    reserved up front, or they must not stall in-flight work on an allocation). Its scratch is a static device
+    array shared by every call; calls that overlap on the GPU race on it."""
+    lib = load(dll)
+    M, K = A.shape
+    N = W.shape[0]
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_k_gemm_noalloc(_dtype_code(A), int(epi), int(bn), A.data_ptr(), W.data_ptr(), bias.data_ptr(),
+                                    C.data_ptr(), M, N, K, C.stride(0), _stream(), err, ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_k_gemm_noalloc: {_msg(err)}")
     return C
 
 
