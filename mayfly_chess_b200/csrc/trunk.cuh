@@ -218,18 +218,24 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const T* __re
     const size_t row0 = (size_t)b * kTokens;
     const size_t ld = 3 * (size_t)d;
 
-    // stage Q, K, V (rows 65..79 zero)
-    for (int i = tid; i < kAttRows * CH * 3; i += blockDim.x) {
-        const int which = i / (kAttRows * CH);
-        const int rem = i % (kAttRows * CH);
+    // stage Q, K, V: every 16-byte piece of the 65 live rows is an asynchronous copy (all in flight at once),
+    // rows 65..79 are zero
+    constexpr int LIVE = kTokens * CH * 3;
+    for (int i = tid; i < LIVE; i += kAttWarps * 32) {
+        const int which = i / (kTokens * CH);
+        const int rem = i % (kTokens * CH);
         const int r = rem / CH, c = rem % CH;
         T* dst = (which == 0 ? sQ : which == 1 ? sK : sV) + r * P + c * 8;
-        uint4 val = make_uint4(0, 0, 0, 0);
-        if (r < kTokens)
-            val = __ldg(reinterpret_cast<const uint4*>(qkv + (row0 + r) * ld + (size_t)which * d +
-                                                       (size_t)head * DH) + c);
-        *reinterpret_cast<uint4*>(dst) = val;
+        const T* src = qkv + (row0 + r) * ld + (size_t)which * d + (size_t)head * DH + c * 8;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
     }
+    for (int i = tid; i < (kAttRows - kTokens) * CH * 3; i += kAttWarps * 32) {
+        const int which = i / ((kAttRows - kTokens) * CH);
+        const int rem = i % ((kAttRows - kTokens) * CH);
+        const int r = kTokens + rem / CH, c = rem % CH;
+        *reinterpret_cast<uint4*>((which == 0 ? sQ : which == 1 ? sK : sV) + r * P + c * 8) = make_uint4(0, 0, 0, 0);
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     __syncthreads();
 
     const int g = lane >> 2, t = lane & 3;
