@@ -103,7 +103,7 @@ CUDANET_API int cudanet_check(void* handle, void* stream, char* err, int err_len
 /* C = A[M, K] * W[N, K]^T + epilogue, with epi 0: C 16-bit = acc + bias; 1: C 16-bit = gelu(acc + bias);
  * 2: C f32 += acc + bias; 3: C f32 = acc + bias. C has leading dimension ldc (elements); C's row length and
  * pitch in bytes must be multiples of 16. K must be a multiple of 64 and A's, W's row pitch K elements. bn 0
- * picks the tile width, else 64, 128 or 256. */
+ * picks the tile, 64, 128 or 256 ask for single-CTA tiles of that width, 2 for CTA-pair 256 x 256 tiles. */
 CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const void* W, const float* bias,
                                void* C, int M, int N, int K, int ldc, void* stream, char* err, int err_len);
 

@@ -10,10 +10,16 @@
 //   kEpiResidual  X (f32)   = X + (acc + bias), in place             out and ff2 (gemm.h F32_BIAS_RESIDUAL)
 //   kEpiF32       C (f32)   = acc + bias                             heads
 //
-// Design (one CTA per SM, persistent over output tiles of 128 x BN):
+// Two kernels, both persistent over output tiles with one CTA per SM:
+//   gemm_tc_kernel       one CTA per 128 x BN tile (BN 64, 128 or 256): tcgen05.mma.cta_group::1, M=128.
+//   gemm_tc_pair_kernel  a cluster of 2 CTAs per 256 x 256 tile: tcgen05.mma.cta_group::2, M=256, issued by the
+//                        leader CTA. Each CTA loads its 128 rows of A and 128 of the 256 rows of W, so a CTA moves
+//                        a third less operand data per FLOP than with 128 x 256 alone, and a 32 KB stage buys a
+//                        deeper ring. Each CTA holds and drains its own 128 rows of the accumulator.
+// Warp roles (both kernels):
 //   warp 0      one thread issues TMA tile loads (128-byte swizzle) of A and W into a STAGES-deep ring
-//   warp 1      allocates tensor memory (2 accumulators of BN f32 columns); one thread issues tcgen05.mma
-//               (M=128, N=BN, K=16 per instruction) and tcgen05.commit to release ring stages / accumulators
+//   warp 1      allocates tensor memory (2 accumulators of BN f32 columns); one thread (the leader CTA's, for a
+//               pair) issues the MMAs (K=16 each) and tcgen05.commit to release ring stages / accumulators
 //   warps 2..   epilogue, 1 or 2 groups of 4 warps (GemmCfg::EG), one output row per thread per group:
 //               tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31; two groups split a tile's
 //               column chunks), bias / GELU / residual, then the row goes into a 128-row x 128-byte staging
@@ -24,10 +30,12 @@
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1. Tiles run M-block-major (all
 // N blocks of an M block back to back), so an A block is read from HBM once and the weights stay in L2.
 // Out-of-range rows and columns (M and N tails) are zero-filled by TMA loads and clipped by TMA stores.
+// No load uses multicast.
 //
 // Every wait is bounded (ptx.cuh). Epilogue decisions are made by one thread and broadcast through shared
-// memory at a named barrier, so the four epilogue warps always take the same path and never strand one
-// another at a barrier.
+// memory at a named barrier, so the epilogue warps always take the same path and never strand one another at a
+// barrier. Before a CTA leaves, its own TMA loads have landed and the MMAs that write its tensor memory have
+// completed.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -42,9 +50,11 @@ template <typename T> struct Fmt;
 template <> struct Fmt<__half> { static constexpr uint32_t v = 0; };
 template <> struct Fmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
 
-template <int BN, int EPI> struct GemmCfg {
-    static constexpr int BM = 128;
+// PAIR: the CTA-pair kernel, where a CTA loads BN/2 rows of W per stage and a pair covers 256 rows of M.
+template <int BN, int EPI, bool PAIR = false> struct GemmCfg {
+    static constexpr int BM = 128;                      // rows of A and of the output per CTA
     static constexpr int BK = 64;                       // 64 x 16-bit = one 128-byte swizzle row
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;   // rows of W per CTA per stage
     static constexpr bool RESID = EPI == kEpiResidual;
     static constexpr int OUT_BYTES = (EPI == kEpiResidual || EPI == kEpiF32) ? 4 : 2;
     static constexpr int CHUNK_COLS = 128 / OUT_BYTES;   // one staging chunk: 128 rows x 128 bytes
@@ -56,7 +66,7 @@ template <int BN, int EPI> struct GemmCfg {
     static constexpr int EG = (!RESID && NC % 2 == 0) ? 2 : 1;
     static constexpr int NBUF = RESID ? 4 : (EG == 2 ? 1 : 2);   // staging buffers per group
     static constexpr uint32_t A_BYTES = BM * BK * 2;
-    static constexpr uint32_t B_BYTES = BN * BK * 2;
+    static constexpr uint32_t B_BYTES = B_ROWS * BK * 2;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES_FIT = (224 * 1024 - EG * NBUF * (int)CHUNK_BYTES) / (int)STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
@@ -67,6 +77,7 @@ template <int BN, int EPI> struct GemmCfg {
     static_assert(STAGES >= 3, "pipeline too shallow");
     static_assert(SMEM <= 232448, "shared memory over the per-block limit");
     static_assert(BN % CHUNK_COLS == 0, "tile width must hold whole staging chunks");
+    static_assert(!PAIR || BN == 256, "the pair kernel covers 256 columns");
 };
 
 __device__ __forceinline__ float gelu_erf(float x)
@@ -112,6 +123,179 @@ __device__ __forceinline__ void add_bias32(float (&v)[NV], int off, const float*
 // CU_TENSOR_MAP_SWIZZLE_128B reads and writes; the chunk base is 1024-byte aligned)
 __device__ __forceinline__ uint32_t swz(int r, int j) { return (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)); }
 
+// The shared-memory carve-up common to both kernels.
+template <typename C> struct SmemLayout {
+    uint8_t *sA, *sB, *sC;
+    uint64_t *full, *empty, *tfull, *tempty, *mma_done, *xfull;
+    uint32_t* tmem_slot;
+    volatile uint32_t* epi_ok;   // per epilogue group: the leader's broadcast flag
+
+    __device__ __forceinline__ explicit SmemLayout(uint8_t* smem_raw)
+    {
+        uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+        sA = smem;
+        sB = smem + C::STAGES * C::A_BYTES;
+        sC = sB + C::STAGES * C::B_BYTES;                                // EG x NBUF staging chunks
+        full = reinterpret_cast<uint64_t*>(sC + C::EG * C::NBUF * C::CHUNK_BYTES);
+        empty = full + C::STAGES;
+        tfull = empty + C::STAGES;
+        tempty = tfull + 2;
+        mma_done = tempty + 2;
+        xfull = mma_done + 1;                                              // NBUF (residual loads)
+        tmem_slot = reinterpret_cast<uint32_t*>(xfull + C::NBUF);
+        epi_ok = tmem_slot + 1;
+    }
+};
+
+// The epilogue warps' loop over this CTA's tiles (warps 2 .. 2 + 4*EG - 1). Tile `it` of this CTA has its
+// output origin at (origin_row(it), origin_col(it)); when a warp has read its last accumulator columns of a
+// tile it calls release(acc) on lane 0 (an arrive on the barrier the MMA thread waits on).
+template <typename T, int EPI, typename C, typename RowFn, typename ColFn, typename ReleaseFn>
+__device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUtensorMap* tmC, uint32_t tmem_base,
+                                              int my_tiles, RowFn origin_row, ColFn origin_col, ReleaseFn release,
+                                              const float* __restrict__ bias, int N, uint32_t* err)
+{
+    constexpr int BN = C::NC * C::CHUNK_COLS;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = (warp - 2) >> 2;                      // epilogue group: chunks grp, grp + EG, ...
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;                  // row of the tile this thread owns
+    const bool leader = threadIdx.x == 64 + 128 * grp;    // issues the group's TMA traffic
+    const uint32_t bar_id = 1 + grp;
+    constexpr int CPG = C::NC / C::EG;                    // chunks per tile for one group
+    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int total_chunks = my_tiles * CPG;              // this group's chunks over all its tiles
+    uint8_t* gbuf = L.sC + grp * C::NBUF * C::CHUNK_BYTES;
+
+    // this group's chunk h: tile h / CPG of this CTA, chunk grp + (h % CPG) * EG of it
+    auto chunk_xy = [&](int h, int& x, int& y) {
+        x = origin_col(h / CPG) + (grp + (h % CPG) * C::EG) * C::CHUNK_COLS;
+        y = origin_row(h / CPG);
+    };
+    int loads = 0;    // residual chunks whose load the leader issued
+    if constexpr (C::RESID) {
+        if (leader)
+            for (; loads < C::NBUF && loads < total_chunks; ++loads) {
+                int x, y;
+                chunk_xy(loads, x, y);
+                mbar_arrive_expect_tx(&L.xfull[loads], C::CHUNK_BYTES);
+                tma_load_2d(gbuf + loads * C::CHUNK_BYTES, tmC, &L.xfull[loads], x, y);
+            }
+    }
+
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    int g = 0;        // this group's chunks done
+    for (int it = 0; it < my_tiles && ok; ++it) {
+        const int row0 = origin_row(it), colb = origin_col(it);
+        if (leader) L.epi_ok[grp] = mbar_wait(&L.tfull[acc], acc_phase, err, kErrTmemFull) ? 1u : 0u;
+        named_barrier(bar_id, 128);
+        if (!L.epi_ok[grp]) break;
+        tc_fence_after();
+        const uint32_t t_acc = t_lane + static_cast<uint32_t>(acc * BN);
+        for (int ci = 0; ci < CPG; ++ci, ++g) {
+            const int c = grp + ci * C::EG;
+            const int b = g % C::NBUF;
+            uint8_t* buf = gbuf + b * C::CHUNK_BYTES;
+            const int col0 = colb + c * C::CHUNK_COLS;
+            // the accumulator columns of this chunk (one or two 32-column loads)
+            float v[C::CHUNK_COLS];
+            {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * C::CHUNK_COLS), r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                if constexpr (C::CHUNK_COLS == 64) {
+                    tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * C::CHUNK_COLS + 32), r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
+                }
+            }
+            if (ci == CPG - 1) {
+                // this warp is done with the accumulator: hand it back to the MMA thread
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) release(acc);
+            }
+            add_bias32<C::CHUNK_COLS>(v, 0, bias, col0, N);
+            if constexpr (C::CHUNK_COLS == 64) add_bias32<C::CHUNK_COLS>(v, 32, bias, col0 + 32, N);
+            if constexpr (EPI == kEpiBiasGelu) {
+#pragma unroll
+                for (int i = 0; i < C::CHUNK_COLS; ++i) v[i] = gelu_erf(v[i]);
+            }
+            // the staging buffer must be ready: loaded (residual) or no longer read by its last store
+            if constexpr (C::RESID) {
+                if (leader) L.epi_ok[grp] = mbar_wait(&L.xfull[b], (g / C::NBUF) & 1u, err, kErrTmaFull) ? 1u : 0u;
+            } else {
+                if (leader) bulk_wait_read<C::NBUF - 1>();
+            }
+            named_barrier(bar_id, 128);
+            if (!L.epi_ok[grp]) {
+                ok = false;
+                break;
+            }
+            if constexpr (C::RESID) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float4* p = reinterpret_cast<float4*>(buf + swz(row, j));
+                    float4 x = *p;
+                    x.x += v[4 * j + 0];
+                    x.y += v[4 * j + 1];
+                    x.z += v[4 * j + 2];
+                    x.w += v[4 * j + 3];
+                    *p = x;
+                }
+            } else if constexpr (C::OUT_BYTES == 4) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    *reinterpret_cast<float4*>(buf + swz(row, j)) =
+                        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    uint4 q;
+                    q.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
+                    q.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
+                    q.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
+                    q.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
+                    *reinterpret_cast<uint4*>(buf + swz(row, j)) = q;
+                }
+            }
+            fence_proxy_async_smem();
+            named_barrier(bar_id, 128);
+            if (leader) {
+                tma_store_2d(tmC, buf, col0, row0);
+                bulk_commit();
+                if constexpr (C::RESID) {
+                    // refill the previous chunk's buffer (its store has been read) NBUF chunks ahead
+                    const int next = g - 1 + C::NBUF;
+                    if (g >= 1 && next < total_chunks && next >= loads) {
+                        bulk_wait_read<1>();
+                        const int nb = next % C::NBUF;
+                        int x, y;
+                        chunk_xy(next, x, y);
+                        mbar_arrive_expect_tx(&L.xfull[nb], C::CHUNK_BYTES);
+                        tma_load_2d(gbuf + nb * C::CHUNK_BYTES, tmC, &L.xfull[nb], x, y);
+                        loads = next + 1;
+                    }
+                }
+            }
+        }
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+    }
+    if (leader) {
+        bulk_wait_all();
+        // residual loads issued but never consumed (only after a failure) land before the CTA leaves
+        if constexpr (C::RESID)
+            for (int h = g; h < loads; ++h) mbar_wait(&L.xfull[h % C::NBUF], (h / C::NBUF) & 1u, err, kErrTmaFull);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ one CTA
 template <typename T, int BN, int EPI>
 __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -120,18 +304,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 {
     using C = GemmCfg<BN, EPI>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;
-    uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-    uint8_t* sC = sB + C::STAGES * C::B_BYTES;                        // EG x NBUF staging chunks
-    uint64_t* full = reinterpret_cast<uint64_t*>(sC + C::EG * C::NBUF * C::CHUNK_BYTES);
-    uint64_t* empty = full + C::STAGES;
-    uint64_t* tfull = empty + C::STAGES;
-    uint64_t* tempty = tfull + 2;
-    uint64_t* mma_done = tempty + 2;
-    uint64_t* xfull = mma_done + 1;                                    // NBUF (residual loads)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + C::NBUF);
-    volatile uint32_t* epi_ok = tmem_slot + 1;                         // per group: the leader's broadcast flag
+    const SmemLayout<C> L(smem_raw);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m_tiles = (M + C::BM - 1) / C::BM;
@@ -141,28 +314,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&L.full[s], 1);
+            mbar_init(&L.empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 4 * C::EG);
+            mbar_init(&L.tfull[b], 1);
+            mbar_init(&L.tempty[b], 4 * C::EG);
         }
-        mbar_init(mma_done, 1);
-        for (int b = 0; b < C::NBUF; ++b) mbar_init(&xfull[b], 1);
+        mbar_init(L.mma_done, 1);
+        for (int b = 0; b < C::NBUF; ++b) mbar_init(&L.xfull[b], 1);
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
         tma_prefetch_desc(&tmC);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_alloc(L.tmem_slot, C::TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t tmem_base = *L.tmem_slot;
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
@@ -175,13 +348,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
                 const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
                 for (int kb = 0; kb < k_iters; ++kb) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, err, kErrSmemEmpty)) {
+                    if (!mbar_wait(&L.empty[stage], phase ^ 1u, err, kErrSmemEmpty)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-                    tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * C::BK, m_blk * C::BM);
-                    tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * C::BK, n_blk * BN);
+                    mbar_arrive_expect_tx(&L.full[stage], C::STAGE_BYTES);
+                    tma_load_2d(L.sA + stage * C::A_BYTES, &tmA, &L.full[stage], kb * C::BK, m_blk * C::BM);
+                    tma_load_2d(L.sB + stage * C::B_BYTES, &tmB, &L.full[stage], kb * C::BK, n_blk * BN);
                     issued |= 1u << stage;
                     issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
                     if (++stage == C::STAGES) {
@@ -193,7 +366,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // every copy this thread started has landed before the CTA can leave (immediate when the MMA warp
             // consumed them all; bounded when something upstream failed)
             for (int s = 0; s < C::STAGES; ++s)
-                if (issued & (1u << s)) mbar_wait(&full[s], (issued_par >> s) & 1u, err, kErrTmaFull);
+                if (issued & (1u << s)) mbar_wait(&L.full[s], (issued_par >> s) & 1u, err, kErrTmaFull);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
@@ -205,177 +378,44 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             uint32_t acc_phase = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err, kErrTmemEmpty)) break;
+                if (!mbar_wait(&L.tempty[acc], acc_phase ^ 1u, err, kErrTmemEmpty)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
                 for (int kb = 0; kb < k_iters; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, err, kErrTmaFull)) {
+                    if (!mbar_wait(&L.full[stage], phase, err, kErrTmaFull)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
-                    const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+                    const uint32_t a_addr = smem_u32(L.sA + stage * C::A_BYTES);
+                    const uint32_t b_addr = smem_u32(L.sB + stage * C::B_BYTES);
 #pragma unroll
                     for (int k = 0; k < C::BK / 16; ++k)
                         umma_f16(d_tmem, sdesc_sw128(a_addr + 32u * k), sdesc_sw128(b_addr + 32u * k), idesc,
                                  (kb | k) != 0 ? 1u : 0u);
-                    umma_commit(&empty[stage]);
+                    umma_commit(&L.empty[stage]);
                     if (++stage == C::STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
-                umma_commit(&tfull[acc]);
+                umma_commit(&L.tfull[acc]);
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1u;
             }
             // every MMA this thread issued has completed before tensor memory is freed
-            umma_commit(mma_done);
-            mbar_wait(mma_done, 0, err, kErrTmemFull);
+            umma_commit(L.mma_done);
+            mbar_wait(L.mma_done, 0, err, kErrTmemFull);
         }
     } else if (k_iters > 0) {
-        // ---------------------------------------------------------------- epilogue (warps 2 .. 2 + 4*EG - 1)
-        const int grp = (warp - 2) >> 2;                      // epilogue group: chunks grp, grp + EG, ...
-        const int quarter = warp & 3;
-        const int row = quarter * 32 + lane;                  // row of the tile this thread owns
-        const bool leader = threadIdx.x == 64 + 128 * grp;    // issues the group's TMA traffic
-        const uint32_t bar_id = 1 + grp;
-        constexpr int CPG = C::NC / C::EG;                    // chunks per tile for one group
-        const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-        const int my_tiles = (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-        const int total_chunks = my_tiles * CPG;              // this group's chunks over all its tiles
-        uint8_t* gbuf = sC + grp * C::NBUF * C::CHUNK_BYTES;
-
-        // this group's chunk h: tile blockIdx.x + (h / CPG) * gridDim.x, chunk grp + (h % CPG) * EG of it
-        auto chunk_xy = [&](int h, int& x, int& y) {
-            const int tile = (int)blockIdx.x + (h / CPG) * (int)gridDim.x;
-            x = (tile % n_tiles) * BN + (grp + (h % CPG) * C::EG) * C::CHUNK_COLS;
-            y = (tile / n_tiles) * C::BM;
-        };
-        int loads = 0;    // residual chunks whose load the leader issued
-        if constexpr (C::RESID) {
-            if (leader)
-                for (; loads < C::NBUF && loads < total_chunks; ++loads) {
-                    int x, y;
-                    chunk_xy(loads, x, y);
-                    mbar_arrive_expect_tx(&xfull[loads], C::CHUNK_BYTES);
-                    tma_load_2d(gbuf + loads * C::CHUNK_BYTES, &tmC, &xfull[loads], x, y);
-                }
-        }
-
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        bool ok = true;
-        int g = 0;        // this group's chunks done
-        for (int it = 0; it < my_tiles && ok; ++it) {
-            const int tile = (int)blockIdx.x + it * (int)gridDim.x;
-            const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
-            if (leader) epi_ok[grp] = mbar_wait(&tfull[acc], acc_phase, err, kErrTmemFull) ? 1u : 0u;
-            named_barrier(bar_id, 128);
-            if (!epi_ok[grp]) break;
-            tc_fence_after();
-            const uint32_t t_acc = t_lane + static_cast<uint32_t>(acc * BN);
-            for (int ci = 0; ci < CPG; ++ci, ++g) {
-                const int c = grp + ci * C::EG;
-                const int b = g % C::NBUF;
-                uint8_t* buf = gbuf + b * C::CHUNK_BYTES;
-                const int col0 = n_blk * BN + c * C::CHUNK_COLS;
-                // the accumulator columns of this chunk (one or two 32-column loads)
-                float v[C::CHUNK_COLS];
-                {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * C::CHUNK_COLS), r);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                    if constexpr (C::CHUNK_COLS == 64) {
-                        tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * C::CHUNK_COLS + 32), r);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
-                    }
-                }
-                if (ci == CPG - 1) {
-                    // this warp is done with the accumulator: hand it back to the MMA warp (all 4*EG warps)
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[acc]);
-                }
-                add_bias32<C::CHUNK_COLS>(v, 0, bias, col0, N);
-                if constexpr (C::CHUNK_COLS == 64) add_bias32<C::CHUNK_COLS>(v, 32, bias, col0 + 32, N);
-                if constexpr (EPI == kEpiBiasGelu) {
-#pragma unroll
-                    for (int i = 0; i < C::CHUNK_COLS; ++i) v[i] = gelu_erf(v[i]);
-                }
-                // the staging buffer must be ready: loaded (residual) or no longer read by its last store
-                if constexpr (C::RESID) {
-                    if (leader) epi_ok[grp] = mbar_wait(&xfull[b], (g / C::NBUF) & 1u, err, kErrTmaFull) ? 1u : 0u;
-                } else {
-                    if (leader) bulk_wait_read<C::NBUF - 1>();
-                }
-                named_barrier(bar_id, 128);
-                if (!epi_ok[grp]) {
-                    ok = false;
-                    break;
-                }
-                if constexpr (C::RESID) {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        float4* p = reinterpret_cast<float4*>(buf + swz(row, j));
-                        float4 x = *p;
-                        x.x += v[4 * j + 0];
-                        x.y += v[4 * j + 1];
-                        x.z += v[4 * j + 2];
-                        x.w += v[4 * j + 3];
-                        *p = x;
-                    }
-                } else if constexpr (C::OUT_BYTES == 4) {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        *reinterpret_cast<float4*>(buf + swz(row, j)) =
-                            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        uint4 q;
-                        q.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
-                        q.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
-                        q.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
-                        q.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
-                        *reinterpret_cast<uint4*>(buf + swz(row, j)) = q;
-                    }
-                }
-                fence_proxy_async_smem();
-                named_barrier(bar_id, 128);
-                if (leader) {
-                    tma_store_2d(&tmC, buf, col0, m_blk * C::BM);
-                    bulk_commit();
-                    if constexpr (C::RESID) {
-                        // refill the previous chunk's buffer (its store has been read) NBUF chunks ahead
-                        const int next = g - 1 + C::NBUF;
-                        if (g >= 1 && next < total_chunks && next >= loads) {
-                            bulk_wait_read<1>();
-                            const int nb = next % C::NBUF;
-                            int x, y;
-                            chunk_xy(next, x, y);
-                            mbar_arrive_expect_tx(&xfull[nb], C::CHUNK_BYTES);
-                            tma_load_2d(gbuf + nb * C::CHUNK_BYTES, &tmC, &xfull[nb], x, y);
-                            loads = next + 1;
-                        }
-                    }
-                }
-            }
-            acc ^= 1;
-            if (acc == 0) acc_phase ^= 1u;
-        }
-        if (leader) {
-            bulk_wait_all();
-            // residual loads issued but never consumed (only after a failure) land before the CTA leaves
-            if constexpr (C::RESID)
-                for (int h = g; h < loads; ++h) mbar_wait(&xfull[h % C::NBUF], (h / C::NBUF) & 1u, err, kErrTmaFull);
-        }
+        const int my_tiles =
+            (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        epilogue_loop<T, EPI, C>(
+            L, &tmC, tmem_base, my_tiles,
+            [&](int it) { return (((int)blockIdx.x + it * (int)gridDim.x) / n_tiles) * C::BM; },
+            [&](int it) { return (((int)blockIdx.x + it * (int)gridDim.x) % n_tiles) * BN; },
+            [&](int acc) { mbar_arrive(&L.tempty[acc]); }, bias, N, err);
     }
 
     __syncwarp();
@@ -383,6 +423,154 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// ------------------------------------------------------------------------------------------------ CTA pair
+// A cluster of two CTAs computes a 256 x 256 tile. Rank 0 (the leader) owns the ring's `full` barriers (both
+// CTAs' loads complete there), the accumulator's `tempty` barriers (both CTAs' epilogue warps arrive there) and
+// issues every MMA; each CTA's `empty` and `tfull` barriers are signalled by the leader's commits.
+template <typename T, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<256, EPI, true>::THREADS, 1)
+gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, int M, int N, int K, const float* __restrict__ bias,
+                    uint32_t* err)
+{
+    constexpr int BN = 256;
+    using C = GemmCfg<BN, EPI, true>;
+    extern __shared__ uint8_t smem_raw[];
+    const SmemLayout<C> L(smem_raw);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool lead = rank == 0;
+    const int pair = (int)blockIdx.x >> 1, num_pairs = (int)gridDim.x >> 1;
+    const int m_tiles = (M + 2 * C::BM - 1) / (2 * C::BM);
+    const int n_tiles = (N + BN - 1) / BN;
+    const int num_tiles = m_tiles * n_tiles;
+    const int k_iters = K / C::BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&L.full[s], 1);
+            mbar_init(&L.empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&L.tfull[b], 1);
+            mbar_init(&L.tempty[b], 2 * 4 * C::EG);   // the epilogue warps of both CTAs
+        }
+        mbar_init(L.mma_done, 1);
+        for (int b = 0; b < C::NBUF; ++b) mbar_init(&L.xfull[b], 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        tma_prefetch_desc(&tmC);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(L.tmem_slot, C::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();   // both CTAs' barriers exist before either signals the other's
+    tc_fence_after();
+    const uint32_t tmem_base = *L.tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer (both CTAs)
+        if (lane == 0 && k_iters > 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0, issued_par = 0;
+            bool ok = true;
+            for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+                const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
+                const int a_row = m_blk * 2 * C::BM + (int)rank * C::BM;
+                const int b_row = n_blk * BN + (int)rank * C::B_ROWS;
+                for (int kb = 0; kb < k_iters; ++kb) {
+                    if (!mbar_wait(&L.empty[stage], phase ^ 1u, err, kErrSmemEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    if (lead) mbar_arrive_expect_tx(&L.full[stage], 2 * C::STAGE_BYTES);
+                    const uint32_t full_lead = mapa_shared(smem_u32(&L.full[stage]), 0);
+                    tma_load_2d_pair(L.sA + stage * C::A_BYTES, &tmA, full_lead, kb * C::BK, a_row);
+                    tma_load_2d_pair(L.sB + stage * C::B_BYTES, &tmB, full_lead, kb * C::BK, b_row);
+                    issued |= 1u << stage;
+                    issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // this CTA's copies have landed before it can leave: the leader sees them on its `full` barriers;
+            // the other CTA learns it from its `empty` barriers (a stage is released only after both halves
+            // landed and were read)
+            for (int s = 0; s < C::STAGES; ++s)
+                if (issued & (1u << s)) {
+                    if (lead) mbar_wait(&L.full[s], (issued_par >> s) & 1u, err, kErrTmaFull);
+                    else mbar_wait(&L.empty[s], (issued_par >> s) & 1u, err, kErrSmemEmpty);
+                }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer (leader only)
+        if (lead && lane == 0 && k_iters > 0) {
+            constexpr uint32_t idesc = idesc_f16(Fmt<T>::v, 256, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+                if (!mbar_wait(&L.tempty[acc], acc_phase ^ 1u, err, kErrTmemEmpty)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < k_iters; ++kb) {
+                    if (!mbar_wait(&L.full[stage], phase, err, kErrTmaFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(L.sA + stage * C::A_BYTES);
+                    const uint32_t b_addr = smem_u32(L.sB + stage * C::B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < C::BK / 16; ++k)
+                        umma_f16_pair(d_tmem, sdesc_sw128(a_addr + 32u * k), sdesc_sw128(b_addr + 32u * k), idesc,
+                                      (kb | k) != 0 ? 1u : 0u);
+                    const uint32_t e = smem_u32(&L.empty[stage]);
+                    umma_commit_pair(e);                    // this CTA's stage
+                    umma_commit_pair(mapa_shared(e, 1));    // the other CTA's stage
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                const uint32_t tf = smem_u32(&L.tfull[acc]);
+                umma_commit_pair(tf);
+                umma_commit_pair(mapa_shared(tf, 1));
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            // every MMA issued has completed (both CTAs' tensor memory) before either frees it
+            umma_commit_pair(smem_u32(L.mma_done));
+            mbar_wait(L.mma_done, 0, err, kErrTmemFull);
+        }
+    } else if (k_iters > 0) {
+        const int my_tiles = pair < num_tiles ? (num_tiles - 1 - pair) / num_pairs + 1 : 0;
+        const uint32_t tempty_lead0 = mapa_shared(smem_u32(&L.tempty[0]), 0);
+        const uint32_t tempty_lead1 = mapa_shared(smem_u32(&L.tempty[1]), 0);
+        epilogue_loop<T, EPI, C>(
+            L, &tmC, tmem_base, my_tiles,
+            [&](int it) { return ((pair + it * num_pairs) / n_tiles) * 2 * C::BM + (int)rank * C::BM; },
+            [&](int it) { return ((pair + it * num_pairs) % n_tiles) * BN; },
+            [&](int acc) { mbar_arrive_cluster(acc ? tempty_lead1 : tempty_lead0); }, bias, N, err);
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();   // the leader's MMAs are done and no CTA signals the other any more
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
 }
 
 }  // namespace mf

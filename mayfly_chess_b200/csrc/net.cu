@@ -138,6 +138,37 @@ static void launch_gemm_bn(const CUtensorMap& ma, const CUtensorMap& mb, const C
     RT(cudaGetLastError());
 }
 
+// The CTA-pair kernel: 256 x 256 tiles, as many clusters as can be resident at once (a persistent grid must
+// never wait for a cluster slot).
+template <typename T, int EPI>
+static void launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M, int N,
+                             int K, const float* bias, uint32_t* err, cudaStream_t s)
+{
+    using C = GemmCfg<256, EPI, true>;
+    static int max_pairs[64] = {};
+    int dev = 0;
+    RT(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw std::runtime_error("cudanet_b200: device index out of range");
+    if (!max_pairs[dev]) {
+        RT(cudaFuncSetAttribute(gemm_tc_pair_kernel<T, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)C::SMEM));
+        int sms = 0;
+        RT(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1));
+        cfg.blockDim = dim3(C::THREADS);
+        cfg.dynamicSmemBytes = C::SMEM;
+        int clusters = 0;
+        RT(cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_pair_kernel<T, EPI>, &cfg));
+        if (clusters < 1) throw std::runtime_error("cudanet_b200: no CTA pair fits on this device");
+        max_pairs[dev] = clusters;
+    }
+    const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    const int pairs = std::min(tiles, max_pairs[dev]);
+    gemm_tc_pair_kernel<T, EPI><<<2 * pairs, C::THREADS, C::SMEM, s>>>(ma, mb, mc, M, N, K, bias, err);
+    RT(cudaGetLastError());
+}
+
 template <typename T, int BN>
 static void launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
                             int N, int K, const float* bias, uint32_t* err, int num_sms, cudaStream_t s)
@@ -151,14 +182,39 @@ static void launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& m
     }
 }
 
-// The widest tile that still gives every SM a tile (weights stream through fewer SMs otherwise).
-static int pick_bn(int M, int N, int num_sms)
+// Tile choice: kPairTile (a CTA pair per 256 x 256 tile) when there are at least as many pair tiles as pairs
+// fit and the epilogue is light next to the MMAs (bias-only or f32 outputs, or K >= 2048: measured on a B200,
+// the pair kernel is faster for qkv and ff2 and slower for out and ff1, whose epilogues gate both CTAs of a
+// pair), else the widest single-CTA tile that still gives every SM a tile (weights stream through fewer SMs
+// otherwise).
+constexpr int kPairTile = 2;
+
+// MAYFLY_CUDANET_TILE: "pair" or "single" forces the CTA-pair or the single-CTA kernels, anything else (the
+// default) chooses per product.
+static int tile_mode()
 {
+    static int mode = [] {
+        const char* e = std::getenv("MAYFLY_CUDANET_TILE");
+        if (e && std::strcmp(e, "pair") == 0) return 1;
+        if (e && std::strcmp(e, "single") == 0) return 2;
+        return 0;
+    }();
+    return mode;
+}
+
+static int pick_bn(int M, int N, int K, int epi, int num_sms)
+{
+    const int mode = tile_mode();
+    const bool light = epi == kEpiBias || epi == kEpiF32 || K >= 2048;
+    if (mode == 1 || (mode == 0 && light && ((M + 255) / 256) * ((N + 255) / 256) >= num_sms / 2)) return kPairTile;
     const int m_tiles = (M + 127) / 128;
     for (int bn : {256, 128})
         if (m_tiles * ((N + bn - 1) / bn) >= num_sms) return bn;
     return 64;
 }
+
+// rows of W in one TMA box for a tile choice
+static uint32_t w_box_rows(int bn) { return bn == kPairTile ? 128u : static_cast<uint32_t>(bn); }
 
 template <typename T>
 static void launch_gemm(int epi, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
@@ -167,10 +223,18 @@ static void launch_gemm(int epi, int bn, const CUtensorMap& ma, const CUtensorMa
     if (K % 64 || K <= 0) throw std::runtime_error("cudanet_b200: GEMM K must be a positive multiple of 64");
     if (M < 1 || N < 1) throw std::runtime_error("cudanet_b200: GEMM with an empty output");
     if (reinterpret_cast<uintptr_t>(bias) & 15) throw std::runtime_error("cudanet_b200: bias not 16-byte aligned");
-    if (bn == 256) launch_gemm_epi<T, 256>(epi, ma, mb, mc, M, N, K, bias, err, num_sms, s);
+    if (bn == kPairTile) {
+        switch (epi) {
+            case kEpiBias: launch_gemm_pair<T, kEpiBias>(ma, mb, mc, M, N, K, bias, err, s); break;
+            case kEpiBiasGelu: launch_gemm_pair<T, kEpiBiasGelu>(ma, mb, mc, M, N, K, bias, err, s); break;
+            case kEpiResidual: launch_gemm_pair<T, kEpiResidual>(ma, mb, mc, M, N, K, bias, err, s); break;
+            case kEpiF32: launch_gemm_pair<T, kEpiF32>(ma, mb, mc, M, N, K, bias, err, s); break;
+            default: throw std::runtime_error("cudanet_b200: unknown epilogue");
+        }
+    } else if (bn == 256) launch_gemm_epi<T, 256>(epi, ma, mb, mc, M, N, K, bias, err, num_sms, s);
     else if (bn == 128) launch_gemm_epi<T, 128>(epi, ma, mb, mc, M, N, K, bias, err, num_sms, s);
     else if (bn == 64) launch_gemm_epi<T, 64>(epi, ma, mb, mc, M, N, K, bias, err, num_sms, s);
-    else throw std::runtime_error("cudanet_b200: tile width must be 64, 128 or 256");
+    else throw std::runtime_error("cudanet_b200: tile choice must be 2 (CTA pair), 64, 128 or 256");
 }
 
 template <typename T>
@@ -604,8 +668,8 @@ const CUtensorMap& Net::wmap(const void* W, int N, int K, int bn)
 void Net::gemm(int epi, const CUtensorMap& ma, const void* W, int M, int N, int K, const float* bias, void* out,
                int ldc, cudaStream_t s)
 {
-    const int bn = pick_bn(M, N, num_sms_);
-    const CUtensorMap& mb = wmap(W, N, K, bn);
+    const int bn = pick_bn(M, N, K, epi, num_sms_);
+    const CUtensorMap& mb = wmap(W, N, K, static_cast<int>(w_box_rows(bn)));
     const auto okey = std::make_tuple(static_cast<const void*>(out), epi, M, N);
     auto it = omaps_.find(okey);
     if (it == omaps_.end()) it = omaps_.emplace(okey, output_map(out, epi, bf16(), M, N, ldc)).first;
@@ -1108,7 +1172,7 @@ CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const 
         mf::RT(cudaGetDevice(&dev));
         int sms = 0;
         mf::RT(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        if (bn == 0) bn = mf::pick_bn(M, N, sms);
+        if (bn == 0) bn = mf::pick_bn(M, N, K, epi, sms);
         if ((reinterpret_cast<uintptr_t>(C) | reinterpret_cast<uintptr_t>(bias)) & 15)
             throw std::runtime_error("cudanet_k_gemm: C and bias must be 16-byte aligned");
         const long long ob = (epi == 2 || epi == 3) ? 4 : 2;
@@ -1119,7 +1183,7 @@ CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const 
         if (epi < 0 || epi > 3) throw std::runtime_error("cudanet_k_gemm: epi must be 0..3");
         const CUtensorMap ma = mf::operand_map(A, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
         const CUtensorMap mb = mf::operand_map(W, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
-                                               static_cast<uint32_t>(bn));
+                                               mf::w_box_rows(bn));
         const CUtensorMap mc = mf::output_map(C, epi, b16, M, N, ldc);
         uint32_t* errw = nullptr;
         mf::RT(cudaMalloc(&errw, 4));
@@ -1157,7 +1221,7 @@ CUDANET_API int cudanet_k_gemm_noalloc(int dtype, int epi, int bn, const void* A
         uint32_t* errw = mf::noalloc_scratch(dev);   // the first call on a device looks the address up
         int sms = 0;
         mf::RT(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        if (bn == 0) bn = mf::pick_bn(M, N, sms);
+        if (bn == 0) bn = mf::pick_bn(M, N, K, epi, sms);
         if ((reinterpret_cast<uintptr_t>(C) | reinterpret_cast<uintptr_t>(bias)) & 15)
             throw std::runtime_error("cudanet_k_gemm_noalloc: C and bias must be 16-byte aligned");
         const long long ob = (epi == 2 || epi == 3) ? 4 : 2;
@@ -1166,7 +1230,7 @@ CUDANET_API int cudanet_k_gemm_noalloc(int dtype, int epi, int bn, const void* A
         const bool b16 = dtype == 1;
         const CUtensorMap ma = mf::operand_map(A, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
         const CUtensorMap mb = mf::operand_map(W, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
-                                               static_cast<uint32_t>(bn));
+                                               mf::w_box_rows(bn));
         const CUtensorMap mc = mf::output_map(C, epi, b16, M, N, ldc);
         const cudaStream_t s = static_cast<cudaStream_t>(stream);
         // the word keeps the last call's value: clear it for this call, in stream order

@@ -30,7 +30,10 @@ def _ref_gemm(A, W, bias, epi, C0=None):
 @pytest.mark.parametrize("epi", [0, 1, 2, 3])
 @pytest.mark.parametrize("M,N,K,bn", [(195, 1024, 1024, 0), (4160, 3072, 1024, 256), (1300, 1024, 2048, 128),
                                       (65, 2048, 1024, 64), (300, 8328, 1024, 256), (300, 8324, 1024, 256),
-                                      (128, 256, 64, 256)])
+                                      (128, 256, 64, 256),
+                                      # CTA pairs (bn 2): 256 x 256 tiles, M and N tails, K = 2048
+                                      (4160, 3072, 1024, 2), (300, 8328, 1024, 2), (1300, 1024, 2048, 2),
+                                      (65, 512, 128, 2)])
 def test_gemm(k, dtype, epi, M, N, K, bn):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K + epi)
     A = torch.randn(M, K, device="cuda", generator=g).to(dtype)
