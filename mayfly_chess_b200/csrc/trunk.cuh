@@ -198,6 +198,14 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                  : "r"(addr));
 }
 
+// 2^x by the special-function unit (ex2.approx.ftz.f32); 2^-inf = 0
+__device__ __forceinline__ float ex2_approx(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 constexpr int kAttRows = 80;     // 65 tokens padded to 5 tiles of 16
 constexpr int kAttWarps = 5;
 
@@ -241,7 +249,8 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const T* __re
     const int g = lane >> 2, t = lane & 3;
     const int q0 = warp * 16;
 
-    // S = Q K^T for this warp's 16 rows and all 80 keys
+    // S = Q K^T for this warp's 16 rows and keys 0..71 (key tile 9, keys 72..79, is all padding: P = 0 there)
+    constexpr int NT_LIVE = (kTokens + 7) / 8;   // 9 key tiles hold the 65 live keys
     float s[NT][4];
 #pragma unroll
     for (int n = 0; n < NT; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
@@ -250,18 +259,21 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const T* __re
         uint32_t a[4];
         ldsm_x4(smem_u32(sQ + (q0 + (lane & 15)) * P + k0 + (lane >> 4) * 8), a[0], a[1], a[2], a[3]);
 #pragma unroll
-        for (int n = 0; n < NT; n += 2) {
+        for (int n = 0; n < NT_LIVE; n += 2) {
             // keys n*8 .. n*8+15: matrices (keys 0-7, k0), (keys 0-7, k0+8), (keys 8-15, k0), (keys 8-15, k0+8)
             const int key = n * 8 + (lane & 7) + ((lane >> 4) << 3);
             const int kk = k0 + ((lane >> 3) & 1) * 8;
             uint32_t b0, b1, b2, b3;
             ldsm_x4(smem_u32(sK + key * P + kk), b0, b1, b2, b3);
             MmaName<T>::mma(s[n], a, b0, b1);
-            MmaName<T>::mma(s[n + 1], a, b2, b3);
+            if (n + 1 < NT_LIVE) MmaName<T>::mma(s[n + 1], a, b2, b3);
         }
     }
 
-    // softmax over keys 0..64 of rows g and g+8 (each row spread over the quad's 4 lanes)
+    // softmax over keys 0..64 of rows g and g+8 (each row spread over the quad's 4 lanes), in base 2:
+    // exp(x * scale - m) = 2^(x * scale * log2(e) - m * log2(e)), with the hardware 2^x (ex2.approx, relative
+    // error near 2^-22, far below the 16-bit rounding P gets next)
+    const float sl2 = scale * 1.4426950408889634f;
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
@@ -269,8 +281,8 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const T* __re
         for (int j = 0; j < 2; ++j) {
             const int key = n * 8 + 2 * t + j;
             const bool live = key < kTokens;
-            s[n][j] = live ? s[n][j] * scale : -INFINITY;
-            s[n][2 + j] = live ? s[n][2 + j] * scale : -INFINITY;
+            s[n][j] = live ? s[n][j] * sl2 : -INFINITY;
+            s[n][2 + j] = live ? s[n][2 + j] * sl2 : -INFINITY;
             mx0 = fmaxf(mx0, s[n][j]);
             mx1 = fmaxf(mx1, s[n][2 + j]);
         }
@@ -284,8 +296,8 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const T* __re
     for (int n = 0; n < NT; ++n) {
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            s[n][j] = expf(s[n][j] - mx0);
-            s[n][2 + j] = expf(s[n][2 + j] - mx1);
+            s[n][j] = ex2_approx(s[n][j] - mx0);
+            s[n][2 + j] = ex2_approx(s[n][2 + j] - mx1);
             sum0 += s[n][j];
             sum1 += s[n][2 + j];
         }
