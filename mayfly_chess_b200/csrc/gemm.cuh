@@ -80,10 +80,28 @@ template <int BN, int EPI, bool PAIR = false> struct GemmCfg {
     static_assert(!PAIR || BN == 256, "the pair kernel covers 256 columns");
 };
 
+// erf(x) by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26:
+//   erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2),  t = 1 / (1 + p x),  x >= 0,
+// |error| <= 1.5e-7, odd in x. The reciprocal and 2^x run on the special-function unit (rcp.approx and
+// ex2.approx, relative errors near 2^-23); the result feeds a 16-bit rounding (2^-9 or 2^-12 relative), so the
+// exact-erf GELU is kept to far below what the output can show, with fewer instructions than erff (the GELU
+// epilogue is the busiest of the four).
+__device__ __forceinline__ float erf_as(float x)
+{
+    const float ax = fabsf(x);
+    float t;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, ax, 1.0f)));
+    const float poly =
+        t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-ax * ax * 1.4426950408889634f));
+    return copysignf(fmaf(-poly, e, 1.0f), x);
+}
+
 __device__ __forceinline__ float gelu_erf(float x)
 {
     // F.gelu(approximate="none"): x * 0.5 * (1 + erf(x / sqrt(2)))
-    return x * 0.5f * (1.0f + erff(x * 0.70710678118654752440f));
+    return x * 0.5f * (1.0f + erf_as(x * 0.70710678118654752440f));
 }
 
 template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);

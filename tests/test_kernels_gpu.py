@@ -63,6 +63,22 @@ def test_gemm(k, dtype, epi, M, N, K, bn):
     assert math.isfinite(excess) and excess <= 0, excess
 
 
+def test_gelu_epilogue_is_exact_erf_gelu(k):
+    """The GELU epilogue against F.gelu (exact erf) over a dense range: an identity W makes acc = A exactly, so
+    every f16 value of x in [-10, 10) goes through the epilogue once; the f16 output must be the correctly
+    rounded exact GELU to within one f16 unit in the last place."""
+    K = 1024
+    x = torch.arange(-10.0, 10.0, 20.0 / (256 * K), device="cuda").to(torch.float16).view(256, K)
+    W = torch.eye(K, device="cuda", dtype=torch.float16)
+    b = torch.zeros(K, device="cuda")
+    C = torch.empty(256, K, device="cuda", dtype=torch.float16)
+    k.k_gemm(x, W, b, C, 1)
+    torch.cuda.synchronize()
+    ref = F.gelu(x.float().double()).float()
+    ulp = torch.clamp(ref.abs(), min=2.0 ** -14) * 2.0 ** -10
+    assert ((C.float() - ref).abs() <= ulp + 1e-7).all()
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_gemm_repeatable(k, dtype):
     A = torch.randn(4160, 1024, device="cuda").to(dtype)
