@@ -118,6 +118,12 @@ CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const 
 CUDANET_API int cudanet_k_gemm_noalloc(int dtype, int epi, int bn, const void* A, const void* W, const float* bias,
                                        void* C, int M, int N, int K, int ldc, void* stream, char* err, int err_len);
 
+/* X[M, N] += A[M, K] * W[N, K]^T + bias (f32, in place), then H[M, N] = LayerNorm(X) * g + b (16-bit, eps 1e-5):
+ * the residual product fused with the LayerNorm after it. N must be 256, 512 or 1024. */
+CUDANET_API int cudanet_k_gemm_resln(int dtype, const void* A, const void* W, const float* bias, float* X,
+                                     const float* g, const float* b, void* H, int M, int N, int K, void* stream,
+                                     char* err, int err_len);
+
 /* att[rows, d] = per (board, head) softmax(q k^T / sqrt(d/heads)) v over the 65 tokens of each board, qkv
  * [B*65, 3d]. */
 CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,

@@ -27,6 +27,7 @@
 #include <vector>
 
 #include "../../include/cudanet_b200.h"
+#include "gemm_ln.cuh"
 #include "json_min.h"
 #include "trunk.cuh"
 
@@ -49,6 +50,7 @@ static const char* err_site_name(uint32_t site)
         case kErrTmemFull: return "an epilogue waited too long for its accumulator";
         case kErrTmemEmpty: return "a tensor-core product waited too long for a free accumulator";
         case kErrArgs: return "a kernel was launched with arguments it cannot handle";
+        case kErrCluster: return "a CTA waited too long for its cluster's row statistics";
         default: return "unknown device error";
     }
 }
@@ -167,6 +169,56 @@ static void launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const
     const int pairs = std::min(tiles, max_pairs[dev]);
     gemm_tc_pair_kernel<T, EPI><<<2 * pairs, C::THREADS, C::SMEM, s>>>(ma, mb, mc, M, N, K, bias, err);
     RT(cudaGetLastError());
+}
+
+// X += A W^T + bias, then H = LN(X) (gemm_ln.cuh): one cluster of d / 256 CTAs per 128-row block, as many
+// clusters as can be resident.
+template <typename T, int NCL>
+static void launch_gemm_resln_ncl(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mx,
+                                  const CUtensorMap& mh, int M, int K, const float* bias, const float* g,
+                                  const float* b, uint32_t* err, cudaStream_t s)
+{
+    using C = ResLnCfg<NCL>;
+    static int max_clusters[64] = {};
+    int dev = 0;
+    RT(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw std::runtime_error("cudanet_b200: device index out of range");
+    if (!max_clusters[dev]) {
+        RT(cudaFuncSetAttribute(gemm_tc_resln_kernel<T, NCL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)C::SMEM));
+        int sms = 0;
+        RT(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(sms / NCL * NCL));
+        cfg.blockDim = dim3(C::THREADS);
+        cfg.dynamicSmemBytes = C::SMEM;
+        int clusters = 0;
+        RT(cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_resln_kernel<T, NCL>, &cfg));
+        if (clusters < 1) throw std::runtime_error("cudanet_b200: no LayerNorm cluster fits on this device");
+        max_clusters[dev] = clusters;
+    }
+    const int m_tiles = (M + 127) / 128;
+    const int clusters = std::min(m_tiles, max_clusters[dev]);
+    gemm_tc_resln_kernel<T, NCL><<<clusters * NCL, C::THREADS, C::SMEM, s>>>(ma, mb, mx, mh, M, K, bias, g, b, 1e-5f,
+                                                                            err);
+    RT(cudaGetLastError());
+}
+
+template <typename T>
+static void launch_gemm_resln(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mx,
+                              const CUtensorMap& mh, int M, int N, int K, const float* bias, const float* g,
+                              const float* b, uint32_t* err, cudaStream_t s)
+{
+    if (K % 64 || K <= 0) throw std::runtime_error("cudanet_b200: GEMM K must be a positive multiple of 64");
+    if (M < 1) throw std::runtime_error("cudanet_b200: GEMM with an empty output");
+    if ((reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(b)) & 15)
+        throw std::runtime_error("cudanet_b200: bias and LayerNorm vectors must be 16-byte aligned");
+    switch (N) {
+        case 256: launch_gemm_resln_ncl<T, 1>(ma, mb, mx, mh, M, K, bias, g, b, err, s); break;
+        case 512: launch_gemm_resln_ncl<T, 2>(ma, mb, mx, mh, M, K, bias, g, b, err, s); break;
+        case 1024: launch_gemm_resln_ncl<T, 4>(ma, mb, mx, mh, M, K, bias, g, b, err, s); break;
+        default: throw std::runtime_error("cudanet_b200: the fused LayerNorm product needs N in {256, 512, 1024}");
+    }
 }
 
 template <typename T, int BN>
@@ -522,6 +574,9 @@ private:
     const CUtensorMap& wmap(const void* W, int N, int K, int bn);
     void gemm(int epi, const CUtensorMap& ma, const void* W, int M, int N, int K, const float* bias, void* out,
               int ldc, cudaStream_t s);
+    // x += A W^T + bias, then h = LN(x; g, b), in one cluster kernel (gemm_ln.cuh)
+    void gemm_resln(const CUtensorMap& ma, const void* W, int M, int K, const float* bias, const float* g,
+                    const float* b, cudaStream_t s);
     void forward_kernels(int B, cudaStream_t s);
     void forward(int B, cudaStream_t s);
     void capture(int B);
@@ -679,6 +734,35 @@ void Net::gemm(int epi, const CUtensorMap& ma, const void* W, int M, int N, int 
         launch_gemm<__half>(epi, bn, ma, mb, it->second, M, N, K, bias, err_word(), num_sms_, s);
 }
 
+void Net::gemm_resln(const CUtensorMap& ma, const void* W, int M, int K, const float* bias, const float* g,
+                     const float* b, cudaStream_t s)
+{
+    const int d = w_.a.d;
+    const CUtensorMap& mb = wmap(W, d, K, 256);
+    const auto xkey = std::make_tuple(static_cast<const void*>(x_), static_cast<int>(kEpiResidual), M, d);
+    auto ix = omaps_.find(xkey);
+    if (ix == omaps_.end()) ix = omaps_.emplace(xkey, output_map(x_, kEpiResidual, bf16(), M, d, d)).first;
+    const auto hkey = std::make_tuple(static_cast<const void*>(h_), static_cast<int>(kEpiBias), M, d);
+    auto ih = omaps_.find(hkey);
+    if (ih == omaps_.end()) ih = omaps_.emplace(hkey, output_map(h_, kEpiBias, bf16(), M, d, d)).first;
+    if (bf16())
+        launch_gemm_resln<__nv_bfloat16>(ma, mb, ix->second, ih->second, M, d, K, bias, g, b, err_word(), s);
+    else
+        launch_gemm_resln<__half>(ma, mb, ix->second, ih->second, M, d, K, bias, g, b, err_word(), s);
+}
+
+// MAYFLY_CUDANET_FUSE_LN=1 fuses each LayerNorm into the residual product before it (gemm_ln.cuh). Off by
+// default: on a B200 the fused kernels' epilogues (a whole-row statistics exchange per tile) cost more than the
+// separate LayerNorm passes they save (measured 23.1 vs 22.3 ms per 1,024-position pass).
+static bool fuse_ln()
+{
+    static bool on = [] {
+        const char* e = std::getenv("MAYFLY_CUDANET_FUSE_LN");
+        return e && std::strcmp(e, "1") == 0;
+    }();
+    return on;
+}
+
 void Net::mark(int op, cudaStream_t s)
 {
     if (!prof_on_) return;
@@ -727,22 +811,33 @@ template <typename T> void Net::forward_t(int B, cudaStream_t s)
         }
         RT(cudaGetLastError());
     }
+    const bool fuse = fuse_ln();
     for (int i = 0; i < a.layers; ++i) {
         const LayerW& l = L_[static_cast<size_t>(i)];
+        const bool last = i + 1 == a.layers;
         mark(kPLn1, s);
-        if (i > 0) launch_layernorm<T>(x_, l.n1_g, l.n1_b, h, rows, d, 1, s);
+        if (i > 0 && !fuse) launch_layernorm<T>(x_, l.n1_g, l.n1_b, h, rows, d, 1, s);
         mark(kPQkv, s);
         gemm(kEpiBias, map_h_, l.qkv_w, rows, 3 * d, d, l.qkv_b, qkv_, 3 * d, s);
         mark(kPAtt, s);
         launch_attention<T>(static_cast<const T*>(qkv_), static_cast<T*>(att_), B, d, a.heads, s);
         mark(kPOut, s);
-        gemm(kEpiResidual, map_att_, l.out_w, rows, d, d, l.out_b, x_, d, s);
-        mark(kPLn2, s);
-        launch_layernorm<T>(x_, l.n2_g, l.n2_b, h, rows, d, 1, s);
+        if (fuse) {
+            gemm_resln(map_att_, l.out_w, rows, d, l.out_b, l.n2_g, l.n2_b, s);   // x += out; h = LN2(x)
+        } else {
+            gemm(kEpiResidual, map_att_, l.out_w, rows, d, d, l.out_b, x_, d, s);
+            mark(kPLn2, s);
+            launch_layernorm<T>(x_, l.n2_g, l.n2_b, h, rows, d, 1, s);
+        }
         mark(kPFf1, s);
         gemm(kEpiBiasGelu, map_h_, l.ff1_w, rows, ff, d, l.ff1_b, ff_, ff, s);
         mark(kPFf2, s);
-        gemm(kEpiResidual, map_ff_, l.ff2_w, rows, d, ff, l.ff2_b, x_, d, s);
+        if (fuse && !last) {
+            const LayerW& n = L_[static_cast<size_t>(i + 1)];
+            gemm_resln(map_ff_, l.ff2_w, rows, ff, l.ff2_b, n.n1_g, n.n1_b, s);   // x += ff; h = next LN1(x)
+        } else {
+            gemm(kEpiResidual, map_ff_, l.ff2_w, rows, d, ff, l.ff2_b, x_, d, s);
+        }
     }
     mark(kPCls, s);
     launch_layernorm<T>(x_, w_.ptr<float>("ln_g"), w_.ptr<float>("ln_b"), static_cast<T*>(cls_), B, d, kTokens, s);
@@ -1242,6 +1337,40 @@ CUDANET_API int cudanet_k_gemm_noalloc(int dtype, int epi, int bn, const void* A
         mf::RT(cudaStreamSynchronize(s));
         if (e)
             throw std::runtime_error(std::string("cudanet_k_gemm_noalloc: device error: ") + mf::err_site_name(e >> 8));
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_k_gemm_resln(int dtype, const void* A, const void* W, const float* bias, float* X,
+                                     const float* g, const float* b, void* H, int M, int N, int K, void* stream,
+                                     char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_k_gemm_resln: unknown exception", [&] {
+        if (dtype != 0 && dtype != 1) throw std::runtime_error("cudanet_k_gemm_resln: dtype must be 0 (f16) or 1 (bf16)");
+        if (M < 1 || K < 64) throw std::runtime_error("cudanet_k_gemm_resln: bad sizes");
+        if ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(H)) & 15)
+            throw std::runtime_error("cudanet_k_gemm_resln: X and H must be 16-byte aligned");
+        const bool b16 = dtype == 1;
+        const CUtensorMap ma = mf::operand_map(A, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
+        const CUtensorMap mb = mf::operand_map(W, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 256);
+        const CUtensorMap mx = mf::output_map(X, mf::kEpiResidual, b16, M, N, N);
+        const CUtensorMap mh = mf::output_map(H, mf::kEpiBias, b16, M, N, N);
+        uint32_t* errw = nullptr;
+        mf::RT(cudaMalloc(&errw, 4));
+        mf::RT(cudaMemset(errw, 0, 4));
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        try {
+            if (b16) mf::launch_gemm_resln<__nv_bfloat16>(ma, mb, mx, mh, M, N, K, bias, g, b, errw, s);
+            else mf::launch_gemm_resln<__half>(ma, mb, mx, mh, M, N, K, bias, g, b, errw, s);
+            mf::RT(cudaStreamSynchronize(s));
+        } catch (...) {
+            cudaFree(errw);
+            throw;
+        }
+        uint32_t e = 0;
+        mf::RT(cudaMemcpy(&e, errw, 4, cudaMemcpyDeviceToHost));
+        cudaFree(errw);
+        if (e) throw std::runtime_error(std::string("cudanet_k_gemm_resln: device error: ") + mf::err_site_name(e >> 8));
         return 0;
     });
 }

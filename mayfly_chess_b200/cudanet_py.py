@@ -78,6 +78,8 @@ def load(dll=None):
         lib.cudanet_k_gemm.restype = i32
         lib.cudanet_k_gemm_noalloc.argtypes = [i32, i32, i32, vp, vp, vp, vp, i32, i32, i32, i32, vp, cp, i32]
         lib.cudanet_k_gemm_noalloc.restype = i32
+        lib.cudanet_k_gemm_resln.argtypes = [i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, cp, i32]
+        lib.cudanet_k_gemm_resln.restype = i32
         lib.cudanet_k_attention.argtypes = [i32, vp, vp, i32, i32, i32, vp, cp, i32]
         lib.cudanet_k_attention.restype = i32
         lib.cudanet_k_layernorm.argtypes = [i32, vp, vp, vp, vp, i32, i32, i32, vp, cp, i32]
@@ -315,6 +317,19 @@ def k_gemm_noalloc(A, W, bias, C, epi, bn=0, dll=None):
     if rc != 0:
         raise RuntimeError(f"cudanet_k_gemm_noalloc: {_msg(err)}")
     return C
+
+
+def k_gemm_resln(A, W, bias, X, g, b, H, dll=None):
+    """X += A W^T + bias (f32, in place), then H = LayerNorm(X) * g + b (16-bit), in one fused kernel."""
+    lib = load(dll)
+    M, K = A.shape
+    N = W.shape[0]
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_k_gemm_resln(_dtype_code(A), A.data_ptr(), W.data_ptr(), bias.data_ptr(), X.data_ptr(),
+                                  g.data_ptr(), b.data_ptr(), H.data_ptr(), M, N, K, _stream(), err, ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_k_gemm_resln: {_msg(err)}")
+    return X, H
 
 
 def k_attention(qkv, att, B, d, heads, dll=None):

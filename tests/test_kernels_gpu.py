@@ -125,3 +125,27 @@ def test_layernorm(k, dtype, d, stride):
     rel = 2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11      # one rounding of the output
     excess = ((h.float() - ref).abs() - (1e-4 + rel * ref.abs())).max().item()
     assert excess <= 0, excess
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N,K", [(195, 1024, 1024), (4160, 1024, 2048), (1300, 512, 1024), (300, 256, 1024),
+                                   (66560, 1024, 1024)])
+def test_gemm_resln(k, dtype, M, N, K):
+    """The residual product fused with the next LayerNorm (clusters of N / 256 CTAs exchanging row statistics)."""
+    g0 = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.randn(M, K, device="cuda", generator=g0).to(dtype)
+    W = (torch.randn(N, K, device="cuda", generator=g0) * 0.02).to(dtype)
+    bias = torch.randn(N, device="cuda", generator=g0) * 0.02
+    X = torch.randn(M, N, device="cuda", generator=g0) * 3 + 0.5
+    g = torch.randn(N, device="cuda", generator=g0)
+    b = torch.randn(N, device="cuda", generator=g0)
+    H = torch.full((M, N), float("nan"), device="cuda", dtype=dtype)
+    X0 = X.clone()
+    k.k_gemm_resln(A, W, bias, X, g, b, H)
+    torch.cuda.synchronize()
+    xr = X0 + (A.float() @ W.float().t() + bias)
+    assert (X - xr).abs().max().item() < 2e-3
+    hr = F.layer_norm(X, (N,), g, b, 1e-5)          # normalise the kernel's own X: isolates the LayerNorm
+    rel = 2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11
+    excess = ((H.float() - hr).abs() - (2e-4 + rel * hr.abs())).max().item()
+    assert math.isfinite(excess) and excess <= 0, excess
