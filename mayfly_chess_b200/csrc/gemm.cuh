@@ -201,12 +201,24 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
             }
     }
 
+    // the bias slice of the next tile is pulled into L1 a tile ahead (8 x 128-byte lines for 256 columns), so
+    // the epilogue's bias reads do not wait on L2
+    const int gtid = (int)threadIdx.x - 64 - 128 * grp;
+    auto prefetch_bias = [&](int it) {
+        if (it < my_tiles && gtid < BN / 32) {
+            const int c = origin_col(it) + 32 * gtid;
+            if (c < N) asm volatile("prefetch.global.L1 [%0];" ::"l"(bias + c));
+        }
+    };
+    prefetch_bias(0);
+
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
     int g = 0;        // this group's chunks done
     for (int it = 0; it < my_tiles && ok; ++it) {
         const int row0 = origin_row(it), colb = origin_col(it);
+        prefetch_bias(it + 1);
         if (leader) L.epi_ok[grp] = mbar_wait(&L.tfull[acc], acc_phase, err, kErrTmemFull) ? 1u : 0u;
         named_barrier(bar_id, 128);
         if (!L.epi_ok[grp]) break;
@@ -256,16 +268,19 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                 break;
             }
             if constexpr (C::RESID) {
+                // all 8 loads first, then the adds, then the stores (no load waits behind a store)
+                float4 xs[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) xs[j] = *reinterpret_cast<const float4*>(buf + swz(row, j));
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    float4* p = reinterpret_cast<float4*>(buf + swz(row, j));
-                    float4 x = *p;
-                    x.x += v[4 * j + 0];
-                    x.y += v[4 * j + 1];
-                    x.z += v[4 * j + 2];
-                    x.w += v[4 * j + 3];
-                    *p = x;
+                    xs[j].x += v[4 * j + 0];
+                    xs[j].y += v[4 * j + 1];
+                    xs[j].z += v[4 * j + 2];
+                    xs[j].w += v[4 * j + 3];
                 }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(buf + swz(row, j)) = xs[j];
             } else if constexpr (C::OUT_BYTES == 4) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
