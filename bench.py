@@ -1,6 +1,7 @@
 """Throughput of MayFly's batched network evaluation on B200s: positions evaluated per second.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch 1024] [--precision bf16|f16] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch 1024] [--precision bf16|f16|e4m3]
+                    [--impl reference]
 
 Workload (the metric's configuration): the 146M trunk (d 1024, 16 layers, 16 heads, FFN
 2048, 65 tokens, policy + qvalue heads and the search's reduction) with seed-1 random-init weights in bf16,
@@ -18,6 +19,11 @@ independent evaluator per GPU, no collective on the data path (weak scaling: 1,0
              the measured sustained bf16 peak.
   cpu_baseline  the CPU fp32 restatement of the reference forward (oracle/, test infrastructure) on a bounded
              sample on this host's cores.
+
+--precision e4m3 --batch 4096 is BASELINE config 4: the same net with e4m3 weight matrices (per-output-channel
+scales) and e4m3 product inputs at static per-layer scales calibrated on 256 seed-1 positions outside every
+rank's batch (mayfly_chess_b200.quant, one bf16 pass on the GPU before the file is written); its roofline
+peak is twice the measured bf16 figure (no FP8 peak is measured).
 
 --impl reference times the reference's CPU path (the same fp32 restatement, all host threads) on the same
 metric, rank 0 only.
@@ -38,6 +44,7 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 METRIC = "NN positions evaluated/sec (146M trunk, bs1024, 1/2/4/8 B200); p50 latency at bs64"
+CALIB_ROWS = (7936, 8192)   # positions_seed1.npz rows the e4m3 input scales are calibrated on
 POSITIONS = os.path.join(REPO, "tests", "golden", "positions_seed1.npz")
 PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -178,7 +185,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1024)
-    ap.add_argument("--precision", default="bf16", choices=["bf16", "f16"])
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "f16", "e4m3"])
     ap.add_argument("--impl", default="own", choices=["own", "reference"])
     ap.add_argument("--ref-sample", type=int, default=16, help="positions per step of the reference arm")
     ap.add_argument("--cpu-sample", type=int, default=32, help="positions of the cpu_baseline sample")
@@ -221,12 +228,21 @@ def main():
     st = W.random_state(arch, 1)
     tmp = tempfile.mkdtemp(prefix="mayfly_b200_")
     path = os.path.join(tmp, f"net_{args.precision}_{rank}.cnw")
-    W.write_cnw(path, st, arch, args.precision)
+    ps = PositionSet(POSITIONS)
     os.environ.setdefault("MAYFLY_CUDANET_MAX_BATCH", str(max(B, 1024)))
+    if args.precision == "e4m3":
+        from mayfly_chess_b200 import quant
+        amax = quant.calibrate(st, arch, ps.batch(CALIB_ROWS[0], CALIB_ROWS[1] - CALIB_ROWS[0]), device=local)
+        quant.write_e4m3(path, st, arch, amax)
+    else:
+        W.write_cnw(path, st, arch, args.precision)
     net = CudaNet(path, device=local)
     os.remove(path)
-    ps = PositionSet(POSITIONS)
-    b = ps.batch(rank * B, B)
+    if B > len(ps):
+        raise SystemExit(f"--batch {B}: the position set holds {len(ps)}")
+    start = (rank * B) % len(ps)
+    start = start if start + B <= len(ps) else 0
+    b = ps.batch(start, B)
     wide = b["I"].shape[1]
 
     # ---------------------------------------------------------------- value: inputs resident in HBM
@@ -283,12 +299,16 @@ def main():
     achieved = gemm_fl_pos * B / launches / per_launch_s / 1e12
     peaks, peak_kind = load_peaks()
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    peak_source = f"{peak_kind} bf16 sustained"
+    if args.precision == "e4m3":
+        peak *= 2.0
+        peak_source = f"2 x {peak_kind} bf16 sustained (no measured FP8 peak)"
 
     # ---------------------------------------------------------------- latency (config 3) and CPU baseline
     sweep = {}
     if not args.no_sweep:
         for Bs in (1, 16, 64, 128, 256):
-            bs = ps.batch(rank * B, Bs)
+            bs = ps.batch(start, Bs)
             for _ in range(5):
                 net.evaluate(bs["ids"], bs["cast"], bs["hm"], bs["ep"], bs["I"], bs["M"])
             ts = []
@@ -298,7 +318,8 @@ def main():
                 ts.append(time.perf_counter() - t0)
             ts.sort()
             p50, p99 = ts[len(ts) // 2], ts[int(len(ts) * 0.99)]
-            wbytes = 285483008 + 811008   # bf16 matrices + f32 vectors read once per call
+            # matrices (bf16, or e4m3 layer matrices + bf16 heads) + f32 vectors and scales, read once per call
+            wbytes = (151265280 + 1302528) if args.precision == "e4m3" else (285483008 + 811008)
             sweep[str(Bs)] = {"p50_ms": 1000 * p50, "p99_ms": 1000 * p99, "positions_per_s": Bs / p50,
                               "weight_stream_gbs": wbytes / p50 / 1e9}
     cpu = None
@@ -318,7 +339,9 @@ def main():
         "metric": METRIC, "value": value, "unit": "positions/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
-        "config": {"workload": "config 2: 146M trunk (d1024 L16 H16 FF2048, 65 tokens), seed-1 random-init "
+        "config": {"workload": ("config 4 (e4m3 layer products, calibrated static input scales)"
+                                if args.precision == "e4m3" else "config 2") +
+                               ": 146M trunk (d1024 L16 H16 FF2048, 65 tokens), seed-1 random-init "
                                f"weights, {B} seed-1 random-playout positions per GPU per step",
                    "batch_per_gpu": B, "global_batch": B * world, "wide": wide, "precision": args.precision,
                    "parallelism": f"replicas x{world} (no collective)",
@@ -327,7 +350,7 @@ def main():
         "gpu_launches": (1 + 7 * arch.layers - 1 + 2 + 1) * args.steps,
         "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (qkv, out, ff1, ff2 of every layer)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} bf16 sustained", "traffic": None,
+                     "peak_source": peak_source, "traffic": None,
                      "flop_per_launch": gemm_fl_pos * B / launches},
         "pass": {"flop_per_position": fl_pos, "tflops_whole_pass": fl_pos * value / world / 1e12,
                  "frac_whole_pass": fl_pos * value / world / 1e12 / peak, "profile_ms": prof},

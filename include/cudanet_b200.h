@@ -80,7 +80,8 @@ CUDANET_API int cudanet_begin(void* handle, int B, int wide, const int64_t* ids,
                               char* err, int err_len);
 CUDANET_API int cudanet_end(void* handle, float* pol, float* val, float* qv, char* err, int err_len);
 
-/* The arithmetic the handle runs its products in: "f16" or "bf16". Returns the length, -1 on a null handle. */
+/* The arithmetic the handle runs its products in: "f16", "bf16" or "e4m3" (the layer products on e4m3
+ * operands, the heads in bf16). Returns the length, -1 on a null handle. */
 CUDANET_API int cudanet_precision(void* handle, char* buf, int buf_len);
 
 /* One batch whose inputs and outputs are already in device memory of the handle's device, queued on `stream`
@@ -95,6 +96,14 @@ CUDANET_API int cudanet_evaluate_device(void* handle, int B, int wide, const int
 /* Wait for the handle's work, including work queued by cudanet_evaluate_device on `stream`, and report a
  * device-side failure recorded since the last check. Returns 0, or -1 with the reason in err. */
 CUDANET_API int cudanet_check(void* handle, void* stream, char* err, int err_len);
+
+/* Runs the handle's 16-bit pass on B positions (ids, cast, hm, ep as for cudanet_evaluate) and writes, per
+ * layer i, max |.| of the inputs of its four products to amax[4i + 0..3] (qkv, out, ff1, ff2): the ranges an
+ * e4m3 weight file's static input scales are set from. amax holds n floats, at least 4 * layers. Returns the
+ * count written, or -1 with the reason in err (also for an e4m3 handle). No counterpart in the reference,
+ * whose FP8 path was a simulation (mayfly/docs/cuda_backend.md:150-152). */
+CUDANET_API int cudanet_calibrate(void* handle, int B, const int64_t* ids, const float* cast, const int64_t* hm,
+                                  const int64_t* ep, float* amax, int n, char* err, int err_len);
 
 /* ---------------------------------------------------------------- single kernels, for unit tests
  * Device pointers on the current device, queued on `stream`, synchronous (the call waits for the stream).
@@ -132,6 +141,22 @@ CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B
 /* h[i] = LayerNorm(x[i * row_stride]) (f32 in, 16-bit out), i < n, eps 1e-5. */
 CUDANET_API int cudanet_k_layernorm(int dtype, const float* x, const float* g, const float* b, void* h, int n,
                                     int d, int row_stride, void* stream, char* err, int err_len);
+
+/* The FP8 pieces (no counterpart in the reference). A[M, K] and W[N, K] are e4m3 bytes, K a multiple of 128;
+ * v = acc * colscale[n] + bias[n] with epi 0: C bf16 = v; 2: C f32 += v; 3: C f32 = v; 4: C e4m3 =
+ * gelu(v) * out_scale_inv (round to nearest even, saturating at +-448). bn as for cudanet_k_gemm (epi 4 needs
+ * 128 or wider). */
+CUDANET_API int cudanet_k_gemm_f8(int epi, int bn, const void* A, const void* W, const float* colscale,
+                                  const float* bias, float out_scale_inv, void* C, int M, int N, int K, int ldc,
+                                  void* stream, char* err, int err_len);
+
+/* cudanet_k_attention on bf16 qkv with e4m3 output: att = e4m3(attention * mul). */
+CUDANET_API int cudanet_k_attention_f8(const void* qkv, void* att, int B, int d, int heads, float mul, void* stream,
+                                       char* err, int err_len);
+
+/* cudanet_k_layernorm with e4m3 output: h[i] = e4m3(LayerNorm(x[i * row_stride]) * mul). */
+CUDANET_API int cudanet_k_layernorm_f8(const float* x, const float* g, const float* b, void* h, int n, int d,
+                                       int row_stride, float mul, void* stream, char* err, int err_len);
 
 #ifdef __cplusplus
 }

@@ -39,24 +39,64 @@
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include "ptx.cuh"
 
 namespace mf {
 
-enum Epi : int { kEpiBias = 0, kEpiBiasGelu = 1, kEpiResidual = 2, kEpiF32 = 3 };
+// kEpiGeluE4m3 (the FP8 path's ff1): C (e4m3) = e4m3(gelu(acc * s + bias) * out_scale_inv)
+enum Epi : int { kEpiBias = 0, kEpiBiasGelu = 1, kEpiResidual = 2, kEpiF32 = 3, kEpiGeluE4m3 = 4 };
 
-template <typename T> struct Fmt;
-template <> struct Fmt<__half> { static constexpr uint32_t v = 0; };
-template <> struct Fmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
+// Operand types: 16-bit (kind::f16) or e4m3 (kind::f8f6f4). A stage row is always 128 bytes (the swizzle atom),
+// so an FP8 stage holds 128 elements of K and each MMA instruction 32 (16 for 16-bit); the byte sizes, smem
+// descriptors and the 32-byte step per instruction are the same.
+template <typename T> struct Operand;
+template <> struct Operand<__half> {
+    static constexpr bool F8 = false;
+    __host__ __device__ static constexpr uint32_t idesc(uint32_t M, uint32_t N) { return idesc_f16(0, M, N); }
+};
+template <> struct Operand<__nv_bfloat16> {
+    static constexpr bool F8 = false;
+    __host__ __device__ static constexpr uint32_t idesc(uint32_t M, uint32_t N) { return idesc_f16(1, M, N); }
+};
+template <> struct Operand<__nv_fp8_e4m3> {
+    static constexpr bool F8 = true;
+    __host__ __device__ static constexpr uint32_t idesc(uint32_t M, uint32_t N) { return idesc_e4m3(M, N); }
+};
+
+template <typename TI>
+__device__ __forceinline__ void umma_issue(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc)
+{
+    if constexpr (Operand<TI>::F8) umma_f8(d, a, b, idesc, acc);
+    else umma_f16(d, a, b, idesc, acc);
+}
+
+template <typename TI>
+__device__ __forceinline__ void umma_issue_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc)
+{
+    if constexpr (Operand<TI>::F8) umma_f8_pair(d, a, b, idesc, acc);
+    else umma_f16_pair(d, a, b, idesc, acc);
+}
+
+// The epilogue's per-product constants: FP8 products scale the accumulator column by column
+// (colscale[c] = input scale x weight scale of output channel c) and the e4m3 output divides by its own scale.
+struct EpiArgs {
+    const float* bias;
+    const float* colscale;   // nullptr: no scaling (16-bit operands)
+    float out_scale_inv;     // kEpiGeluE4m3 only
+};
 
 // PAIR: the CTA-pair kernel, where a CTA loads BN/2 rows of W per stage and a pair covers 256 rows of M.
-template <int BN, int EPI, bool PAIR = false> struct GemmCfg {
+// F8: e4m3 operands (128 elements of K per stage instead of 64; the same bytes).
+template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
     static constexpr int BM = 128;                      // rows of A and of the output per CTA
-    static constexpr int BK = 64;                       // 64 x 16-bit = one 128-byte swizzle row
+    static constexpr int BK = F8 ? 128 : 64;            // elements of K per stage: one 128-byte swizzle row
+    static constexpr int KSTEPS = 4;                    // MMA instructions per stage (K = 16 or 32 each, 32 bytes)
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;   // rows of W per CTA per stage
     static constexpr bool RESID = EPI == kEpiResidual;
-    static constexpr int OUT_BYTES = (EPI == kEpiResidual || EPI == kEpiF32) ? 4 : 2;
+    static constexpr bool IS_F8 = F8;
+    static constexpr int OUT_BYTES = (EPI == kEpiResidual || EPI == kEpiF32) ? 4 : (EPI == kEpiGeluE4m3 ? 1 : 2);
     static constexpr int CHUNK_COLS = 128 / OUT_BYTES;   // one staging chunk: 128 rows x 128 bytes
     static constexpr int NC = BN / CHUNK_COLS;           // staging chunks per tile
     static constexpr uint32_t CHUNK_BYTES = 128 * 128;
@@ -65,8 +105,8 @@ template <int BN, int EPI, bool PAIR = false> struct GemmCfg {
     // keeps one group with deeper prefetch.
     static constexpr int EG = (!RESID && NC % 2 == 0) ? 2 : 1;
     static constexpr int NBUF = RESID ? 4 : (EG == 2 ? 1 : 2);   // staging buffers per group
-    static constexpr uint32_t A_BYTES = BM * BK * 2;
-    static constexpr uint32_t B_BYTES = B_ROWS * BK * 2;
+    static constexpr uint32_t A_BYTES = BM * 128;
+    static constexpr uint32_t B_BYTES = B_ROWS * 128;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES_FIT = (224 * 1024 - EG * NBUF * (int)CHUNK_BYTES) / (int)STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
@@ -76,7 +116,7 @@ template <int BN, int EPI, bool PAIR = false> struct GemmCfg {
     static constexpr int THREADS = 64 + 128 * EG;
     static_assert(STAGES >= 3, "pipeline too shallow");
     static_assert(SMEM <= 232448, "shared memory over the per-block limit");
-    static_assert(BN % CHUNK_COLS == 0, "tile width must hold whole staging chunks");
+    static_assert(BN % CHUNK_COLS == 0 && NC >= 1, "tile width must hold whole staging chunks");
     static_assert(!PAIR || BN == 256, "the pair kernel covers 256 columns");
 };
 
@@ -137,6 +177,37 @@ __device__ __forceinline__ void add_bias32(float (&v)[NV], int off, const float*
     }
 }
 
+// v[off + i] = v[off + i] * colscale[col0 + i] + bias[col0 + i], i < 32 (the FP8 products)
+template <int NV>
+__device__ __forceinline__ void scale_bias32(float (&v)[NV], int off, const float* __restrict__ colscale,
+                                             const float* __restrict__ bias, int col0, int N)
+{
+    if (col0 + 32 <= N) {
+        const float4* s4 = reinterpret_cast<const float4*>(colscale + col0);
+        const float4* b4 = reinterpret_cast<const float4*>(bias + col0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 sc = __ldg(s4 + i), b = __ldg(b4 + i);
+            v[off + 4 * i + 0] = fmaf(v[off + 4 * i + 0], sc.x, b.x);
+            v[off + 4 * i + 1] = fmaf(v[off + 4 * i + 1], sc.y, b.y);
+            v[off + 4 * i + 2] = fmaf(v[off + 4 * i + 2], sc.z, b.z);
+            v[off + 4 * i + 3] = fmaf(v[off + 4 * i + 3], sc.w, b.w);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (col0 + i < N) v[off + i] = fmaf(v[off + i], __ldg(colscale + col0 + i), __ldg(bias + col0 + i));
+    }
+}
+
+// four floats to four e4m3 bytes (round to nearest even, saturating to +-448), first value in the lowest byte
+__device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d)
+{
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+    return lo | (hi << 16);
+}
+
 // byte offset of 16-byte unit j of row r in a 128-byte-swizzled staging chunk (what a TMA tensor map with
 // CU_TENSOR_MAP_SWIZZLE_128B reads and writes; the chunk base is 1024-byte aligned)
 __device__ __forceinline__ uint32_t swz(int r, int j) { return (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)); }
@@ -168,11 +239,14 @@ template <typename C> struct SmemLayout {
 // The epilogue warps' loop over this CTA's tiles (warps 2 .. 2 + 4*EG - 1). Tile `it` of this CTA has its
 // output origin at (origin_row(it), origin_col(it)); when a warp has read its last accumulator columns of a
 // tile it calls release(acc) on lane 0 (an arrive on the barrier the MMA thread waits on).
+// T is the 16-bit output type (kEpiBias / kEpiBiasGelu); the FP8 products (C::F8) scale each column first.
 template <typename T, int EPI, typename C, typename RowFn, typename ColFn, typename ReleaseFn>
 __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUtensorMap* tmC, uint32_t tmem_base,
                                               int my_tiles, RowFn origin_row, ColFn origin_col, ReleaseFn release,
-                                              const float* __restrict__ bias, int N, uint32_t* err)
+                                              const EpiArgs& ep, int N, uint32_t* err)
 {
+    const float* __restrict__ bias = ep.bias;
+    const float* __restrict__ colscale = ep.colscale;
     constexpr int BN = C::NC * C::CHUNK_COLS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = (warp - 2) >> 2;                      // epilogue group: chunks grp, grp + EG, ...
@@ -202,12 +276,15 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
     }
 
     // the bias slice of the next tile is pulled into L1 a tile ahead (8 x 128-byte lines for 256 columns), so
-    // the epilogue's bias reads do not wait on L2
+    // the epilogue's bias reads do not wait on L2 (and the column scales, for FP8 products)
     const int gtid = (int)threadIdx.x - 64 - 128 * grp;
     auto prefetch_bias = [&](int it) {
         if (it < my_tiles && gtid < BN / 32) {
             const int c = origin_col(it) + 32 * gtid;
-            if (c < N) asm volatile("prefetch.global.L1 [%0];" ::"l"(bias + c));
+            if (c < N) {
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(bias + c));
+                if constexpr (C::IS_F8) asm volatile("prefetch.global.L1 [%0];" ::"l"(colscale + c));
+            }
         }
     };
     prefetch_bias(0);
@@ -229,32 +306,40 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
             const int b = g % C::NBUF;
             uint8_t* buf = gbuf + b * C::CHUNK_BYTES;
             const int col0 = colb + c * C::CHUNK_COLS;
-            // the accumulator columns of this chunk (one or two 32-column loads)
-            float v[C::CHUNK_COLS];
-            {
+            // this chunk's row in registers, 32 accumulator columns at a time: f32 values (4-byte outputs, the
+            // only one-load case) or the row's 128 output bytes already packed (16-bit and e4m3 outputs)
+            constexpr int LOADS = C::CHUNK_COLS / 32;
+            float v[32];
+            uint32_t q[32];
+#pragma unroll
+            for (int p = 0; p < LOADS; ++p) {
                 uint32_t r[32];
-                tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * C::CHUNK_COLS), r);
+                tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * C::CHUNK_COLS + 32 * p), r);
                 tmem_ld_wait();
+                if (ci == CPG - 1 && p == LOADS - 1) {
+                    // this warp is done with the accumulator: hand it back to the MMA thread
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) release(acc);
+                }
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                if constexpr (C::CHUNK_COLS == 64) {
-                    tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * C::CHUNK_COLS + 32), r);
-                    tmem_ld_wait();
+                if constexpr (C::IS_F8) scale_bias32<32>(v, 0, colscale, bias, col0 + 32 * p, N);
+                else add_bias32<32>(v, 0, bias, col0 + 32 * p, N);
+                if constexpr (EPI == kEpiBiasGelu) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
+                    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
                 }
-            }
-            if (ci == CPG - 1) {
-                // this warp is done with the accumulator: hand it back to the MMA thread
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) release(acc);
-            }
-            add_bias32<C::CHUNK_COLS>(v, 0, bias, col0, N);
-            if constexpr (C::CHUNK_COLS == 64) add_bias32<C::CHUNK_COLS>(v, 32, bias, col0 + 32, N);
-            if constexpr (EPI == kEpiBiasGelu) {
+                if constexpr (EPI == kEpiGeluE4m3) {
+                    const float inv = ep.out_scale_inv;
 #pragma unroll
-                for (int i = 0; i < C::CHUNK_COLS; ++i) v[i] = gelu_erf(v[i]);
+                    for (int i = 0; i < 8; ++i)
+                        q[8 * p + i] = pack_e4m3x4(gelu_erf(v[4 * i]) * inv, gelu_erf(v[4 * i + 1]) * inv,
+                                                   gelu_erf(v[4 * i + 2]) * inv, gelu_erf(v[4 * i + 3]) * inv);
+                } else if constexpr (C::OUT_BYTES == 2) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) q[16 * p + i] = pack2<T>(v[2 * i], v[2 * i + 1]);
+                }
             }
             // the staging buffer must be ready: loaded (residual) or no longer read by its last store
             if constexpr (C::RESID) {
@@ -288,14 +373,9 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                         make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             } else {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    uint4 q;
-                    q.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
-                    q.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
-                    q.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
-                    q.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
-                    *reinterpret_cast<uint4*>(buf + swz(row, j)) = q;
-                }
+                for (int j = 0; j < 8; ++j)
+                    *reinterpret_cast<uint4*>(buf + swz(row, j)) =
+                        make_uint4(q[4 * j], q[4 * j + 1], q[4 * j + 2], q[4 * j + 3]);
             }
             fence_proxy_async_smem();
             named_barrier(bar_id, 128);
@@ -329,13 +409,13 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
 }
 
 // ------------------------------------------------------------------------------------------------ one CTA
-template <typename T, int BN, int EPI>
-__global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
+// TI: the operands' type (f16, bf16 or e4m3); T: the 16-bit output type of kEpiBias / kEpiBiasGelu.
+template <typename TI, typename T, int BN, int EPI>
+__global__ void __launch_bounds__(GemmCfg<BN, EPI, false, Operand<TI>::F8>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC, int M, int N, int K, const float* __restrict__ bias,
-               uint32_t* err)
+               const __grid_constant__ CUtensorMap tmC, int M, int N, int K, const EpiArgs ep, uint32_t* err)
 {
-    using C = GemmCfg<BN, EPI>;
+    using C = GemmCfg<BN, EPI, false, Operand<TI>::F8>;
     extern __shared__ uint8_t smem_raw[];
     const SmemLayout<C> L(smem_raw);
 
@@ -404,7 +484,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0 && k_iters > 0) {
-            constexpr uint32_t idesc = idesc_f16(Fmt<T>::v, 128, BN);
+            constexpr uint32_t idesc = Operand<TI>::idesc(128, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -423,9 +503,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const uint32_t a_addr = smem_u32(L.sA + stage * C::A_BYTES);
                     const uint32_t b_addr = smem_u32(L.sB + stage * C::B_BYTES);
 #pragma unroll
-                    for (int k = 0; k < C::BK / 16; ++k)
-                        umma_f16(d_tmem, sdesc_sw128(a_addr + 32u * k), sdesc_sw128(b_addr + 32u * k), idesc,
-                                 (kb | k) != 0 ? 1u : 0u);
+                    for (int k = 0; k < C::KSTEPS; ++k)
+                        umma_issue<TI>(d_tmem, sdesc_sw128(a_addr + 32u * k), sdesc_sw128(b_addr + 32u * k), idesc,
+                                       (kb | k) != 0 ? 1u : 0u);
                     umma_commit(&L.empty[stage]);
                     if (++stage == C::STAGES) {
                         stage = 0;
@@ -448,7 +528,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             L, &tmC, tmem_base, my_tiles,
             [&](int it) { return (((int)blockIdx.x + it * (int)gridDim.x) / n_tiles) * C::BM; },
             [&](int it) { return (((int)blockIdx.x + it * (int)gridDim.x) % n_tiles) * BN; },
-            [&](int acc) { mbar_arrive(&L.tempty[acc]); }, bias, N, err);
+            [&](int acc) { mbar_arrive(&L.tempty[acc]); }, ep, N, err);
     }
 
     __syncwarp();
@@ -462,14 +542,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // A cluster of two CTAs computes a 256 x 256 tile. Rank 0 (the leader) owns the ring's `full` barriers (both
 // CTAs' loads complete there), the accumulator's `tempty` barriers (both CTAs' epilogue warps arrive there) and
 // issues every MMA; each CTA's `empty` and `tfull` barriers are signalled by the leader's commits.
-template <typename T, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<256, EPI, true>::THREADS, 1)
+template <typename TI, typename T, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<256, EPI, true, Operand<TI>::F8>::THREADS, 1)
 gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, int M, int N, int K, const float* __restrict__ bias,
-                    uint32_t* err)
+                    const __grid_constant__ CUtensorMap tmC, int M, int N, int K, const EpiArgs ep, uint32_t* err)
 {
     constexpr int BN = 256;
-    using C = GemmCfg<BN, EPI, true>;
+    using C = GemmCfg<BN, EPI, true, Operand<TI>::F8>;
     extern __shared__ uint8_t smem_raw[];
     const SmemLayout<C> L(smem_raw);
 
@@ -547,7 +626,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer (leader only)
         if (lead && lane == 0 && k_iters > 0) {
-            constexpr uint32_t idesc = idesc_f16(Fmt<T>::v, 256, BN);
+            constexpr uint32_t idesc = Operand<TI>::idesc(256, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -566,9 +645,9 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     const uint32_t a_addr = smem_u32(L.sA + stage * C::A_BYTES);
                     const uint32_t b_addr = smem_u32(L.sB + stage * C::B_BYTES);
 #pragma unroll
-                    for (int k = 0; k < C::BK / 16; ++k)
-                        umma_f16_pair(d_tmem, sdesc_sw128(a_addr + 32u * k), sdesc_sw128(b_addr + 32u * k), idesc,
-                                      (kb | k) != 0 ? 1u : 0u);
+                    for (int k = 0; k < C::KSTEPS; ++k)
+                        umma_issue_pair<TI>(d_tmem, sdesc_sw128(a_addr + 32u * k), sdesc_sw128(b_addr + 32u * k),
+                                            idesc, (kb | k) != 0 ? 1u : 0u);
                     const uint32_t e = smem_u32(&L.empty[stage]);
                     umma_commit_pair(e);                    // this CTA's stage
                     umma_commit_pair(mapa_shared(e, 1));    // the other CTA's stage
@@ -596,7 +675,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             L, &tmC, tmem_base, my_tiles,
             [&](int it) { return ((pair + it * num_pairs) / n_tiles) * 2 * C::BM + (int)rank * C::BM; },
             [&](int it) { return ((pair + it * num_pairs) % n_tiles) * BN; },
-            [&](int acc) { mbar_arrive_cluster(acc ? tempty_lead1 : tempty_lead0); }, bias, N, err);
+            [&](int acc) { mbar_arrive_cluster(acc ? tempty_lead1 : tempty_lead0); }, ep, N, err);
     }
 
     __syncwarp();

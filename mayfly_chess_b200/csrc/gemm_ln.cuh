@@ -155,7 +155,7 @@ gemm_tc_resln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0 && k_iters > 0) {
-            constexpr uint32_t idesc = idesc_f16(Fmt<T>::v, 128, BN);
+            constexpr uint32_t idesc = Operand<T>::idesc(128, BN);
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
             bool ok = true;

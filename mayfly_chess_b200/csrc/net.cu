@@ -77,13 +77,15 @@ static EncodeTiledFn encode_tiled()
 
 // A row-major matrix [outer, inner] with row pitch `pitch` elements, tiles of box_inner x box_outer with the
 // 128-byte swizzle (box_inner * element size = 128 bytes: the layout sdesc_sw128 and the epilogue's staging
-// describe). Reads past the extents are zero, writes past them are dropped.
-enum class MapType { F16, BF16, F32 };
+// describe). Reads past the extents are zero, writes past them are dropped. U8 carries e4m3 bytes.
+enum class MapType { F16, BF16, F32, U8 };
+
+static uint64_t map_elem_bytes(MapType type) { return type == MapType::F32 ? 4 : type == MapType::U8 ? 1 : 2; }
 
 static CUtensorMap make_map(const void* base, MapType type, uint64_t inner, uint64_t outer, uint64_t pitch,
                             uint32_t box_inner, uint32_t box_outer)
 {
-    const uint64_t es = type == MapType::F32 ? 4 : 2;
+    const uint64_t es = map_elem_bytes(type);
     if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch * es) % 16)
         throw std::runtime_error("cudanet_b200: a TMA operand or its row pitch is not 16-byte aligned");
     if (box_inner * es != 128) throw std::runtime_error("cudanet_b200: TMA box rows must be 128 bytes");
@@ -94,6 +96,7 @@ static CUtensorMap make_map(const void* base, MapType type, uint64_t inner, uint
     const cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType dt = type == MapType::F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                    : type == MapType::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                   : type == MapType::U8   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const CUresult r = encode_tiled()(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -103,26 +106,30 @@ static CUtensorMap make_map(const void* base, MapType type, uint64_t inner, uint
     return m;
 }
 
-// A K-major 16-bit operand [rows, K] (tiles of 64 x box_rows).
-static CUtensorMap operand_map(const void* base, bool bf16, uint64_t K, uint64_t rows, uint32_t box_rows)
+static MapType type16(bool bf16) { return bf16 ? MapType::BF16 : MapType::F16; }
+
+// A K-major operand [rows, K]: 16-bit (tiles of 64 x box_rows) or e4m3 (U8, tiles of 128 x box_rows).
+static CUtensorMap operand_map(const void* base, MapType type, uint64_t K, uint64_t rows, uint32_t box_rows)
 {
-    return make_map(base, bf16 ? MapType::BF16 : MapType::F16, K, rows, K, 64, box_rows);
+    return make_map(base, type, K, rows, K, static_cast<uint32_t>(128 / map_elem_bytes(type)), box_rows);
 }
 
-// The output (and, for the residual, the input) of a product: [M, N] with pitch ldc, 16-bit for the kEpiBias /
-// kEpiBiasGelu epilogues, f32 for kEpiResidual / kEpiF32; staging chunks of 128 rows x 128 bytes.
-static CUtensorMap output_map(void* base, int epi, bool bf16, int M, int N, int ldc)
+// The output (and, for the residual, the input) of a product: [M, N] with pitch ldc, 16-bit (`t16`) for the
+// kEpiBias / kEpiBiasGelu epilogues, f32 for kEpiResidual / kEpiF32, e4m3 for kEpiGeluE4m3; staging chunks of
+// 128 rows x 128 bytes.
+static CUtensorMap output_map(void* base, int epi, MapType t16, int M, int N, int ldc)
 {
     if (epi == kEpiResidual || epi == kEpiF32) return make_map(base, MapType::F32, N, M, ldc, 32, 128);
-    return make_map(base, bf16 ? MapType::BF16 : MapType::F16, N, M, ldc, 64, 128);
+    if (epi == kEpiGeluE4m3) return make_map(base, MapType::U8, N, M, ldc, 128, 128);
+    return make_map(base, t16, N, M, ldc, 64, 128);
 }
 
 // ------------------------------------------------------------------------------------------------ launchers
-template <typename T, int BN, int EPI>
+template <typename TI, typename T, int BN, int EPI>
 static void launch_gemm_bn(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M, int N, int K,
-                           const float* bias, uint32_t* err, int num_sms, cudaStream_t s)
+                           const EpiArgs& ep, uint32_t* err, int num_sms, cudaStream_t s)
 {
-    using C = GemmCfg<BN, EPI>;
+    using C = GemmCfg<BN, EPI, false, Operand<TI>::F8>;
     // the shared-memory opt-in, once per instantiation and device (the first launch of a batch size is eager,
     // never inside a graph capture)
     static bool attr[64] = {};
@@ -130,29 +137,29 @@ static void launch_gemm_bn(const CUtensorMap& ma, const CUtensorMap& mb, const C
     RT(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) throw std::runtime_error("cudanet_b200: device index out of range");
     if (!attr[dev]) {
-        RT(cudaFuncSetAttribute(gemm_tc_kernel<T, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        RT(cudaFuncSetAttribute(gemm_tc_kernel<TI, T, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)C::SMEM));
         attr[dev] = true;
     }
     const int tiles = ((M + C::BM - 1) / C::BM) * ((N + BN - 1) / BN);
     const int grid = std::min(tiles, num_sms);
-    gemm_tc_kernel<T, BN, EPI><<<grid, C::THREADS, C::SMEM, s>>>(ma, mb, mc, M, N, K, bias, err);
+    gemm_tc_kernel<TI, T, BN, EPI><<<grid, C::THREADS, C::SMEM, s>>>(ma, mb, mc, M, N, K, ep, err);
     RT(cudaGetLastError());
 }
 
 // The CTA-pair kernel: 256 x 256 tiles, as many clusters as can be resident at once (a persistent grid must
 // never wait for a cluster slot).
-template <typename T, int EPI>
+template <typename TI, typename T, int EPI>
 static void launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M, int N,
-                             int K, const float* bias, uint32_t* err, cudaStream_t s)
+                             int K, const EpiArgs& ep, uint32_t* err, cudaStream_t s)
 {
-    using C = GemmCfg<256, EPI, true>;
+    using C = GemmCfg<256, EPI, true, Operand<TI>::F8>;
     static int max_pairs[64] = {};
     int dev = 0;
     RT(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) throw std::runtime_error("cudanet_b200: device index out of range");
     if (!max_pairs[dev]) {
-        RT(cudaFuncSetAttribute(gemm_tc_pair_kernel<T, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        RT(cudaFuncSetAttribute(gemm_tc_pair_kernel<TI, T, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)C::SMEM));
         int sms = 0;
         RT(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -161,13 +168,13 @@ static void launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const
         cfg.blockDim = dim3(C::THREADS);
         cfg.dynamicSmemBytes = C::SMEM;
         int clusters = 0;
-        RT(cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_pair_kernel<T, EPI>, &cfg));
+        RT(cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_pair_kernel<TI, T, EPI>, &cfg));
         if (clusters < 1) throw std::runtime_error("cudanet_b200: no CTA pair fits on this device");
         max_pairs[dev] = clusters;
     }
     const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
     const int pairs = std::min(tiles, max_pairs[dev]);
-    gemm_tc_pair_kernel<T, EPI><<<2 * pairs, C::THREADS, C::SMEM, s>>>(ma, mb, mc, M, N, K, bias, err);
+    gemm_tc_pair_kernel<TI, T, EPI><<<2 * pairs, C::THREADS, C::SMEM, s>>>(ma, mb, mc, M, N, K, ep, err);
     RT(cudaGetLastError());
 }
 
@@ -221,17 +228,42 @@ static void launch_gemm_resln(const CUtensorMap& ma, const CUtensorMap& mb, cons
     }
 }
 
-template <typename T, int BN>
+// The epilogues each operand type has: 16-bit products bias / bias+GELU (16-bit out), residual, f32; FP8
+// products bias (16-bit out), residual, f32, and bias+GELU with e4m3 out (tiles of at least 128 columns).
+template <typename TI, int EPI, int BN> constexpr bool epi_supported()
+{
+    if constexpr (Operand<TI>::F8) return EPI != kEpiBiasGelu && (EPI != kEpiGeluE4m3 || BN >= 128);
+    else return EPI != kEpiGeluE4m3;
+}
+
+template <typename TI, typename T, int BN, int EPI>
+static void launch_gemm_bn_if(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M, int N,
+                              int K, const EpiArgs& ep, uint32_t* err, int num_sms, cudaStream_t s)
+{
+    if constexpr (epi_supported<TI, EPI, BN>()) launch_gemm_bn<TI, T, BN, EPI>(ma, mb, mc, M, N, K, ep, err, num_sms, s);
+    else throw std::runtime_error("cudanet_b200: this epilogue is not built for this operand type and tile");
+}
+
+template <typename TI, typename T, int BN>
 static void launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
-                            int N, int K, const float* bias, uint32_t* err, int num_sms, cudaStream_t s)
+                            int N, int K, const EpiArgs& ep, uint32_t* err, int num_sms, cudaStream_t s)
 {
     switch (epi) {
-        case kEpiBias: launch_gemm_bn<T, BN, kEpiBias>(ma, mb, mc, M, N, K, bias, err, num_sms, s); break;
-        case kEpiBiasGelu: launch_gemm_bn<T, BN, kEpiBiasGelu>(ma, mb, mc, M, N, K, bias, err, num_sms, s); break;
-        case kEpiResidual: launch_gemm_bn<T, BN, kEpiResidual>(ma, mb, mc, M, N, K, bias, err, num_sms, s); break;
-        case kEpiF32: launch_gemm_bn<T, BN, kEpiF32>(ma, mb, mc, M, N, K, bias, err, num_sms, s); break;
+        case kEpiBias: launch_gemm_bn_if<TI, T, BN, kEpiBias>(ma, mb, mc, M, N, K, ep, err, num_sms, s); break;
+        case kEpiBiasGelu: launch_gemm_bn_if<TI, T, BN, kEpiBiasGelu>(ma, mb, mc, M, N, K, ep, err, num_sms, s); break;
+        case kEpiResidual: launch_gemm_bn_if<TI, T, BN, kEpiResidual>(ma, mb, mc, M, N, K, ep, err, num_sms, s); break;
+        case kEpiF32: launch_gemm_bn_if<TI, T, BN, kEpiF32>(ma, mb, mc, M, N, K, ep, err, num_sms, s); break;
+        case kEpiGeluE4m3: launch_gemm_bn_if<TI, T, BN, kEpiGeluE4m3>(ma, mb, mc, M, N, K, ep, err, num_sms, s); break;
         default: throw std::runtime_error("cudanet_b200: unknown epilogue");
     }
+}
+
+template <typename TI, typename T, int EPI>
+static void launch_gemm_pair_if(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M, int N,
+                                int K, const EpiArgs& ep, uint32_t* err, cudaStream_t s)
+{
+    if constexpr (epi_supported<TI, EPI, 256>()) launch_gemm_pair<TI, T, EPI>(ma, mb, mc, M, N, K, ep, err, s);
+    else throw std::runtime_error("cudanet_b200: this epilogue is not built for this operand type");
 }
 
 // Tile choice: kPairTile (a CTA pair per 256 x 256 tile) when there are at least as many pair tiles as pairs
@@ -262,55 +294,64 @@ static int pick_bn(int M, int N, int K, int epi, int num_sms)
     const int m_tiles = (M + 127) / 128;
     for (int bn : {256, 128})
         if (m_tiles * ((N + bn - 1) / bn) >= num_sms) return bn;
-    return 64;
+    return epi == kEpiGeluE4m3 ? 128 : 64;   // an e4m3 staging chunk is 128 columns wide
 }
 
 // rows of W in one TMA box for a tile choice
 static uint32_t w_box_rows(int bn) { return bn == kPairTile ? 128u : static_cast<uint32_t>(bn); }
 
-template <typename T>
+// C = epilogue(A W^T) with A, W of type TI (f16, bf16 or e4m3) and T the 16-bit output type of kEpiBias.
+template <typename TI, typename T>
 static void launch_gemm(int epi, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
-                        int N, int K, const float* bias, uint32_t* err, int num_sms, cudaStream_t s)
+                        int N, int K, const EpiArgs& ep, uint32_t* err, int num_sms, cudaStream_t s)
 {
-    if (K % 64 || K <= 0) throw std::runtime_error("cudanet_b200: GEMM K must be a positive multiple of 64");
+    constexpr int bk = Operand<TI>::F8 ? 128 : 64;
+    if (K % bk || K <= 0)
+        throw std::runtime_error("cudanet_b200: GEMM K must be a positive multiple of " + std::to_string(bk));
     if (M < 1 || N < 1) throw std::runtime_error("cudanet_b200: GEMM with an empty output");
-    if (reinterpret_cast<uintptr_t>(bias) & 15) throw std::runtime_error("cudanet_b200: bias not 16-byte aligned");
+    if (!ep.bias || (reinterpret_cast<uintptr_t>(ep.bias) & 15))
+        throw std::runtime_error("cudanet_b200: bias missing or not 16-byte aligned");
+    if (Operand<TI>::F8 && (!ep.colscale || (reinterpret_cast<uintptr_t>(ep.colscale) & 15)))
+        throw std::runtime_error("cudanet_b200: FP8 column scales missing or not 16-byte aligned");
     if (bn == kPairTile) {
         switch (epi) {
-            case kEpiBias: launch_gemm_pair<T, kEpiBias>(ma, mb, mc, M, N, K, bias, err, s); break;
-            case kEpiBiasGelu: launch_gemm_pair<T, kEpiBiasGelu>(ma, mb, mc, M, N, K, bias, err, s); break;
-            case kEpiResidual: launch_gemm_pair<T, kEpiResidual>(ma, mb, mc, M, N, K, bias, err, s); break;
-            case kEpiF32: launch_gemm_pair<T, kEpiF32>(ma, mb, mc, M, N, K, bias, err, s); break;
+            case kEpiBias: launch_gemm_pair_if<TI, T, kEpiBias>(ma, mb, mc, M, N, K, ep, err, s); break;
+            case kEpiBiasGelu: launch_gemm_pair_if<TI, T, kEpiBiasGelu>(ma, mb, mc, M, N, K, ep, err, s); break;
+            case kEpiResidual: launch_gemm_pair_if<TI, T, kEpiResidual>(ma, mb, mc, M, N, K, ep, err, s); break;
+            case kEpiF32: launch_gemm_pair_if<TI, T, kEpiF32>(ma, mb, mc, M, N, K, ep, err, s); break;
+            case kEpiGeluE4m3: launch_gemm_pair_if<TI, T, kEpiGeluE4m3>(ma, mb, mc, M, N, K, ep, err, s); break;
             default: throw std::runtime_error("cudanet_b200: unknown epilogue");
         }
-    } else if (bn == 256) launch_gemm_epi<T, 256>(epi, ma, mb, mc, M, N, K, bias, err, num_sms, s);
-    else if (bn == 128) launch_gemm_epi<T, 128>(epi, ma, mb, mc, M, N, K, bias, err, num_sms, s);
-    else if (bn == 64) launch_gemm_epi<T, 64>(epi, ma, mb, mc, M, N, K, bias, err, num_sms, s);
+    } else if (bn == 256) launch_gemm_epi<TI, T, 256>(epi, ma, mb, mc, M, N, K, ep, err, num_sms, s);
+    else if (bn == 128) launch_gemm_epi<TI, T, 128>(epi, ma, mb, mc, M, N, K, ep, err, num_sms, s);
+    else if (bn == 64) launch_gemm_epi<TI, T, 64>(epi, ma, mb, mc, M, N, K, ep, err, num_sms, s);
     else throw std::runtime_error("cudanet_b200: tile choice must be 2 (CTA pair), 64, 128 or 256");
 }
 
+// h = LN(x) in T (16-bit, or e4m3 of h * mul)
 template <typename T>
 static void launch_layernorm(const float* x, const float* g, const float* b, T* h, int n, int d, int row_stride,
-                             cudaStream_t s)
+                             float mul, cudaStream_t s)
 {
     const dim3 grid((n + 7) / 8), block(256);
     switch (d) {
-        case 256: layernorm_kernel<T, 2><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f); break;
-        case 512: layernorm_kernel<T, 4><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f); break;
-        case 1024: layernorm_kernel<T, 8><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f); break;
+        case 256: layernorm_kernel<T, 2><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
+        case 512: layernorm_kernel<T, 4><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
+        case 1024: layernorm_kernel<T, 8><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
         default: throw std::runtime_error("cudanet_b200: width must be 256, 512 or 1024");
     }
     RT(cudaGetLastError());
 }
 
-template <typename T>
-static void launch_attention(const T* qkv, T* att, int B, int d, int heads, cudaStream_t s)
+// att = attention(qkv) in TO (T, or e4m3 of att * mul)
+template <typename T, typename TO>
+static void launch_attention(const T* qkv, TO* att, int B, int d, int heads, float mul, cudaStream_t s)
 {
     const int dh = d / heads;
     const dim3 grid(heads, B), block(kAttWarps * 32);
     const float scale = 1.0f / std::sqrt(static_cast<float>(dh));
-    if (dh == 64) attention_kernel<T, 64><<<grid, block, 0, s>>>(qkv, att, d, scale);
-    else if (dh == 32) attention_kernel<T, 32><<<grid, block, 0, s>>>(qkv, att, d, scale);
+    if (dh == 64) attention_kernel<T, TO, 64><<<grid, block, 0, s>>>(qkv, att, d, scale, mul);
+    else if (dh == 32) attention_kernel<T, TO, 32><<<grid, block, 0, s>>>(qkv, att, d, scale, mul);
     else throw std::runtime_error("cudanet_b200: head width must be 32 or 64");
     RT(cudaGetLastError());
 }
@@ -320,7 +361,9 @@ struct Arch {
     int d = 0, layers = 0, heads = 0, ff = 0, tokens = 0, moves = 0;
 };
 
-enum class Prec { F16, BF16 };
+// F16 and BF16 run every product in that type; E4M3 runs the four layer products on e4m3 operands (the heads
+// and every 16-bit activation in bf16).
+enum class Prec { F16, BF16, E4M3 };
 
 struct TensorEntry {
     std::string dtype;
@@ -328,7 +371,14 @@ struct TensorEntry {
     size_t offset = 0, nbytes = 0;
 };
 
-// The weight file (mayfly/chess/cudanet/cudanet_spec.h:35-55; version 2 adds bf16 matrices), parsed,
+// The FP8 products of one layer: per product (qkv, out, ff1, ff2) the offset of its column scales in
+// Weights::colscale (input scale x weight scale of each output channel) and the reciprocal of its input scale.
+struct F8Layer {
+    size_t cs[4];
+    float inv_in[4];
+};
+
+// The weight file (mayfly/chess/cudanet/cudanet_spec.h:35-55; version 2 adds bf16 and e4m3 matrices), parsed,
 // checked (magic, version, numbers, every tensor with its dtype, shape, offset and size) and uploaded in one
 // device allocation (cudanet/weights.cpp:264 is the reference's reader).
 struct Weights {
@@ -338,10 +388,13 @@ struct Weights {
     void* base = nullptr;
     size_t bytes = 0;
     std::map<std::string, TensorEntry> t;
+    float* colscale = nullptr;      // e4m3 files: every product's column scales, one device allocation
+    std::vector<F8Layer> f8;
 
     ~Weights()
     {
         if (base) cudaFree(base);
+        if (colscale) cudaFree(colscale);
     }
 
     [[noreturn]] static void fail(const std::string& path, const std::string& why)
@@ -380,7 +433,8 @@ struct Weights {
         if (const JVal* p = h.get("precision")) prec_name = p->str;
         if (prec_name == "f16") prec = Prec::F16;
         else if (prec_name == "bf16") prec = Prec::BF16;
-        else fail(path, "precision " + prec_name + " is not supported by this build (f16, bf16)");
+        else if (prec_name == "e4m3") prec = Prec::E4M3;
+        else fail(path, "precision " + prec_name + " is not supported by this build (f16, bf16, e4m3)");
         check_arch(path);
 
         const JVal* ts = h.get("tensors");
@@ -409,7 +463,8 @@ struct Weights {
             size_t es = 0;
             if (te.dtype == "f16" || te.dtype == "bf16") es = 2;
             else if (te.dtype == "f32") es = 4;
-            else fail(path, nm->str + ": dtype " + te.dtype + " (f16, bf16 or f32 only)");
+            else if (te.dtype == "e4m3") es = 1;
+            else fail(path, nm->str + ": dtype " + te.dtype + " (f16, bf16, e4m3 or f32 only)");
             if (te.offset % 256) fail(path, nm->str + ": offset not 256-aligned");
             if (te.nbytes != count * es) fail(path, nm->str + ": nbytes does not match dtype and shape");
             if (start + te.offset + te.nbytes > raw.size()) fail(path, nm->str + ": runs past the end of the file");
@@ -420,6 +475,38 @@ struct Weights {
         bytes = (end + 255) / 256 * 256;
         RT(cudaMalloc(&base, bytes));
         RT(cudaMemcpy(base, raw.data() + start, std::min(bytes, raw.size() - start), cudaMemcpyHostToDevice));
+        if (prec == Prec::E4M3) derive_f8(path, raw, start);
+    }
+
+    // e4m3 files: W[o, :] ~= w_scale[o] * e4m3 and a product's input x ~= act_scale * e4m3 (static, per layer
+    // and product), so a product's f32 accumulator times act_scale * w_scale[o] is its value in column o.
+    void derive_f8(const std::string& path, const std::vector<char>& raw, size_t start)
+    {
+        auto host = [&](const std::string& name) {
+            const TensorEntry& e = t.at(name);
+            std::vector<float> v(e.nbytes / 4);
+            std::memcpy(v.data(), raw.data() + start + e.offset, e.nbytes);
+            for (float x : v)
+                if (!(x > 0.f) || !std::isfinite(x)) fail(path, name + ": scales must be positive and finite");
+            return v;
+        };
+        static const char* const kMat[4] = {"qkv_w", "out_w", "ff1_w", "ff2_w"};
+        std::vector<float> all;
+        for (int i = 0; i < a.layers; ++i) {
+            const std::string p = "L" + std::to_string(i) + ".";
+            const std::vector<float> act = host(p + "act_scale");
+            F8Layer fl;
+            for (int j = 0; j < 4; ++j) {
+                const std::vector<float> ws = host(p + kMat[j] + "_scale");
+                fl.cs[j] = all.size();
+                for (float w : ws) all.push_back(act[static_cast<size_t>(j)] * w);
+                while (all.size() % 64) all.push_back(0.f);   // every product's scales 256-byte aligned
+                fl.inv_in[j] = 1.0f / act[static_cast<size_t>(j)];
+            }
+            f8.push_back(fl);
+        }
+        RT(cudaMalloc(&colscale, all.size() * 4));
+        RT(cudaMemcpy(colscale, all.data(), all.size() * 4, cudaMemcpyHostToDevice));
     }
 
     void check_arch(const std::string& path) const
@@ -439,6 +526,7 @@ struct Weights {
     void check_tensors(const std::string& path) const
     {
         const std::string m16 = prec == Prec::F16 ? "f16" : "bf16";
+        const std::string mat = prec == Prec::E4M3 ? "e4m3" : m16;   // the layers' four matrices
         const long long d = a.d, ff = a.ff, mv = a.moves;
         std::vector<std::pair<std::string, std::pair<std::string, std::vector<long long>>>> want = {
             {"piece", {"f32", {13, d}}}, {"pos", {"f32", {64, d}}},   {"cls", {"f32", {d}}},
@@ -449,16 +537,23 @@ struct Weights {
             const std::string p = "L" + std::to_string(i) + ".";
             want.push_back({p + "n1_g", {"f32", {d}}});
             want.push_back({p + "n1_b", {"f32", {d}}});
-            want.push_back({p + "qkv_w", {m16, {3 * d, d}}});
+            want.push_back({p + "qkv_w", {mat, {3 * d, d}}});
             want.push_back({p + "qkv_b", {"f32", {3 * d}}});
-            want.push_back({p + "out_w", {m16, {d, d}}});
+            want.push_back({p + "out_w", {mat, {d, d}}});
             want.push_back({p + "out_b", {"f32", {d}}});
             want.push_back({p + "n2_g", {"f32", {d}}});
             want.push_back({p + "n2_b", {"f32", {d}}});
-            want.push_back({p + "ff1_w", {m16, {ff, d}}});
+            want.push_back({p + "ff1_w", {mat, {ff, d}}});
             want.push_back({p + "ff1_b", {"f32", {ff}}});
-            want.push_back({p + "ff2_w", {m16, {d, ff}}});
+            want.push_back({p + "ff2_w", {mat, {d, ff}}});
             want.push_back({p + "ff2_b", {"f32", {d}}});
+            if (prec == Prec::E4M3) {
+                want.push_back({p + "qkv_w_scale", {"f32", {3 * d}}});
+                want.push_back({p + "out_w_scale", {"f32", {d}}});
+                want.push_back({p + "ff1_w_scale", {"f32", {ff}}});
+                want.push_back({p + "ff2_w_scale", {"f32", {d}}});
+                want.push_back({p + "act_scale", {"f32", {4}}});   // inputs of qkv, out, ff1, ff2
+            }
         }
         for (const auto& w : want) {
             auto it = t.find(w.first);
@@ -508,6 +603,9 @@ static InLayout in_layout(int B, int wide)
 struct LayerW {
     const float *n1_g, *n1_b, *qkv_b, *out_b, *n2_g, *n2_b, *ff1_b, *ff2_b;
     const void *qkv_w, *out_w, *ff1_w, *ff2_w;
+    // e4m3 files: the products' column scales and the reciprocals of their static input scales
+    const float *qkv_cs = nullptr, *out_cs = nullptr, *ff1_cs = nullptr, *ff2_cs = nullptr;
+    float inv_qkv = 1.f, inv_out = 1.f, inv_ff1 = 1.f, inv_ff2 = 1.f;
 };
 
 class Net {
@@ -519,7 +617,10 @@ public:
 
     int max_batch() const { return max_batch_; }
     const std::string& fingerprint() const { return w_.fingerprint; }
-    const char* precision() const { return w_.prec == Prec::F16 ? "f16" : "bf16"; }
+    const char* precision() const
+    {
+        return w_.prec == Prec::F16 ? "f16" : w_.prec == Prec::BF16 ? "bf16" : "e4m3";
+    }
 
     void begin(int B, int wide, const int64_t* ids, const float* cast, const int64_t* hm, const int64_t* ep,
                const int64_t* I, const uint8_t* M, bool queued, bool want_logits);
@@ -529,6 +630,7 @@ public:
                          cudaStream_t s);
     void check(cudaStream_t s);
     std::vector<double> profile(int B, int reps);
+    std::vector<float> calibrate(int B, const int64_t* ids, const float* cast, const int64_t* hm, const int64_t* ep);
 
 private:
     int device_ = 0;
@@ -560,6 +662,9 @@ private:
     Fly fly_[2];
     int fly_n_ = 0;
 
+    // calibration: while set, the 16-bit pass records max |.| of the four products' inputs per layer here
+    unsigned int* amax_ = nullptr;
+
     // profiling marks
     bool prof_on_ = false;
     std::vector<cudaEvent_t> prof_ev_;
@@ -567,13 +672,17 @@ private:
     size_t prof_n_ = 0;
 
     uint32_t* err_word() const { return reinterpret_cast<uint32_t*>(d_out_); }
-    bool bf16() const { return w_.prec == Prec::BF16; }
+    bool bf16() const { return w_.prec != Prec::F16; }   // the 16-bit type is bf16 (also in e4m3 files)
+    bool f8() const { return w_.prec == Prec::E4M3; }
 
     void init(const std::string& path, int device);
     void release();
-    const CUtensorMap& wmap(const void* W, int N, int K, int bn);
-    void gemm(int epi, const CUtensorMap& ma, const void* W, int M, int N, int K, const float* bias, void* out,
-              int ldc, cudaStream_t s);
+    const CUtensorMap& wmap(const void* W, MapType type, int N, int K, int bn);
+    // out = epilogue(A W^T); W is e4m3 when w_f8 (A then is too, and ep carries the column scales)
+    void gemm(int epi, const CUtensorMap& ma, const void* W, bool w_f8, int M, int N, int K, const EpiArgs& ep,
+              void* out, int ldc, cudaStream_t s);
+    void amax(int slot, const void* p, size_t n, cudaStream_t s);
+    void forward_f8(int B, cudaStream_t s);
     // x += A W^T + bias, then h = LN(x; g, b), in one cluster kernel (gemm_ln.cuh)
     void gemm_resln(const CUtensorMap& ma, const void* W, int M, int K, const float* bias, const float* g,
                     const float* b, cudaStream_t s);
@@ -638,6 +747,17 @@ void Net::init(const std::string& path, int device)
             l.ff1_b = w_.ptr<float>(p + "ff1_b");
             l.ff2_w = w_.ptr(p + "ff2_w");
             l.ff2_b = w_.ptr<float>(p + "ff2_b");
+            if (f8()) {
+                const F8Layer& f = w_.f8[static_cast<size_t>(i)];
+                l.qkv_cs = w_.colscale + f.cs[0];
+                l.out_cs = w_.colscale + f.cs[1];
+                l.ff1_cs = w_.colscale + f.cs[2];
+                l.ff2_cs = w_.colscale + f.cs[3];
+                l.inv_qkv = f.inv_in[0];
+                l.inv_out = f.inv_in[1];
+                l.inv_ff1 = f.inv_in[2];
+                l.inv_ff2 = f.inv_in[3];
+            }
             L_.push_back(l);
         }
         const size_t d = a.d, ff = a.ff;
@@ -669,11 +789,12 @@ void Net::init(const std::string& path, int device)
             RT(cudaEventCreateWithFlags(&done_[s], cudaEventDisableTiming));
         }
         RT(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
-        const bool b = bf16();
-        map_h_ = operand_map(h_, b, d, rows_pad_, 128);
-        map_att_ = operand_map(att_, b, d, rows_pad_, 128);
-        map_ff_ = operand_map(ff_, b, ff, rows_pad_, 128);
-        map_cls_ = operand_map(cls_, b, d, cls_pad_, 128);
+        // the products' activation inputs: 16-bit, or e4m3 (the same buffers, 1 byte an element)
+        const MapType act = f8() ? MapType::U8 : type16(bf16());
+        map_h_ = operand_map(h_, act, d, rows_pad_, 128);
+        map_att_ = operand_map(att_, act, d, rows_pad_, 128);
+        map_ff_ = operand_map(ff_, act, ff, rows_pad_, 128);
+        map_cls_ = operand_map(cls_, type16(bf16()), d, cls_pad_, 128);
         const char* g = std::getenv("MAYFLY_CUDANET_GRAPH");
         use_graph_ = !(g && std::strcmp(g, "0") == 0);
         RT(cudaStreamSynchronize(stream_));
@@ -711,40 +832,52 @@ void Net::release()
     stream_ = nullptr;
 }
 
-const CUtensorMap& Net::wmap(const void* W, int N, int K, int bn)
+const CUtensorMap& Net::wmap(const void* W, MapType type, int N, int K, int bn)
 {
     const auto key = std::make_pair(W, bn);
     auto it = wmaps_.find(key);
     if (it != wmaps_.end()) return it->second;
-    return wmaps_[key] = operand_map(W, bf16(), static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+    return wmaps_[key] = operand_map(W, type, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
                                      static_cast<uint32_t>(bn));
 }
 
-void Net::gemm(int epi, const CUtensorMap& ma, const void* W, int M, int N, int K, const float* bias, void* out,
-               int ldc, cudaStream_t s)
+void Net::gemm(int epi, const CUtensorMap& ma, const void* W, bool w_f8, int M, int N, int K, const EpiArgs& ep,
+               void* out, int ldc, cudaStream_t s)
 {
     const int bn = pick_bn(M, N, K, epi, num_sms_);
-    const CUtensorMap& mb = wmap(W, N, K, static_cast<int>(w_box_rows(bn)));
+    const CUtensorMap& mb = wmap(W, w_f8 ? MapType::U8 : type16(bf16()), N, K, static_cast<int>(w_box_rows(bn)));
     const auto okey = std::make_tuple(static_cast<const void*>(out), epi, M, N);
     auto it = omaps_.find(okey);
-    if (it == omaps_.end()) it = omaps_.emplace(okey, output_map(out, epi, bf16(), M, N, ldc)).first;
-    if (bf16())
-        launch_gemm<__nv_bfloat16>(epi, bn, ma, mb, it->second, M, N, K, bias, err_word(), num_sms_, s);
+    if (it == omaps_.end()) it = omaps_.emplace(okey, output_map(out, epi, type16(bf16()), M, N, ldc)).first;
+    if (w_f8)
+        launch_gemm<__nv_fp8_e4m3, __nv_bfloat16>(epi, bn, ma, mb, it->second, M, N, K, ep, err_word(), num_sms_, s);
+    else if (bf16())
+        launch_gemm<__nv_bfloat16, __nv_bfloat16>(epi, bn, ma, mb, it->second, M, N, K, ep, err_word(), num_sms_, s);
     else
-        launch_gemm<__half>(epi, bn, ma, mb, it->second, M, N, K, bias, err_word(), num_sms_, s);
+        launch_gemm<__half, __half>(epi, bn, ma, mb, it->second, M, N, K, ep, err_word(), num_sms_, s);
+}
+
+void Net::amax(int slot, const void* p, size_t n, cudaStream_t s)
+{
+    if (!amax_) return;
+    if (bf16())
+        absmax_kernel<__nv_bfloat16><<<4 * num_sms_, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(p), n, amax_ + slot);
+    else
+        absmax_kernel<__half><<<4 * num_sms_, 256, 0, s>>>(static_cast<const __half*>(p), n, amax_ + slot);
+    RT(cudaGetLastError());
 }
 
 void Net::gemm_resln(const CUtensorMap& ma, const void* W, int M, int K, const float* bias, const float* g,
                      const float* b, cudaStream_t s)
 {
     const int d = w_.a.d;
-    const CUtensorMap& mb = wmap(W, d, K, 256);
+    const CUtensorMap& mb = wmap(W, type16(bf16()), d, K, 256);
     const auto xkey = std::make_tuple(static_cast<const void*>(x_), static_cast<int>(kEpiResidual), M, d);
     auto ix = omaps_.find(xkey);
-    if (ix == omaps_.end()) ix = omaps_.emplace(xkey, output_map(x_, kEpiResidual, bf16(), M, d, d)).first;
+    if (ix == omaps_.end()) ix = omaps_.emplace(xkey, output_map(x_, kEpiResidual, type16(bf16()), M, d, d)).first;
     const auto hkey = std::make_tuple(static_cast<const void*>(h_), static_cast<int>(kEpiBias), M, d);
     auto ih = omaps_.find(hkey);
-    if (ih == omaps_.end()) ih = omaps_.emplace(hkey, output_map(h_, kEpiBias, bf16(), M, d, d)).first;
+    if (ih == omaps_.end()) ih = omaps_.emplace(hkey, output_map(h_, kEpiBias, type16(bf16()), M, d, d)).first;
     if (bf16())
         launch_gemm_resln<__nv_bfloat16>(ma, mb, ix->second, ih->second, M, d, K, bias, g, b, err_word(), s);
     else
@@ -777,78 +910,128 @@ void Net::mark(int op, cudaStream_t s)
     ++prof_n_;
 }
 
+// The embedding fused with layer 0's first LayerNorm: x (f32) and h (T: 16-bit, or e4m3 of h * mul).
+template <typename T>
+static void launch_embed_ln(const Weights& w, const LayerW& l0, const uint8_t* d_in, int B, float* x, T* h,
+                            float mul, cudaStream_t s)
+{
+    const int rows = B * kTokens;
+    const InLayout lay = in_layout(B, 1);
+    const int64_t* ids = reinterpret_cast<const int64_t*>(d_in + lay.ids);
+    const int64_t* hm = reinterpret_cast<const int64_t*>(d_in + lay.hm);
+    const int64_t* ep = reinterpret_cast<const int64_t*>(d_in + lay.ep);
+    const float* cast = reinterpret_cast<const float*>(d_in + lay.cast);
+    const dim3 grid((rows + 7) / 8), block(256);
+    const float *piece = w.ptr<float>("piece"), *pos = w.ptr<float>("pos"), *cls = w.ptr<float>("cls"),
+                *cast_w = w.ptr<float>("cast_w"), *cast_b = w.ptr<float>("cast_b"), *hm_emb = w.ptr<float>("hm"),
+                *ep_mark = w.ptr<float>("ep_mark");
+    switch (w.a.d) {
+        case 256:
+            embed_ln_kernel<T, 2><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
+                                                          ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
+            break;
+        case 512:
+            embed_ln_kernel<T, 4><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
+                                                          ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
+            break;
+        default:
+            embed_ln_kernel<T, 8><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
+                                                          ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
+    }
+    RT(cudaGetLastError());
+}
+
 template <typename T> void Net::forward_t(int B, cudaStream_t s)
 {
     const Arch& a = w_.a;
     const int rows = B * kTokens, d = a.d, ff = a.ff;
-    const InLayout lay = in_layout(B, 1);
-    const int64_t* ids = reinterpret_cast<const int64_t*>(d_in_ + lay.ids);
-    const int64_t* hm = reinterpret_cast<const int64_t*>(d_in_ + lay.hm);
-    const int64_t* ep = reinterpret_cast<const int64_t*>(d_in_ + lay.ep);
-    const float* cast = reinterpret_cast<const float*>(d_in_ + lay.cast);
+    const size_t nd = static_cast<size_t>(rows) * d, nf = static_cast<size_t>(rows) * ff;
     T* h = static_cast<T*>(h_);
     mark(kPEmbed, s);
-    {
-        const dim3 grid((rows + 7) / 8), block(256);
-        const float* args_f[] = {w_.ptr<float>("piece"), w_.ptr<float>("pos"), w_.ptr<float>("cls"),
-                                 w_.ptr<float>("cast_w"), w_.ptr<float>("cast_b"), w_.ptr<float>("hm"),
-                                 w_.ptr<float>("ep_mark")};
-        switch (d) {
-            case 256:
-                embed_ln_kernel<T, 2><<<grid, block, 0, s>>>(ids, cast, hm, ep, args_f[0], args_f[1], args_f[2],
-                                                              args_f[3], args_f[4], args_f[5], args_f[6], L_[0].n1_g,
-                                                              L_[0].n1_b, x_, h, rows, 1e-5f);
-                break;
-            case 512:
-                embed_ln_kernel<T, 4><<<grid, block, 0, s>>>(ids, cast, hm, ep, args_f[0], args_f[1], args_f[2],
-                                                              args_f[3], args_f[4], args_f[5], args_f[6], L_[0].n1_g,
-                                                              L_[0].n1_b, x_, h, rows, 1e-5f);
-                break;
-            default:
-                embed_ln_kernel<T, 8><<<grid, block, 0, s>>>(ids, cast, hm, ep, args_f[0], args_f[1], args_f[2],
-                                                              args_f[3], args_f[4], args_f[5], args_f[6], L_[0].n1_g,
-                                                              L_[0].n1_b, x_, h, rows, 1e-5f);
-        }
-        RT(cudaGetLastError());
-    }
-    const bool fuse = fuse_ln();
+    launch_embed_ln<T>(w_, L_[0], d_in_, B, x_, h, 1.f, s);
+    const bool fuse = fuse_ln() && !amax_;
     for (int i = 0; i < a.layers; ++i) {
         const LayerW& l = L_[static_cast<size_t>(i)];
         const bool last = i + 1 == a.layers;
         mark(kPLn1, s);
-        if (i > 0 && !fuse) launch_layernorm<T>(x_, l.n1_g, l.n1_b, h, rows, d, 1, s);
+        if (i > 0 && !fuse) launch_layernorm<T>(x_, l.n1_g, l.n1_b, h, rows, d, 1, 1.f, s);
+        amax(4 * i + 0, h, nd, s);
         mark(kPQkv, s);
-        gemm(kEpiBias, map_h_, l.qkv_w, rows, 3 * d, d, l.qkv_b, qkv_, 3 * d, s);
+        gemm(kEpiBias, map_h_, l.qkv_w, false, rows, 3 * d, d, EpiArgs{l.qkv_b, nullptr, 1.f}, qkv_, 3 * d, s);
         mark(kPAtt, s);
-        launch_attention<T>(static_cast<const T*>(qkv_), static_cast<T*>(att_), B, d, a.heads, s);
+        launch_attention<T, T>(static_cast<const T*>(qkv_), static_cast<T*>(att_), B, d, a.heads, 1.f, s);
+        amax(4 * i + 1, att_, nd, s);
         mark(kPOut, s);
         if (fuse) {
             gemm_resln(map_att_, l.out_w, rows, d, l.out_b, l.n2_g, l.n2_b, s);   // x += out; h = LN2(x)
         } else {
-            gemm(kEpiResidual, map_att_, l.out_w, rows, d, d, l.out_b, x_, d, s);
+            gemm(kEpiResidual, map_att_, l.out_w, false, rows, d, d, EpiArgs{l.out_b, nullptr, 1.f}, x_, d, s);
             mark(kPLn2, s);
-            launch_layernorm<T>(x_, l.n2_g, l.n2_b, h, rows, d, 1, s);
+            launch_layernorm<T>(x_, l.n2_g, l.n2_b, h, rows, d, 1, 1.f, s);
         }
+        amax(4 * i + 2, h, nd, s);
         mark(kPFf1, s);
-        gemm(kEpiBiasGelu, map_h_, l.ff1_w, rows, ff, d, l.ff1_b, ff_, ff, s);
+        gemm(kEpiBiasGelu, map_h_, l.ff1_w, false, rows, ff, d, EpiArgs{l.ff1_b, nullptr, 1.f}, ff_, ff, s);
+        amax(4 * i + 3, ff_, nf, s);
         mark(kPFf2, s);
         if (fuse && !last) {
             const LayerW& n = L_[static_cast<size_t>(i + 1)];
             gemm_resln(map_ff_, l.ff2_w, rows, ff, l.ff2_b, n.n1_g, n.n1_b, s);   // x += ff; h = next LN1(x)
         } else {
-            gemm(kEpiResidual, map_ff_, l.ff2_w, rows, d, ff, l.ff2_b, x_, d, s);
+            gemm(kEpiResidual, map_ff_, l.ff2_w, false, rows, d, ff, EpiArgs{l.ff2_b, nullptr, 1.f}, x_, d, s);
         }
     }
     mark(kPCls, s);
-    launch_layernorm<T>(x_, w_.ptr<float>("ln_g"), w_.ptr<float>("ln_b"), static_cast<T*>(cls_), B, d, kTokens, s);
+    launch_layernorm<T>(x_, w_.ptr<float>("ln_g"), w_.ptr<float>("ln_b"), static_cast<T*>(cls_), B, d, kTokens, 1.f,
+                        s);
     mark(kPHeads, s);
-    gemm(kEpiF32, map_cls_, w_.ptr("heads_w"), B, 2 * a.moves, d, w_.ptr<float>("heads_b"), logits_, 2 * a.moves, s);
+    gemm(kEpiF32, map_cls_, w_.ptr("heads_w"), false, B, 2 * a.moves, d,
+         EpiArgs{w_.ptr<float>("heads_b"), nullptr, 1.f}, logits_, 2 * a.moves, s);
+    mark(kPHeads, s);
+}
+
+// The FP8 pass: each layer product's input is written as e4m3 of x / act_scale by its producer (the
+// LayerNorms, attention, ff1's GELU epilogue) and the product scales its f32 accumulator per column; q, k, v,
+// the residual stream and the heads stay bf16 / f32 as in the 16-bit pass.
+void Net::forward_f8(int B, cudaStream_t s)
+{
+    using T = __nv_bfloat16;
+    using F8 = __nv_fp8_e4m3;
+    const Arch& a = w_.a;
+    const int rows = B * kTokens, d = a.d, ff = a.ff;
+    F8* h = static_cast<F8*>(h_);
+    mark(kPEmbed, s);
+    launch_embed_ln<F8>(w_, L_[0], d_in_, B, x_, h, L_[0].inv_qkv, s);
+    for (int i = 0; i < a.layers; ++i) {
+        const LayerW& l = L_[static_cast<size_t>(i)];
+        mark(kPLn1, s);
+        if (i > 0) launch_layernorm<F8>(x_, l.n1_g, l.n1_b, h, rows, d, 1, l.inv_qkv, s);
+        mark(kPQkv, s);
+        gemm(kEpiBias, map_h_, l.qkv_w, true, rows, 3 * d, d, EpiArgs{l.qkv_b, l.qkv_cs, 1.f}, qkv_, 3 * d, s);
+        mark(kPAtt, s);
+        launch_attention<T, F8>(static_cast<const T*>(qkv_), static_cast<F8*>(att_), B, d, a.heads, l.inv_out, s);
+        mark(kPOut, s);
+        gemm(kEpiResidual, map_att_, l.out_w, true, rows, d, d, EpiArgs{l.out_b, l.out_cs, 1.f}, x_, d, s);
+        mark(kPLn2, s);
+        launch_layernorm<F8>(x_, l.n2_g, l.n2_b, h, rows, d, 1, l.inv_ff1, s);
+        mark(kPFf1, s);
+        gemm(kEpiGeluE4m3, map_h_, l.ff1_w, true, rows, ff, d, EpiArgs{l.ff1_b, l.ff1_cs, l.inv_ff2}, ff_, ff, s);
+        mark(kPFf2, s);
+        gemm(kEpiResidual, map_ff_, l.ff2_w, true, rows, d, ff, EpiArgs{l.ff2_b, l.ff2_cs, 1.f}, x_, d, s);
+    }
+    mark(kPCls, s);
+    launch_layernorm<T>(x_, w_.ptr<float>("ln_g"), w_.ptr<float>("ln_b"), static_cast<T*>(cls_), B, d, kTokens, 1.f,
+                        s);
+    mark(kPHeads, s);
+    gemm(kEpiF32, map_cls_, w_.ptr("heads_w"), false, B, 2 * a.moves, d,
+         EpiArgs{w_.ptr<float>("heads_b"), nullptr, 1.f}, logits_, 2 * a.moves, s);
     mark(kPHeads, s);
 }
 
 void Net::forward_kernels(int B, cudaStream_t s)
 {
-    if (bf16()) forward_t<__nv_bfloat16>(B, s);
+    if (f8()) forward_f8(B, s);
+    else if (bf16()) forward_t<__nv_bfloat16>(B, s);
     else forward_t<__half>(B, s);
 }
 
@@ -1001,6 +1184,45 @@ void Net::check(cudaStream_t s)
         RT(cudaMemset(d_out_, 0, 4));
         throw std::runtime_error(std::string("cudanet_b200: device error: ") + err_site_name(errw >> 8));
     }
+}
+
+// Runs the 16-bit pass eagerly on B positions and returns, per layer, max |.| of the inputs of its four
+// products (qkv, out, ff1, ff2): the ranges an e4m3 weight file's static input scales are set from.
+std::vector<float> Net::calibrate(int B, const int64_t* ids, const float* cast, const int64_t* hm, const int64_t* ep)
+{
+    check_batch(B);
+    if (!ids || !cast || !hm || !ep) throw std::runtime_error("cudanet_calibrate: a null input pointer");
+    if (f8()) throw std::runtime_error("cudanet_calibrate: needs a 16-bit weight file (this one is e4m3)");
+    if (fly_n_) throw std::runtime_error("cudanet_calibrate: a batch is in flight");
+    RT(cudaSetDevice(device_));
+    const size_t b = static_cast<size_t>(B);
+    const InLayout lay = in_layout(B, 1);
+    uint8_t* hin = h_in_[0];
+    std::memcpy(hin + lay.ids, ids, 8 * b * 64);
+    std::memcpy(hin + lay.hm, hm, 8 * b);
+    std::memcpy(hin + lay.ep, ep, 8 * b);
+    std::memcpy(hin + lay.cast, cast, 4 * b * 4);
+    RT(cudaMemcpyAsync(d_in_, hin, lay.I, cudaMemcpyHostToDevice, stream_));
+    const size_t n = 4 * static_cast<size_t>(w_.a.layers);
+    RT(cudaMalloc(&amax_, n * sizeof(unsigned int)));
+    std::vector<unsigned int> bits(n, 0);
+    try {
+        RT(cudaMemsetAsync(amax_, 0, n * sizeof(unsigned int), stream_));
+        forward_kernels(B, stream_);
+        RT(cudaMemcpyAsync(bits.data(), amax_, n * sizeof(unsigned int), cudaMemcpyDeviceToHost, stream_));
+        RT(cudaStreamSynchronize(stream_));
+    } catch (...) {
+        cudaStreamSynchronize(stream_);
+        cudaFree(amax_);
+        amax_ = nullptr;
+        throw;
+    }
+    cudaFree(amax_);
+    amax_ = nullptr;
+    check(nullptr);
+    std::vector<float> out(n);
+    std::memcpy(out.data(), bits.data(), n * sizeof(float));
+    return out;
 }
 
 std::vector<double> Net::profile(int B, int reps)
@@ -1257,6 +1479,22 @@ CUDANET_API int cudanet_check(void* handle, void* stream, char* err, int err_len
     });
 }
 
+CUDANET_API int cudanet_calibrate(void* handle, int B, const int64_t* ids, const float* cast, const int64_t* hm,
+                                  const int64_t* ep, float* amax, int n, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_calibrate: unknown exception", [&] {
+        if (!handle || !amax) throw std::runtime_error("cudanet_calibrate: null handle or output");
+        Net* net = static_cast<Net*>(handle);
+        std::lock_guard<std::mutex> lock(net->mu);
+        const std::vector<float> got = net->calibrate(B, ids, cast, hm, ep);
+        if (n < static_cast<int>(got.size()))
+            throw std::runtime_error("cudanet_calibrate: the output holds " + std::to_string(n) + " floats, needs " +
+                                     std::to_string(got.size()));
+        std::memcpy(amax, got.data(), got.size() * sizeof(float));
+        return static_cast<int>(got.size());
+    });
+}
+
 CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const void* W, const float* bias, void* C,
                                int M, int N, int K, int ldc, void* stream, char* err, int err_len)
 {
@@ -1276,17 +1514,19 @@ CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const 
         if (ldc < N) throw std::runtime_error("cudanet_k_gemm: ldc < N");
         const bool b16 = dtype == 1;
         if (epi < 0 || epi > 3) throw std::runtime_error("cudanet_k_gemm: epi must be 0..3");
-        const CUtensorMap ma = mf::operand_map(A, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
-        const CUtensorMap mb = mf::operand_map(W, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+        const mf::MapType t = mf::type16(b16);
+        const CUtensorMap ma = mf::operand_map(A, t, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
+        const CUtensorMap mb = mf::operand_map(W, t, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
                                                mf::w_box_rows(bn));
-        const CUtensorMap mc = mf::output_map(C, epi, b16, M, N, ldc);
+        const CUtensorMap mc = mf::output_map(C, epi, t, M, N, ldc);
+        const mf::EpiArgs ep{bias, nullptr, 1.f};
         uint32_t* errw = nullptr;
         mf::RT(cudaMalloc(&errw, 4));
         mf::RT(cudaMemset(errw, 0, 4));
         const cudaStream_t s = static_cast<cudaStream_t>(stream);
         try {
-            if (b16) mf::launch_gemm<__nv_bfloat16>(epi, bn, ma, mb, mc, M, N, K, bias, errw, sms, s);
-            else mf::launch_gemm<__half>(epi, bn, ma, mb, mc, M, N, K, bias, errw, sms, s);
+            if (b16) mf::launch_gemm<__nv_bfloat16, __nv_bfloat16>(epi, bn, ma, mb, mc, M, N, K, ep, errw, sms, s);
+            else mf::launch_gemm<__half, __half>(epi, bn, ma, mb, mc, M, N, K, ep, errw, sms, s);
             mf::RT(cudaStreamSynchronize(s));
         } catch (...) {
             cudaFree(errw);
@@ -1323,15 +1563,17 @@ CUDANET_API int cudanet_k_gemm_noalloc(int dtype, int epi, int bn, const void* A
         if ((ldc * ob) % 16 || (N * ob) % 16)
             throw std::runtime_error("cudanet_k_gemm_noalloc: C's rows and row pitch must be multiples of 16 bytes");
         const bool b16 = dtype == 1;
-        const CUtensorMap ma = mf::operand_map(A, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
-        const CUtensorMap mb = mf::operand_map(W, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+        const mf::MapType t = mf::type16(b16);
+        const CUtensorMap ma = mf::operand_map(A, t, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
+        const CUtensorMap mb = mf::operand_map(W, t, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
                                                mf::w_box_rows(bn));
-        const CUtensorMap mc = mf::output_map(C, epi, b16, M, N, ldc);
+        const CUtensorMap mc = mf::output_map(C, epi, t, M, N, ldc);
+        const mf::EpiArgs ep{bias, nullptr, 1.f};
         const cudaStream_t s = static_cast<cudaStream_t>(stream);
         // the word keeps the last call's value: clear it for this call, in stream order
         mf::RT(cudaMemsetAsync(errw, 0, mf::kNoAllocBytesPerCall, s));
-        if (b16) mf::launch_gemm<__nv_bfloat16>(epi, bn, ma, mb, mc, M, N, K, bias, errw, sms, s);
-        else mf::launch_gemm<__half>(epi, bn, ma, mb, mc, M, N, K, bias, errw, sms, s);
+        if (b16) mf::launch_gemm<__nv_bfloat16, __nv_bfloat16>(epi, bn, ma, mb, mc, M, N, K, ep, errw, sms, s);
+        else mf::launch_gemm<__half, __half>(epi, bn, ma, mb, mc, M, N, K, ep, errw, sms, s);
         uint32_t e = 0;
         mf::RT(cudaMemcpyAsync(&e, errw, sizeof e, cudaMemcpyDeviceToHost, s));
         mf::RT(cudaStreamSynchronize(s));
@@ -1351,10 +1593,11 @@ CUDANET_API int cudanet_k_gemm_resln(int dtype, const void* A, const void* W, co
         if ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(H)) & 15)
             throw std::runtime_error("cudanet_k_gemm_resln: X and H must be 16-byte aligned");
         const bool b16 = dtype == 1;
-        const CUtensorMap ma = mf::operand_map(A, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
-        const CUtensorMap mb = mf::operand_map(W, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 256);
-        const CUtensorMap mx = mf::output_map(X, mf::kEpiResidual, b16, M, N, N);
-        const CUtensorMap mh = mf::output_map(H, mf::kEpiBias, b16, M, N, N);
+        const mf::MapType t = mf::type16(b16);
+        const CUtensorMap ma = mf::operand_map(A, t, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
+        const CUtensorMap mb = mf::operand_map(W, t, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 256);
+        const CUtensorMap mx = mf::output_map(X, mf::kEpiResidual, t, M, N, N);
+        const CUtensorMap mh = mf::output_map(H, mf::kEpiBias, t, M, N, N);
         uint32_t* errw = nullptr;
         mf::RT(cudaMalloc(&errw, 4));
         mf::RT(cudaMemset(errw, 0, 4));
@@ -1382,10 +1625,11 @@ CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B
         const cudaStream_t s = static_cast<cudaStream_t>(stream);
         if (B < 1 || heads < 1 || d % heads) throw std::runtime_error("cudanet_k_attention: bad sizes");
         if (dtype == 1)
-            mf::launch_attention<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(qkv),
-                                                static_cast<__nv_bfloat16*>(att), B, d, heads, s);
+            mf::launch_attention<__nv_bfloat16, __nv_bfloat16>(static_cast<const __nv_bfloat16*>(qkv),
+                                                               static_cast<__nv_bfloat16*>(att), B, d, heads, 1.f, s);
         else if (dtype == 0)
-            mf::launch_attention<__half>(static_cast<const __half*>(qkv), static_cast<__half*>(att), B, d, heads, s);
+            mf::launch_attention<__half, __half>(static_cast<const __half*>(qkv), static_cast<__half*>(att), B, d,
+                                                 heads, 1.f, s);
         else
             throw std::runtime_error("cudanet_k_attention: dtype must be 0 (f16) or 1 (bf16)");
         mf::RT(cudaStreamSynchronize(s));
@@ -1399,9 +1643,83 @@ CUDANET_API int cudanet_k_layernorm(int dtype, const float* x, const float* g, c
     return mf::guarded(err, err_len, "cudanet_k_layernorm: unknown exception", [&] {
         const cudaStream_t s = static_cast<cudaStream_t>(stream);
         if (n < 1 || row_stride < 1) throw std::runtime_error("cudanet_k_layernorm: bad sizes");
-        if (dtype == 1) mf::launch_layernorm<__nv_bfloat16>(x, g, b, static_cast<__nv_bfloat16*>(h), n, d, row_stride, s);
-        else if (dtype == 0) mf::launch_layernorm<__half>(x, g, b, static_cast<__half*>(h), n, d, row_stride, s);
-        else throw std::runtime_error("cudanet_k_layernorm: dtype must be 0 (f16) or 1 (bf16)");
+        if (dtype == 1)
+            mf::launch_layernorm<__nv_bfloat16>(x, g, b, static_cast<__nv_bfloat16*>(h), n, d, row_stride, 1.f, s);
+        else if (dtype == 0)
+            mf::launch_layernorm<__half>(x, g, b, static_cast<__half*>(h), n, d, row_stride, 1.f, s);
+        else
+            throw std::runtime_error("cudanet_k_layernorm: dtype must be 0 (f16) or 1 (bf16)");
+        mf::RT(cudaStreamSynchronize(s));
+        return 0;
+    });
+}
+
+// ------------------------------------------------------------------------------------------------ FP8 pieces
+CUDANET_API int cudanet_k_gemm_f8(int epi, int bn, const void* A, const void* W, const float* colscale,
+                                  const float* bias, float out_scale_inv, void* C, int M, int N, int K, int ldc,
+                                  void* stream, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_k_gemm_f8: unknown exception", [&] {
+        if (epi != mf::kEpiBias && epi != mf::kEpiResidual && epi != mf::kEpiF32 && epi != mf::kEpiGeluE4m3)
+            throw std::runtime_error("cudanet_k_gemm_f8: epi must be 0 (bf16 out), 2 (residual), 3 (f32) or 4 "
+                                     "(GELU, e4m3 out)");
+        if (M < 1 || N < 1 || K < 128) throw std::runtime_error("cudanet_k_gemm_f8: bad sizes");
+        int dev = 0;
+        mf::RT(cudaGetDevice(&dev));
+        int sms = 0;
+        mf::RT(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        if (bn == 0) bn = mf::pick_bn(M, N, K, epi, sms);
+        if ((reinterpret_cast<uintptr_t>(C) | reinterpret_cast<uintptr_t>(bias) |
+             reinterpret_cast<uintptr_t>(colscale)) & 15)
+            throw std::runtime_error("cudanet_k_gemm_f8: C, bias and colscale must be 16-byte aligned");
+        const long long ob = (epi == mf::kEpiResidual || epi == mf::kEpiF32) ? 4 : epi == mf::kEpiGeluE4m3 ? 1 : 2;
+        if ((ldc * ob) % 16 || (N * ob) % 16)
+            throw std::runtime_error("cudanet_k_gemm_f8: C's rows and row pitch must be multiples of 16 bytes");
+        if (ldc < N) throw std::runtime_error("cudanet_k_gemm_f8: ldc < N");
+        const CUtensorMap ma = mf::operand_map(A, mf::MapType::U8, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
+        const CUtensorMap mb = mf::operand_map(W, mf::MapType::U8, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                                               mf::w_box_rows(bn));
+        const CUtensorMap mc = mf::output_map(C, epi, mf::MapType::BF16, M, N, ldc);
+        const mf::EpiArgs ep{bias, colscale, out_scale_inv};
+        uint32_t* errw = nullptr;
+        mf::RT(cudaMalloc(&errw, 4));
+        mf::RT(cudaMemset(errw, 0, 4));
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        try {
+            mf::launch_gemm<__nv_fp8_e4m3, __nv_bfloat16>(epi, bn, ma, mb, mc, M, N, K, ep, errw, sms, s);
+            mf::RT(cudaStreamSynchronize(s));
+        } catch (...) {
+            cudaFree(errw);
+            throw;
+        }
+        uint32_t e = 0;
+        mf::RT(cudaMemcpy(&e, errw, 4, cudaMemcpyDeviceToHost));
+        cudaFree(errw);
+        if (e) throw std::runtime_error(std::string("cudanet_k_gemm_f8: device error: ") + mf::err_site_name(e >> 8));
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_k_attention_f8(const void* qkv, void* att, int B, int d, int heads, float mul, void* stream,
+                                       char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_k_attention_f8: unknown exception", [&] {
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (B < 1 || heads < 1 || d % heads || d % 16) throw std::runtime_error("cudanet_k_attention_f8: bad sizes");
+        mf::launch_attention<__nv_bfloat16, __nv_fp8_e4m3>(static_cast<const __nv_bfloat16*>(qkv),
+                                                           static_cast<__nv_fp8_e4m3*>(att), B, d, heads, mul, s);
+        mf::RT(cudaStreamSynchronize(s));
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_k_layernorm_f8(const float* x, const float* g, const float* b, void* h, int n, int d,
+                                       int row_stride, float mul, void* stream, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_k_layernorm_f8: unknown exception", [&] {
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (n < 1 || row_stride < 1) throw std::runtime_error("cudanet_k_layernorm_f8: bad sizes");
+        mf::launch_layernorm<__nv_fp8_e4m3>(x, g, b, static_cast<__nv_fp8_e4m3*>(h), n, d, row_stride, mul, s);
         mf::RT(cudaStreamSynchronize(s));
         return 0;
     });

@@ -271,6 +271,18 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, 
         : "memory");
 }
 
+// The same for 8-bit float inputs (kind::f8f6f4, e4m3 x e4m3), issued by the leader CTA only.
+__device__ __forceinline__ void umma_f8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive once on a barrier of either CTA of the pair when the pair MMAs this thread issued have completed.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr)
 {

@@ -5,6 +5,9 @@
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
+#include <type_traits>
 
 #include "gemm.cuh"
 
@@ -28,19 +31,27 @@ __device__ __forceinline__ float warp_max(float v)
     return v;
 }
 
-template <typename T> __device__ __forceinline__ void store4(T* p, float a, float b, float c, float d)
+template <typename T> constexpr bool is_e4m3 = std::is_same<T, __nv_fp8_e4m3>::value;
+
+// Four values to p in the activation type T: 16-bit (8 bytes), or e4m3 (4 bytes) after multiplying by `mul`
+// (the reciprocal of the consumer's static input scale; the 16-bit types ignore it).
+template <typename T> __device__ __forceinline__ void store4(T* p, float a, float b, float c, float d, float mul)
 {
-    uint2 q;
-    q.x = pack2<T>(a, b);
-    q.y = pack2<T>(c, d);
-    *reinterpret_cast<uint2*>(p) = q;
+    if constexpr (is_e4m3<T>) {
+        *reinterpret_cast<uint32_t*>(p) = pack_e4m3x4(a * mul, b * mul, c * mul, d * mul);
+    } else {
+        uint2 q;
+        q.x = pack2<T>(a, b);
+        q.y = pack2<T>(c, d);
+        *reinterpret_cast<uint2*>(p) = q;
+    }
 }
 
 // LayerNorm of one row held by one warp (V float4 per lane, lane owns float4s lane, lane+32, ...): biased
 // variance from a second pass over (x - mean) in registers, rstd = rsqrt(var + eps), as F.layer_norm in fp32.
 template <typename T, int V>
 __device__ __forceinline__ void ln_row_store(const float4 (&v)[V], int d, const float* __restrict__ g,
-                                             const float* __restrict__ b, T* __restrict__ y, float eps)
+                                             const float* __restrict__ b, T* __restrict__ y, float eps, float mul)
 {
     const int lane = threadIdx.x & 31;
     float s = 0.f;
@@ -61,7 +72,7 @@ __device__ __forceinline__ void ln_row_store(const float4 (&v)[V], int d, const 
         const int c4 = lane + 32 * i;
         const float4 gg = __ldg(g4 + c4), bb = __ldg(b4 + c4);
         store4<T>(y + 4 * c4, (v[i].x - mean) * rstd * gg.x + bb.x, (v[i].y - mean) * rstd * gg.y + bb.y,
-                  (v[i].z - mean) * rstd * gg.z + bb.z, (v[i].w - mean) * rstd * gg.w + bb.w);
+                  (v[i].z - mean) * rstd * gg.z + bb.z, (v[i].w - mean) * rstd * gg.w + bb.w, mul);
     }
 }
 
@@ -71,14 +82,14 @@ __device__ __forceinline__ void ln_row_store(const float4 (&v)[V], int d, const 
 //   x[b*65+1+s] = piece[ids[b*64+s]] + pos[s] (+ ep_mark when ep[b] > 0 and s == ep[b] - 1)
 //   h = LN(x; g, beta)
 // One warp per row, rows = B * 65. ids and hm are clamped to their tables (a bad input cannot read out of
-// bounds), as the reference kernel does. d = 128 * V.
+// bounds), as the reference kernel does. d = 128 * V. h is 16-bit, or e4m3 of h * mul (the FP8 path).
 template <typename T, int V>
 __global__ void __launch_bounds__(256) embed_ln_kernel(
     const int64_t* __restrict__ ids, const float* __restrict__ cast, const int64_t* __restrict__ hm,
     const int64_t* __restrict__ ep, const float* __restrict__ piece, const float* __restrict__ pos,
     const float* __restrict__ cls, const float* __restrict__ cast_w, const float* __restrict__ cast_b,
     const float* __restrict__ hm_emb, const float* __restrict__ ep_mark, const float* __restrict__ g,
-    const float* __restrict__ beta, float* __restrict__ x, T* __restrict__ h, int rows, float eps)
+    const float* __restrict__ beta, float* __restrict__ x, T* __restrict__ h, int rows, float eps, float mul)
 {
     constexpr int d = 128 * V;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -130,16 +141,17 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(
     float4* xr = reinterpret_cast<float4*>(x + (size_t)row * d);
 #pragma unroll
     for (int i = 0; i < V; ++i) xr[lane + 32 * i] = v[i];
-    ln_row_store<T, V>(v, d, g, beta, h + (size_t)row * d, eps);
+    ln_row_store<T, V>(v, d, g, beta, h + (size_t)row * d, eps, mul);
 }
 
 // ------------------------------------------------------------------------------------------------ LayerNorm
 // h[r] = LN(x[r]) for rows r = row0 + i * row_stride, i < n (row_stride 65 picks the CLS rows for the final
 // norm, chess_net.py:194 / cudanet/kernels_heads.cu:64-86). Output rows are dense: h row i. One warp per row.
+// h is 16-bit, or e4m3 of h * mul (the FP8 path).
 template <typename T, int V>
 __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
                                                         const float* __restrict__ b, T* __restrict__ h, int n,
-                                                        int row_stride, float eps)
+                                                        int row_stride, float eps, float mul)
 {
     constexpr int d = 128 * V;
     const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -149,7 +161,7 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
     float4 v[V];
 #pragma unroll
     for (int k = 0; k < V; ++k) v[k] = xr[lane + 32 * k];
-    ln_row_store<T, V>(v, d, g, b, h + (size_t)i * d, eps);
+    ln_row_store<T, V>(v, d, g, b, h + (size_t)i * d, eps, mul);
 }
 
 // ------------------------------------------------------------------------------------------------ attention
@@ -162,6 +174,7 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
 // ldmatrix rows fall in distinct banks); S = Q K^T and O = P V run on mma.sync m16n8k16 with f32 accumulation;
 // the softmax runs on the S fragments in registers (row max and sum across the 4 lanes of a quad by shuffles);
 // P is rounded to the 16-bit type for the second product and O is divided by the f32 row sum at the end.
+// The output type TO is T, or e4m3 of O * mul (the FP8 path: the out-projection's input).
 template <typename T> struct MmaName;
 template <> struct MmaName<__half> {
     static __device__ __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
@@ -209,9 +222,9 @@ __device__ __forceinline__ float ex2_approx(float x)
 constexpr int kAttRows = 80;     // 65 tokens padded to 5 tiles of 16
 constexpr int kAttWarps = 5;
 
-template <typename T, int DH>
-__global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const T* __restrict__ qkv, T* __restrict__ att,
-                                                                   int d, float scale)
+template <typename T, typename TO, int DH>
+__global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const T* __restrict__ qkv, TO* __restrict__ att,
+                                                                   int d, float scale, float mul)
 {
     constexpr int P = DH + 8;                 // smem row pitch in elements (16-byte multiple)
     constexpr int CH = DH * 2 / 16;           // 16-byte chunks per row
@@ -334,19 +347,60 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const T* __re
     // normalise, stage this warp's rows in sQ (its own rows only: no other warp reads them any more), store
     const float inv0 = 1.f / sum0, inv1 = 1.f / sum1;
     __syncwarp();
+    if constexpr (is_e4m3<TO>) {
+        // e4m3 rows of DH bytes, staged at the same row pitch (P * 2 bytes, a multiple of 16)
+        uint8_t* st = reinterpret_cast<uint8_t*>(sQ);
+        constexpr int PB = P * 2;
+        constexpr int CH8 = DH / 16;
+        const float m0 = inv0 * mul, m1 = inv1 * mul;
 #pragma unroll
-    for (int n = 0; n < DT; ++n) {
-        *reinterpret_cast<uint32_t*>(sQ + (q0 + g) * P + n * 8 + 2 * t) = pack2<T>(o[n][0] * inv0, o[n][1] * inv0);
-        *reinterpret_cast<uint32_t*>(sQ + (q0 + g + 8) * P + n * 8 + 2 * t) =
-            pack2<T>(o[n][2] * inv1, o[n][3] * inv1);
+        for (int n = 0; n < DT; ++n) {
+            *reinterpret_cast<uint16_t*>(st + (q0 + g) * PB + n * 8 + 2 * t) = static_cast<uint16_t>(
+                __nv_cvt_float2_to_fp8x2(make_float2(o[n][0] * m0, o[n][1] * m0), __NV_SATFINITE, __NV_E4M3));
+            *reinterpret_cast<uint16_t*>(st + (q0 + g + 8) * PB + n * 8 + 2 * t) = static_cast<uint16_t>(
+                __nv_cvt_float2_to_fp8x2(make_float2(o[n][2] * m1, o[n][3] * m1), __NV_SATFINITE, __NV_E4M3));
+        }
+        __syncwarp();
+        for (int i = lane; i < 16 * CH8; i += 32) {
+            const int r = q0 + i / CH8, c = i % CH8;
+            if (r < kTokens)
+                *(reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(att) + (row0 + r) * d + (size_t)head * DH) + c) =
+                    *reinterpret_cast<const uint4*>(st + r * PB + c * 16);
+        }
+    } else {
+#pragma unroll
+        for (int n = 0; n < DT; ++n) {
+            *reinterpret_cast<uint32_t*>(sQ + (q0 + g) * P + n * 8 + 2 * t) =
+                pack2<T>(o[n][0] * inv0, o[n][1] * inv0);
+            *reinterpret_cast<uint32_t*>(sQ + (q0 + g + 8) * P + n * 8 + 2 * t) =
+                pack2<T>(o[n][2] * inv1, o[n][3] * inv1);
+        }
+        __syncwarp();
+        for (int i = lane; i < 16 * CH; i += 32) {
+            const int r = q0 + i / CH, c = i % CH;
+            if (r < kTokens)
+                *(reinterpret_cast<uint4*>(att + (row0 + r) * d + (size_t)head * DH) + c) =
+                    *reinterpret_cast<const uint4*>(sQ + r * P + c * 8);
+        }
     }
-    __syncwarp();
-    for (int i = lane; i < 16 * CH; i += 32) {
-        const int r = q0 + i / CH, c = i % CH;
-        if (r < kTokens)
-            *(reinterpret_cast<uint4*>(att + (row0 + r) * d + (size_t)head * DH) + c) =
-                *reinterpret_cast<const uint4*>(sQ + r * P + c * 8);
-    }
+}
+
+// ------------------------------------------------------------------------------------------------ calibration
+// out = max(out, max |p[i]|) over i < n (out holds the f32 bits: non-negative floats order like their bits).
+// Records the ranges of the four product inputs in a 16-bit pass, from which the FP8 path's static input
+// scales are set.
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ p, size_t n, unsigned int* __restrict__ out)
+{
+    float m = 0.f;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(to_f32<T>(p[i])));
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
 }
 
 // ------------------------------------------------------------------------------------------------ heads_post

@@ -12,8 +12,8 @@ int64, ep (B,) int64, I (B, wide) int64 and M (B, wide) uint8. The outputs are f
 logits at each row's legal moves, 0 on padding), val (B,) and qv (B, wide).
 
 Additions: evaluate_logits (also the full (B, 8324) logits), begin/end (two batches in flight),
-evaluate_device (torch CUDA tensors in and out, queued on a stream), precision, check, and k_* single-kernel
-entry points for unit tests.
+evaluate_device (torch CUDA tensors in and out, queued on a stream), precision, check, calibrate (the input
+ranges an e4m3 weight file's static scales come from), and k_* single-kernel entry points for unit tests.
 
 The library is MAYFLY_CUDANET_DLL, else libcudanet_b200.so beside this file. There is no fallback: if the
 library is missing the constructor raises.
@@ -84,6 +84,15 @@ def load(dll=None):
         lib.cudanet_k_attention.restype = i32
         lib.cudanet_k_layernorm.argtypes = [i32, vp, vp, vp, vp, i32, i32, i32, vp, cp, i32]
         lib.cudanet_k_layernorm.restype = i32
+        f32 = ctypes.c_float
+        lib.cudanet_calibrate.argtypes = [vp, i32, vp, vp, vp, vp, vp, i32, cp, i32]
+        lib.cudanet_calibrate.restype = i32
+        lib.cudanet_k_gemm_f8.argtypes = [i32, i32, vp, vp, vp, vp, f32, vp, i32, i32, i32, i32, vp, cp, i32]
+        lib.cudanet_k_gemm_f8.restype = i32
+        lib.cudanet_k_attention_f8.argtypes = [vp, vp, i32, i32, i32, f32, vp, cp, i32]
+        lib.cudanet_k_attention_f8.restype = i32
+        lib.cudanet_k_layernorm_f8.argtypes = [vp, vp, vp, vp, i32, i32, i32, f32, vp, cp, i32]
+        lib.cudanet_k_layernorm_f8.restype = i32
         _libs[path] = lib
         return lib
 
@@ -236,6 +245,28 @@ class CudaNet:
             raise RuntimeError("cudanet_fingerprint failed")
         return buf.value.decode("utf-8", "replace")
 
+    def calibrate(self, ids, cast, hm, ep):
+        """Runs the handle's 16-bit pass on these positions and returns max |.| of each layer's four product
+        inputs (qkv, out, ff1, ff2) as float32 (layers, 4)."""
+        if self._h is None:
+            raise RuntimeError("CudaNet is closed")
+        ids = np.asarray(ids)
+        B = ids.shape[0]
+        if not 1 <= B <= self.max_batch:
+            raise ValueError(f"batch {B}: cudanet takes 1 to {self.max_batch} (env MAYFLY_CUDANET_MAX_BATCH)")
+        ids = _arr(ids, np.int64, (B, 64), "ids")
+        cast = _arr(cast, np.float32, (B, 4), "cast")
+        hm = _arr(hm, np.int64, (B,), "hm")
+        ep = _arr(ep, np.int64, (B,), "ep")
+        out = np.zeros(4 * 256, np.float32)
+        err = ctypes.create_string_buffer(ERR_LEN)
+        with self._lock:
+            k = self._lib.cudanet_calibrate(self._h, B, _p(ids), _p(cast), _p(hm), _p(ep), _p(out), out.size, err,
+                                            ERR_LEN)
+        if k < 0:
+            raise RuntimeError(f"cudanet_calibrate: {_msg(err)}")
+        return out[:k].reshape(-1, 4).copy()
+
     def precision(self):
         buf = ctypes.create_string_buffer(32)
         if self._lib.cudanet_precision(self._h, buf, len(buf)) < 0:
@@ -349,4 +380,50 @@ def k_layernorm(x, g, b, h, n, d, row_stride=1, dll=None):
                                  row_stride, _stream(), err, ERR_LEN)
     if rc != 0:
         raise RuntimeError(f"cudanet_k_layernorm: {_msg(err)}")
+    return h
+
+
+# ------------------------------------------------------------------------------------------------ FP8 kernels
+def _e4m3(t, name):
+    import torch
+    if t.dtype not in (torch.float8_e4m3fn, torch.uint8):
+        raise ValueError(f"{name}: e4m3 bytes (torch.float8_e4m3fn or uint8) only, got {t.dtype}")
+
+
+def k_gemm_f8(A, W, colscale, bias, C, epi, out_scale_inv=1.0, bn=0, dll=None):
+    """C = epilogue(A W^T * colscale + bias) with e4m3 A and W (epi 0 bf16 out, 2 C += (f32), 3 f32 out,
+    4 e4m3 out of gelu(.) * out_scale_inv)."""
+    _e4m3(A, "A")
+    _e4m3(W, "W")
+    lib = load(dll)
+    M, K = A.shape
+    N = W.shape[0]
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_k_gemm_f8(int(epi), int(bn), A.data_ptr(), W.data_ptr(), colscale.data_ptr(), bias.data_ptr(),
+                               float(out_scale_inv), C.data_ptr(), M, N, K, C.stride(0), _stream(), err, ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_k_gemm_f8: {_msg(err)}")
+    return C
+
+
+def k_attention_f8(qkv, att, B, d, heads, mul, dll=None):
+    """att (e4m3) = e4m3(attention(qkv) * mul), qkv bf16."""
+    _e4m3(att, "att")
+    lib = load(dll)
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_k_attention_f8(qkv.data_ptr(), att.data_ptr(), B, d, heads, float(mul), _stream(), err, ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_k_attention_f8: {_msg(err)}")
+    return att
+
+
+def k_layernorm_f8(x, g, b, h, n, d, mul, row_stride=1, dll=None):
+    """h (e4m3) = e4m3(LayerNorm(x) * mul)."""
+    _e4m3(h, "h")
+    lib = load(dll)
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_k_layernorm_f8(x.data_ptr(), g.data_ptr(), b.data_ptr(), h.data_ptr(), n, d, row_stride,
+                                    float(mul), _stream(), err, ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_k_layernorm_f8: {_msg(err)}")
     return h

@@ -10,8 +10,11 @@ Version 1 is the reference's file: the five big matrices of a layer and heads_w 
 Version 2 is this evaluator's: the same names and layout, with the matrices in "bf16" (raw bits, round to
 nearest even from fp32), or in "e4m3" (float8 e4m3fn) each with a "<name>_scale" f32 [out] tensor holding the
 per-output-channel scale (absmax / 448), so that W[o, :] ~= scale[o] * e4m3[o, :]. Version 2 also records
-"precision" ("bf16" or "e4m3"). The evaluator accepts both versions and runs its products in the file's
-16-bit type: a version 1 file in f16 (as the reference backend does), a bf16 file in bf16.
+"precision" ("bf16" or "e4m3"). An e4m3 file also holds, per layer, "L<i>.act_scale" f32 [4]: the static
+scales of the inputs of the layer's four products (qkv, out, ff1, ff2), x ~= act_scale * e4m3, set from
+ranges measured on calibration positions (ACT_HEADROOM x max |x| / 448). The heads stay bf16 in an e4m3 file.
+The evaluator accepts both versions and runs its products in the file's type: a version 1 file in f16 (as the
+reference backend does), a bf16 file in bf16, an e4m3 file's layer products on e4m3 operands.
 
 Random init (the seeded weights every parity test and the bench use): a ChessNet(d, nhead, layers, dim_ff,
 qhead=True) state dict (mayfly/chess/chess_net.py:89-119) in its own order. Every LayerNorm weight is 1 and bias
@@ -36,6 +39,11 @@ TOKENS = 65             # CLS + 64 squares (chess_net.py:190-192)
 HM_BUCKETS = 102        # chess_net.py:115
 PIECES = 13             # chess_net.py:93
 MATRICES = ("qkv_w", "out_w", "ff1_w", "ff2_w")
+E4M3_MAX = 448.0
+# An activation scale maps ACT_HEADROOM x the calibrated max |x| to 448, so that positions a little outside the
+# calibration set's range are not clipped. e4m3's relative precision is the same across its normal range (3
+# mantissa bits), so the headroom costs only the bottom binade.
+ACT_HEADROOM = 2.0
 
 
 @dataclass(frozen=True)
@@ -135,15 +143,28 @@ def to_e4m3(t):
     return q.view(torch.uint8).numpy(), scale.numpy().astype("<f4")
 
 
+def act_scales(act_amax, arch):
+    """The per-layer input scales [layers, 4] an e4m3 file stores, from calibrated max |x| [layers, 4]."""
+    a = np.asarray(act_amax, np.float32)
+    if a.shape != (arch.layers, 4) or not np.all(np.isfinite(a)) or np.any(a < 0):
+        raise ValueError(f"act_amax: needs finite non-negative [{arch.layers}, 4], got {a.shape}")
+    return np.where(a > 0, a * ACT_HEADROOM / E4M3_MAX, 1.0).astype("<f4")
+
+
 def e4m3_to_f32(bits, scale):
     q = torch.from_numpy(np.array(bits, dtype=np.uint8)).view(torch.float8_e4m3fn).float()
     return q * torch.from_numpy(np.asarray(scale, np.float32))[:, None]
 
 
 # ---------------------------------------------------------------------------------------------------- the file
-def cnw_tensors(state, arch, precision="bf16"):
+def cnw_tensors(state, arch, precision="bf16", act_amax=None):
     """[(name, dtype, numpy array)] in cudanet_spec.h's order (export_cudanet.py:95-129 tensors), the matrices
-    in `precision`: "f16" (the reference's version 1), "bf16" or "e4m3" (version 2, with *_scale tensors)."""
+    in `precision`: "f16" (the reference's version 1), "bf16" or "e4m3" (version 2, with *_scale tensors and,
+    from act_amax [layers, 4], each layer's act_scale)."""
+    if precision == "e4m3":
+        if act_amax is None:
+            raise ValueError("an e4m3 file needs act_amax: the calibrated input ranges (mayfly_chess_b200.quant)")
+        acts = act_scales(act_amax, arch)
     def f32(t):
         return np.ascontiguousarray(t.detach().float().cpu().numpy(), dtype="<f4")
 
@@ -176,6 +197,8 @@ def cnw_tensors(state, arch, precision="bf16"):
         out += [(f"L{i}.ff1_b", "f32", f32(state[p + "linear1.bias"]))]
         out += mat(f"L{i}.ff2_w", state[p + "linear2.weight"])
         out += [(f"L{i}.ff2_b", "f32", f32(state[p + "linear2.bias"]))]
+        if precision == "e4m3":
+            out += [(f"L{i}.act_scale", "f32", np.ascontiguousarray(acts[i]))]
     out += [("ln_g", "f32", f32(state["ln.weight"])), ("ln_b", "f32", f32(state["ln.bias"]))]
     # the heads stay 16-bit in every precision: they are 0.1% of the work and set the policy's accuracy
     heads = torch.cat([state["policy.weight"], state["qvalue.weight"]], 0)
@@ -188,9 +211,9 @@ def _align(n):
     return (n + ALIGN - 1) // ALIGN * ALIGN
 
 
-def write_cnw(path, state, arch, precision="bf16", source="random-init"):
+def write_cnw(path, state, arch, precision="bf16", source="random-init", act_amax=None):
     """Write the weight file for `state` (export_cudanet.py:149-173 write_cnw), returning its header."""
-    arrays = cnw_tensors(state, arch, precision)
+    arrays = cnw_tensors(state, arch, precision, act_amax)
     entries, off = [], 0
     for name, dt, a in arrays:
         off = _align(off)

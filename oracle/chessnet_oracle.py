@@ -13,6 +13,12 @@ from the reference checkout) through the committed fixtures under tests/golden/ 
   post(policy, qvalue, I, M) -> (pol [B, wide], val [B], qv [B, wide])
       cpp/export_ts.py:325-334 post (= mcts.py:1152-1164 _collect) with the evaluator's padding convention
       (cudanet/kernels_heads.cu:88-143): pol and qv are 0 on padding, a row with no legal move gets val = -1.
+
+The FP8 evaluator has no counterpart in the reference (its FP8 study was a simulation,
+mayfly/docs/cuda_backend.md:150-152). For it, forward takes two options: `act` [layers, 4] rounds the input
+of each layer's four products (qkv, out, ff1, ff2) to e4m3 at that static scale, as the evaluator's producers
+do (with the weight matrices already e4m3-rounded by weights.dequantised_state, this is the FP8 pass in fp32
+arithmetic); `record` [layers, 4] receives max |.| of those inputs (what the evaluator's calibration measures).
 """
 import math
 
@@ -36,31 +42,44 @@ def embed(state, arch, ids, cast, hm, ep):
     return torch.cat([cls, x], dim=1)                                            # (B, 65, d)
 
 
-def layer(state, arch, i, x):
-    """One pre-norm encoder layer (chess_net.py:154-164)."""
+def fq_e4m3(x, scale):
+    """x rounded to the e4m3 grid at `scale`: scale * e4m3(x / scale), round to nearest even, saturating at
+    +-448 (the evaluator's cvt.rn.satfinite)."""
+    return (x / scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn).float() * scale
+
+
+def layer(state, arch, i, x, act=None, record=None):
+    """One pre-norm encoder layer (chess_net.py:154-164); act / record as in the module docstring."""
     B, L, d = x.shape
     H, dh = arch.heads, arch.dh
     p = f"enc.layers.{i}."
+
+    def product_input(t, j):
+        if record is not None:
+            record[i, j] = max(float(record[i, j]), float(t.abs().max()))
+        return fq_e4m3(t, float(act[i][j])) if act is not None else t
+
     h = F.layer_norm(x, (d,), state[p + "norm1.weight"], state[p + "norm1.bias"], LN_EPS)
-    qkv = F.linear(h, state[p + "self_attn.in_proj_weight"], state[p + "self_attn.in_proj_bias"])
+    qkv = F.linear(product_input(h, 0), state[p + "self_attn.in_proj_weight"], state[p + "self_attn.in_proj_bias"])
     q, k, v = qkv.view(B, L, 3, H, dh).permute(2, 0, 3, 1, 4).unbind(0)         # each (B, H, L, dh)
     s = torch.matmul(q, k.transpose(-1, -2)) * (1.0 / math.sqrt(dh))
     o = torch.matmul(torch.softmax(s, dim=-1), v).transpose(1, 2).reshape(B, L, d)
-    x = x + F.linear(o, state[p + "self_attn.out_proj.weight"], state[p + "self_attn.out_proj.bias"])
+    x = x + F.linear(product_input(o, 1), state[p + "self_attn.out_proj.weight"],
+                     state[p + "self_attn.out_proj.bias"])
     h = F.layer_norm(x, (d,), state[p + "norm2.weight"], state[p + "norm2.bias"], LN_EPS)
-    f = F.gelu(F.linear(h, state[p + "linear1.weight"], state[p + "linear1.bias"]))
-    return x + F.linear(f, state[p + "linear2.weight"], state[p + "linear2.bias"])
+    f = F.gelu(F.linear(product_input(h, 2), state[p + "linear1.weight"], state[p + "linear1.bias"]))
+    return x + F.linear(product_input(f, 3), state[p + "linear2.weight"], state[p + "linear2.bias"])
 
 
 @torch.no_grad()
-def forward(state, arch, ids, cast, hm, ep):
+def forward(state, arch, ids, cast, hm, ep, act=None, record=None):
     ids = torch.as_tensor(ids, dtype=torch.long)
     cast = torch.as_tensor(cast, dtype=torch.float32)
     hm = torch.as_tensor(hm, dtype=torch.long)
     ep = torch.as_tensor(ep, dtype=torch.long)
     x = embed(state, arch, ids, cast, hm, ep)
     for i in range(arch.layers):
-        x = layer(state, arch, i, x)
+        x = layer(state, arch, i, x, act, record)
     hc = F.layer_norm(x[:, 0], (arch.d,), state["ln.weight"], state["ln.bias"], LN_EPS)
     return (F.linear(hc, state["policy.weight"], state["policy.bias"]),
             F.linear(hc, state["qvalue.weight"], state["qvalue.bias"]))
@@ -82,9 +101,9 @@ def post(policy, qvalue, I, M):
     return pol.numpy(), val.numpy(), qv.numpy()
 
 
-def evaluate(state, arch, b):
+def evaluate(state, arch, b, act=None):
     """The oracle's answer for one batch dict (ids, cast, hm, ep, I, M): (pol, val, qv) as the evaluator
     returns them, plus the full (policy, qvalue) logits."""
-    policy, qvalue = forward(state, arch, b["ids"], b["cast"], b["hm"], b["ep"])
+    policy, qvalue = forward(state, arch, b["ids"], b["cast"], b["hm"], b["ep"], act)
     pol, val, qv = post(policy, qvalue, b["I"], b["M"])
     return pol, val, qv, policy.numpy(), qvalue.numpy()

@@ -35,7 +35,8 @@ def test_random_state_rule():
 def test_cnw_roundtrip(tmp_path, precision):
     st = W.random_state(W.SMALL, 0)
     path = os.path.join(tmp_path, "n.cnw")
-    hdr = W.write_cnw(path, st, W.SMALL, precision)
+    amax = np.tile(np.array([4.0, 2.5, 5.0, 3.0], np.float32), (W.SMALL.layers, 1))
+    hdr = W.write_cnw(path, st, W.SMALL, precision, act_amax=amax if precision == "e4m3" else None)
     h2, t = W.read_cnw(path)
     assert h2 == hdr
     assert h2["version"] == (1 if precision == "f16" else 2)
@@ -53,6 +54,8 @@ def test_cnw_roundtrip(tmp_path, precision):
         deq = W.e4m3_to_f32(q, t["L1.ff2_w_scale"])
         rel = (deq - ref).abs().max() / ref.abs().max()
         assert rel < 2 ** -3      # e4m3 keeps 3 mantissa bits
+        # the static input scales: ACT_HEADROOM x max |x| maps to 448
+        np.testing.assert_allclose(t["L2.act_scale"], amax[2] * W.ACT_HEADROOM / 448.0, rtol=1e-6)
     # the heads stay 16-bit in every precision
     assert t["heads_w"].dtype == (np.float16 if precision == "f16" else np.uint16)
 
@@ -69,3 +72,13 @@ def test_bf16_rounding_is_nearest_even():
     x = torch.tensor([1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -2.5e-3], dtype=torch.float32)
     bits = W.to_bf16_bits(x)
     assert torch.equal(W.bf16_bits_to_f32(bits), x.bfloat16().float())
+
+
+def test_e4m3_needs_calibration(tmp_path):
+    st = W.random_state(W.SMALL, 0)
+    with pytest.raises(ValueError):
+        W.write_cnw(os.path.join(tmp_path, "n.cnw"), st, W.SMALL, "e4m3")
+    with pytest.raises(ValueError):
+        W.act_scales(np.ones((W.SMALL.layers, 3)), W.SMALL)
+    s = W.act_scales(np.zeros((W.SMALL.layers, 4)), W.SMALL)
+    assert np.all(s == 1.0)       # a product input that is all zeros keeps scale 1
