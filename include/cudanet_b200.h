@@ -144,8 +144,8 @@ CUDANET_API int cudanet_k_layernorm(int dtype, const float* x, const float* g, c
 
 /* The FP8 pieces (no counterpart in the reference). A[M, K] and W[N, K] are e4m3 bytes, K a multiple of 128;
  * v = acc * colscale[n] + bias[n] with epi 0: C bf16 = v; 2: C f32 += v; 3: C f32 = v; 4: C e4m3 =
- * gelu(v) * out_scale_inv (round to nearest even, saturating at +-448). bn as for cudanet_k_gemm (epi 4 needs
- * 128 or wider). */
+ * gelu(v) * out_scale_inv (round to nearest even, saturating at +-448); 5: C bf16 = bf16(C + v). bn as for
+ * cudanet_k_gemm. */
 CUDANET_API int cudanet_k_gemm_f8(int epi, int bn, const void* A, const void* W, const float* colscale,
                                   const float* bias, float out_scale_inv, void* C, int M, int N, int K, int ldc,
                                   void* stream, char* err, int err_len);
@@ -154,9 +154,10 @@ CUDANET_API int cudanet_k_gemm_f8(int epi, int bn, const void* A, const void* W,
 CUDANET_API int cudanet_k_attention_f8(const void* qkv, void* att, int B, int d, int heads, float mul, void* stream,
                                        char* err, int err_len);
 
-/* cudanet_k_layernorm with e4m3 output: h[i] = e4m3(LayerNorm(x[i * row_stride]) * mul). */
-CUDANET_API int cudanet_k_layernorm_f8(const float* x, const float* g, const float* b, void* h, int n, int d,
-                                       int row_stride, float mul, void* stream, char* err, int err_len);
+/* cudanet_k_layernorm with e4m3 output: h[i] = e4m3(LayerNorm(x[i * row_stride]) * mul), x f32 (x_dtype 0)
+ * or bf16 (x_dtype 1, the FP8 path's residual stream). */
+CUDANET_API int cudanet_k_layernorm_f8(int x_dtype, const void* x, const float* g, const float* b, void* h, int n,
+                                       int d, int row_stride, float mul, void* stream, char* err, int err_len);
 
 #ifdef __cplusplus
 }

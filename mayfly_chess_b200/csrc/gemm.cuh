@@ -1,6 +1,7 @@
 // The trunk's and the heads' matrix products on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
-//   C[M, N] = A[M, K] * W[N, K]^T  (+ epilogue), A and W 16-bit (f16 or bf16), K-major, f32 accumulation.
+//   C[M, N] = A[M, K] * W[N, K]^T  (+ epilogue), A and W 16-bit (f16 or bf16, kind::f16) or e4m3 (the FP8
+//   path, kind::f8f6f4, the accumulator scaled per column in the epilogue), K-major, f32 accumulation.
 //
 // These are the five products of mayfly/chess/cudanet/cudanet_spec.h:94-101 (qkv, out, ff1, ff2, heads), which
 // the reference runs through cuBLASLt (cudanet/gemm.cpp:209-231) or mma.sync (cudanet/kernels_gemm.cu:99-302).
@@ -9,6 +10,9 @@
 //   kEpiBiasGelu  C (16-bit) = gelu_erf(acc + bias)                  ff1 + the GELU pass (kernels_trunk.cu:528-549)
 //   kEpiResidual  X (f32)   = X + (acc + bias), in place             out and ff2 (gemm.h F32_BIAS_RESIDUAL)
 //   kEpiF32       C (f32)   = acc + bias                             heads
+// and for the FP8 path (no reference counterpart; acc scaled per column first):
+//   kEpiGeluE4m3  C (e4m3)  = e4m3(gelu_erf(acc + bias) / scale)     ff1, writing ff2's input
+//   kEpiResidual16 X (bf16) = X + (acc + bias), in place             out and ff2 on a bf16 residual stream
 //
 // Two kernels, both persistent over output tiles with one CTA per SM:
 //   gemm_tc_kernel       one CTA per 128 x BN tile (BN 64, 128 or 256): tcgen05.mma.cta_group::1, M=128.
@@ -20,11 +24,12 @@
 //   warp 0      one thread issues TMA tile loads (128-byte swizzle) of A and W into a STAGES-deep ring
 //   warp 1      allocates tensor memory (2 accumulators of BN f32 columns); one thread (the leader CTA's, for a
 //               pair) issues the MMAs (K=16 each) and tcgen05.commit to release ring stages / accumulators
-//   warps 2..   epilogue, 1 or 2 groups of 4 warps (GemmCfg::EG), one output row per thread per group:
-//               tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31; two groups split a tile's
-//               column chunks), bias / GELU / residual, then the row goes into a 128-row x 128-byte staging
-//               chunk in shared memory (128-byte swizzle) and one thread stores the chunk with a TMA tensor
-//               store (coalesced, asynchronous). For the residual the chunk of X is first TMA-loaded into the
+//   warps 2..   epilogue, 1, 2 or 4 groups of 4 warps (GemmCfg::EG), one output row per thread per group:
+//               tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31; the groups split a tile's
+//               column chunks), bias / GELU / residual, then the row goes into a 128-row staging chunk in shared
+//               memory (128-byte rows with the 128-byte swizzle, or 64-byte rows with the 64-byte swizzle for the
+//               4-group GELU epilogues) and one thread stores the chunk with a TMA tensor store (coalesced,
+//               asynchronous). For the residual the chunk of X is first TMA-loaded into the
 //               same staging buffer, several chunks ahead (also across tiles), so the read-modify-write of the
 //               f32 residual stream is pure bulk traffic.
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1. Tiles run M-block-major (all
@@ -45,8 +50,7 @@
 
 namespace mf {
 
-// kEpiGeluE4m3 (the FP8 path's ff1): C (e4m3) = e4m3(gelu(acc * s + bias) * out_scale_inv)
-enum Epi : int { kEpiBias = 0, kEpiBiasGelu = 1, kEpiResidual = 2, kEpiF32 = 3, kEpiGeluE4m3 = 4 };
+enum Epi : int { kEpiBias = 0, kEpiBiasGelu = 1, kEpiResidual = 2, kEpiF32 = 3, kEpiGeluE4m3 = 4, kEpiResidual16 = 5 };
 
 // Operand types: 16-bit (kind::f16) or e4m3 (kind::f8f6f4). A stage row is always 128 bytes (the swizzle atom),
 // so an FP8 stage holds 128 elements of K and each MMA instruction 32 (16 for 16-bit); the byte sizes, smem
@@ -94,17 +98,22 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
     static constexpr int BK = F8 ? 128 : 64;            // elements of K per stage: one 128-byte swizzle row
     static constexpr int KSTEPS = 4;                    // MMA instructions per stage (K = 16 or 32 each, 32 bytes)
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;   // rows of W per CTA per stage
-    static constexpr bool RESID = EPI == kEpiResidual;
+    static constexpr bool RESID = EPI == kEpiResidual || EPI == kEpiResidual16;
     static constexpr bool IS_F8 = F8;
+    static constexpr bool HEAVY = EPI == kEpiBiasGelu || EPI == kEpiGeluE4m3;   // GELU's erf per element
     static constexpr int OUT_BYTES = (EPI == kEpiResidual || EPI == kEpiF32) ? 4 : (EPI == kEpiGeluE4m3 ? 1 : 2);
-    static constexpr int CHUNK_COLS = 128 / OUT_BYTES;   // one staging chunk: 128 rows x 128 bytes
+    // one staging chunk: 128 rows x ROW_BYTES (64-byte rows for the GELU epilogues, whose four groups each take
+    // a narrow chunk at a time; 128-byte rows otherwise)
+    static constexpr int ROW_BYTES = HEAVY ? 64 : 128;
+    static constexpr int CHUNK_COLS = ROW_BYTES / OUT_BYTES;
     static constexpr int NC = BN / CHUNK_COLS;           // staging chunks per tile
-    static constexpr uint32_t CHUNK_BYTES = 128 * 128;
-    // Epilogue groups: 4 warps each, one per TMEM lane quarter. Two groups split a tile's chunks (even / odd)
-    // where the per-element work is heavy (GELU's erf) or the chunks are many; the residual's bulk traffic
-    // keeps one group with deeper prefetch.
-    static constexpr int EG = (!RESID && NC % 2 == 0) ? 2 : 1;
-    static constexpr int NBUF = RESID ? 4 : (EG == 2 ? 1 : 2);   // staging buffers per group
+    static constexpr uint32_t CHUNK_BYTES = 128 * ROW_BYTES;
+    // Epilogue groups: 4 warps each, one per TMEM lane quarter, splitting a tile's chunks round-robin. Four
+    // groups where the per-element work is heavy (GELU's erf: more warps to hide its latency and share its
+    // issue slots), two where the chunks are many, one for the residual, whose bulk traffic wants deeper
+    // prefetch instead.
+    static constexpr int EG = RESID ? 1 : (HEAVY && NC % 4 == 0) ? 4 : (NC % 2 == 0 ? 2 : 1);
+    static constexpr int NBUF = RESID ? 4 : (EG >= 2 ? 1 : 2);   // staging buffers per group
     static constexpr uint32_t A_BYTES = BM * 128;
     static constexpr uint32_t B_BYTES = B_ROWS * 128;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -208,9 +217,17 @@ __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float
     return lo | (hi << 16);
 }
 
-// byte offset of 16-byte unit j of row r in a 128-byte-swizzled staging chunk (what a TMA tensor map with
-// CU_TENSOR_MAP_SWIZZLE_128B reads and writes; the chunk base is 1024-byte aligned)
-__device__ __forceinline__ uint32_t swz(int r, int j) { return (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)); }
+// byte offset of 16-byte unit j of row r in a swizzled staging chunk of ROW_BYTES-byte rows, what a TMA tensor
+// map with CU_TENSOR_MAP_SWIZZLE_128B (128-byte rows: unit ^= row % 8) or _64B (64-byte rows: unit ^= (row / 2)
+// % 4) reads and writes; the chunk base is 1024-byte aligned
+template <int ROW_BYTES> __device__ __forceinline__ uint32_t swz(int r, int j)
+{
+    if constexpr (ROW_BYTES == 128) return (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4));
+    else return (uint32_t)(r * 64 + ((j ^ ((r >> 1) & 3)) << 4));
+}
+
+__device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
 
 // The shared-memory carve-up common to both kernels.
 template <typename C> struct SmemLayout {
@@ -306,11 +323,13 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
             const int b = g % C::NBUF;
             uint8_t* buf = gbuf + b * C::CHUNK_BYTES;
             const int col0 = colb + c * C::CHUNK_COLS;
-            // this chunk's row in registers, 32 accumulator columns at a time: f32 values (4-byte outputs, the
-            // only one-load case) or the row's 128 output bytes already packed (16-bit and e4m3 outputs)
+            // this chunk's row in registers, 32 accumulator columns at a time: f32 values (f32 outputs and the
+            // residuals, which add them to X once its chunk has landed) or the row's output bytes already
+            // packed (16-bit and e4m3 outputs)
             constexpr int LOADS = C::CHUNK_COLS / 32;
-            float v[32];
-            uint32_t q[32];
+            constexpr int QW = C::ROW_BYTES / 4;
+            float v[C::RESID ? C::CHUNK_COLS : 32];
+            uint32_t q[QW];
 #pragma unroll
             for (int p = 0; p < LOADS; ++p) {
                 uint32_t r[32];
@@ -322,21 +341,22 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                     __syncwarp();
                     if (lane == 0) release(acc);
                 }
+                constexpr int off0 = 0;
+                const int off = C::RESID ? 32 * p : off0;
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                if constexpr (C::IS_F8) scale_bias32<32>(v, 0, colscale, bias, col0 + 32 * p, N);
-                else add_bias32<32>(v, 0, bias, col0 + 32 * p, N);
+                for (int i = 0; i < 32; ++i) v[off + i] = __uint_as_float(r[i]);
+                if constexpr (C::IS_F8) scale_bias32(v, off, colscale, bias, col0 + 32 * p, N);
+                else add_bias32(v, off, bias, col0 + 32 * p, N);
                 if constexpr (EPI == kEpiBiasGelu) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
-                }
-                if constexpr (EPI == kEpiGeluE4m3) {
+                    for (int i = 0; i < 16; ++i) q[16 * p + i] = pack2<T>(gelu_erf(v[2 * i]), gelu_erf(v[2 * i + 1]));
+                } else if constexpr (EPI == kEpiGeluE4m3) {
                     const float inv = ep.out_scale_inv;
 #pragma unroll
                     for (int i = 0; i < 8; ++i)
                         q[8 * p + i] = pack_e4m3x4(gelu_erf(v[4 * i]) * inv, gelu_erf(v[4 * i + 1]) * inv,
                                                    gelu_erf(v[4 * i + 2]) * inv, gelu_erf(v[4 * i + 3]) * inv);
-                } else if constexpr (C::OUT_BYTES == 2) {
+                } else if constexpr (EPI == kEpiBias) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) q[16 * p + i] = pack2<T>(v[2 * i], v[2 * i + 1]);
                 }
@@ -352,11 +372,12 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                 ok = false;
                 break;
             }
-            if constexpr (C::RESID) {
+            constexpr int RB = C::ROW_BYTES;
+            if constexpr (EPI == kEpiResidual) {
                 // all 8 loads first, then the adds, then the stores (no load waits behind a store)
                 float4 xs[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) xs[j] = *reinterpret_cast<const float4*>(buf + swz(row, j));
+                for (int j = 0; j < 8; ++j) xs[j] = *reinterpret_cast<const float4*>(buf + swz<RB>(row, j));
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     xs[j].x += v[4 * j + 0];
@@ -365,16 +386,31 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                     xs[j].w += v[4 * j + 3];
                 }
 #pragma unroll
-                for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(buf + swz(row, j)) = xs[j];
+                for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(buf + swz<RB>(row, j)) = xs[j];
+            } else if constexpr (EPI == kEpiResidual16) {
+                // X (bf16) + v in f32, rounded once to bf16
+                uint4 xs[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) xs[j] = *reinterpret_cast<const uint4*>(buf + swz<RB>(row, j));
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float* w = v + 8 * j;
+                    xs[j].x = pack2<__nv_bfloat16>(bf16_lo(xs[j].x) + w[0], bf16_hi(xs[j].x) + w[1]);
+                    xs[j].y = pack2<__nv_bfloat16>(bf16_lo(xs[j].y) + w[2], bf16_hi(xs[j].y) + w[3]);
+                    xs[j].z = pack2<__nv_bfloat16>(bf16_lo(xs[j].z) + w[4], bf16_hi(xs[j].z) + w[5]);
+                    xs[j].w = pack2<__nv_bfloat16>(bf16_lo(xs[j].w) + w[6], bf16_hi(xs[j].w) + w[7]);
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(buf + swz<RB>(row, j)) = xs[j];
             } else if constexpr (C::OUT_BYTES == 4) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
-                    *reinterpret_cast<float4*>(buf + swz(row, j)) =
+                    *reinterpret_cast<float4*>(buf + swz<RB>(row, j)) =
                         make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             } else {
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    *reinterpret_cast<uint4*>(buf + swz(row, j)) =
+                for (int j = 0; j < QW / 4; ++j)
+                    *reinterpret_cast<uint4*>(buf + swz<RB>(row, j)) =
                         make_uint4(q[4 * j], q[4 * j + 1], q[4 * j + 2], q[4 * j + 3]);
             }
             fence_proxy_async_smem();

@@ -271,7 +271,7 @@ gemm_tc_resln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 float s = 0.f;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    float4* p = reinterpret_cast<float4*>(buf + swz(row, j));
+                    float4* p = reinterpret_cast<float4*>(buf + swz<128>(row, j));
                     float4 x = *p;
                     x.x += v[4 * j + 0];
                     x.y += v[4 * j + 1];
@@ -395,7 +395,7 @@ gemm_tc_resln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     q.y = pack2<T>(x[8 * j + 2], x[8 * j + 3]);
                     q.z = pack2<T>(x[8 * j + 4], x[8 * j + 5]);
                     q.w = pack2<T>(x[8 * j + 6], x[8 * j + 7]);
-                    *reinterpret_cast<uint4*>(buf + swz(row, j)) = q;
+                    *reinterpret_cast<uint4*>(buf + swz<128>(row, j)) = q;
                 }
                 fence_proxy_async_smem();
                 named_barrier(1, 128);

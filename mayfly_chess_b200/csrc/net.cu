@@ -24,6 +24,7 @@
 #include <stdexcept>
 #include <string>
 #include <tuple>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/cudanet_b200.h"
@@ -77,18 +78,20 @@ static EncodeTiledFn encode_tiled()
 
 // A row-major matrix [outer, inner] with row pitch `pitch` elements, tiles of box_inner x box_outer with the
 // 128-byte swizzle (box_inner * element size = 128 bytes: the layout sdesc_sw128 and the epilogue's staging
-// describe). Reads past the extents are zero, writes past them are dropped. U8 carries e4m3 bytes.
+// describe) or, with swz64, the 64-byte swizzle (64-byte box rows: the GELU epilogues' staging). Reads past the
+// extents are zero, writes past them are dropped. U8 carries e4m3 bytes.
 enum class MapType { F16, BF16, F32, U8 };
 
 static uint64_t map_elem_bytes(MapType type) { return type == MapType::F32 ? 4 : type == MapType::U8 ? 1 : 2; }
 
 static CUtensorMap make_map(const void* base, MapType type, uint64_t inner, uint64_t outer, uint64_t pitch,
-                            uint32_t box_inner, uint32_t box_outer)
+                            uint32_t box_inner, uint32_t box_outer, bool swz64 = false)
 {
     const uint64_t es = map_elem_bytes(type);
     if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch * es) % 16)
         throw std::runtime_error("cudanet_b200: a TMA operand or its row pitch is not 16-byte aligned");
-    if (box_inner * es != 128) throw std::runtime_error("cudanet_b200: TMA box rows must be 128 bytes");
+    if (box_inner * es != (swz64 ? 64u : 128u))
+        throw std::runtime_error("cudanet_b200: TMA box rows must be 128 bytes (64 with the 64-byte swizzle)");
     CUtensorMap m;
     const cuuint64_t dims[2] = {inner, outer};
     const cuuint64_t strides[1] = {pitch * es};
@@ -99,7 +102,8 @@ static CUtensorMap make_map(const void* base, MapType type, uint64_t inner, uint
                                    : type == MapType::U8   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const CUresult r = encode_tiled()(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                      swz64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         throw std::runtime_error("cudanet_b200: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
@@ -114,13 +118,15 @@ static CUtensorMap operand_map(const void* base, MapType type, uint64_t K, uint6
     return make_map(base, type, K, rows, K, static_cast<uint32_t>(128 / map_elem_bytes(type)), box_rows);
 }
 
-// The output (and, for the residual, the input) of a product: [M, N] with pitch ldc, 16-bit (`t16`) for the
-// kEpiBias / kEpiBiasGelu epilogues, f32 for kEpiResidual / kEpiF32, e4m3 for kEpiGeluE4m3; staging chunks of
-// 128 rows x 128 bytes.
+// The output (and, for the residuals, the input) of a product: [M, N] with pitch ldc, 16-bit (`t16`) for
+// kEpiBias / kEpiBiasGelu, f32 for kEpiResidual / kEpiF32, e4m3 for kEpiGeluE4m3, bf16 for kEpiResidual16;
+// boxes of one staging chunk (128 rows x GemmCfg::ROW_BYTES: 64-byte rows for the GELU epilogues).
 static CUtensorMap output_map(void* base, int epi, MapType t16, int M, int N, int ldc)
 {
     if (epi == kEpiResidual || epi == kEpiF32) return make_map(base, MapType::F32, N, M, ldc, 32, 128);
-    if (epi == kEpiGeluE4m3) return make_map(base, MapType::U8, N, M, ldc, 128, 128);
+    if (epi == kEpiGeluE4m3) return make_map(base, MapType::U8, N, M, ldc, 64, 128, true);
+    if (epi == kEpiBiasGelu) return make_map(base, t16, N, M, ldc, 32, 128, true);
+    if (epi == kEpiResidual16) return make_map(base, MapType::BF16, N, M, ldc, 64, 128);
     return make_map(base, t16, N, M, ldc, 64, 128);
 }
 
@@ -229,11 +235,11 @@ static void launch_gemm_resln(const CUtensorMap& ma, const CUtensorMap& mb, cons
 }
 
 // The epilogues each operand type has: 16-bit products bias / bias+GELU (16-bit out), residual, f32; FP8
-// products bias (16-bit out), residual, f32, and bias+GELU with e4m3 out (tiles of at least 128 columns).
+// products bias (16-bit out), residual (f32 or bf16), f32, and bias+GELU with e4m3 out.
 template <typename TI, int EPI, int BN> constexpr bool epi_supported()
 {
-    if constexpr (Operand<TI>::F8) return EPI != kEpiBiasGelu && (EPI != kEpiGeluE4m3 || BN >= 128);
-    else return EPI != kEpiGeluE4m3;
+    if constexpr (Operand<TI>::F8) return EPI != kEpiBiasGelu;
+    else return EPI != kEpiGeluE4m3 && EPI != kEpiResidual16;
 }
 
 template <typename TI, typename T, int BN, int EPI>
@@ -254,6 +260,9 @@ static void launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& m
         case kEpiResidual: launch_gemm_bn_if<TI, T, BN, kEpiResidual>(ma, mb, mc, M, N, K, ep, err, num_sms, s); break;
         case kEpiF32: launch_gemm_bn_if<TI, T, BN, kEpiF32>(ma, mb, mc, M, N, K, ep, err, num_sms, s); break;
         case kEpiGeluE4m3: launch_gemm_bn_if<TI, T, BN, kEpiGeluE4m3>(ma, mb, mc, M, N, K, ep, err, num_sms, s); break;
+        case kEpiResidual16:
+            launch_gemm_bn_if<TI, T, BN, kEpiResidual16>(ma, mb, mc, M, N, K, ep, err, num_sms, s);
+            break;
         default: throw std::runtime_error("cudanet_b200: unknown epilogue");
     }
 }
@@ -294,7 +303,7 @@ static int pick_bn(int M, int N, int K, int epi, int num_sms)
     const int m_tiles = (M + 127) / 128;
     for (int bn : {256, 128})
         if (m_tiles * ((N + bn - 1) / bn) >= num_sms) return bn;
-    return epi == kEpiGeluE4m3 ? 128 : 64;   // an e4m3 staging chunk is 128 columns wide
+    return 64;
 }
 
 // rows of W in one TMA box for a tile choice
@@ -320,6 +329,7 @@ static void launch_gemm(int epi, int bn, const CUtensorMap& ma, const CUtensorMa
             case kEpiResidual: launch_gemm_pair_if<TI, T, kEpiResidual>(ma, mb, mc, M, N, K, ep, err, s); break;
             case kEpiF32: launch_gemm_pair_if<TI, T, kEpiF32>(ma, mb, mc, M, N, K, ep, err, s); break;
             case kEpiGeluE4m3: launch_gemm_pair_if<TI, T, kEpiGeluE4m3>(ma, mb, mc, M, N, K, ep, err, s); break;
+            case kEpiResidual16: launch_gemm_pair_if<TI, T, kEpiResidual16>(ma, mb, mc, M, N, K, ep, err, s); break;
             default: throw std::runtime_error("cudanet_b200: unknown epilogue");
         }
     } else if (bn == 256) launch_gemm_epi<TI, T, 256>(epi, ma, mb, mc, M, N, K, ep, err, num_sms, s);
@@ -328,32 +338,67 @@ static void launch_gemm(int epi, int bn, const CUtensorMap& ma, const CUtensorMa
     else throw std::runtime_error("cudanet_b200: tile choice must be 2 (CTA pair), 64, 128 or 256");
 }
 
-// h = LN(x) in T (16-bit, or e4m3 of h * mul)
-template <typename T>
-static void launch_layernorm(const float* x, const float* g, const float* b, T* h, int n, int d, int row_stride,
+// h = LN(x) in T (16-bit, or e4m3 of h * mul), x f32 or bf16 (XT)
+template <typename T, typename XT = float>
+static void launch_layernorm(const XT* x, const float* g, const float* b, T* h, int n, int d, int row_stride,
                              float mul, cudaStream_t s)
 {
     const dim3 grid((n + 7) / 8), block(256);
     switch (d) {
-        case 256: layernorm_kernel<T, 2><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
-        case 512: layernorm_kernel<T, 4><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
-        case 1024: layernorm_kernel<T, 8><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
+        case 256: layernorm_kernel<T, 2, XT><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
+        case 512: layernorm_kernel<T, 4, XT><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
+        case 1024: layernorm_kernel<T, 8, XT><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
         default: throw std::runtime_error("cudanet_b200: width must be 256, 512 or 1024");
     }
     RT(cudaGetLastError());
 }
 
-// att = attention(qkv) in TO (T, or e4m3 of att * mul)
-template <typename T, typename TO>
-static void launch_attention(const T* qkv, TO* att, int B, int d, int heads, float mul, cudaStream_t s)
+// The TMA map attention reads qkv [rows, 3d] through: boxes of one head's DH columns x 80 rows.
+static CUtensorMap qkv_map(const void* qkv, bool bf16, int rows, int d, int heads)
 {
     const int dh = d / heads;
-    const dim3 grid(heads, B), block(kAttWarps * 32);
-    const float scale = 1.0f / std::sqrt(static_cast<float>(dh));
-    if (dh == 64) attention_kernel<T, TO, 64><<<grid, block, 0, s>>>(qkv, att, d, scale, mul);
-    else if (dh == 32) attention_kernel<T, TO, 32><<<grid, block, 0, s>>>(qkv, att, d, scale, mul);
-    else throw std::runtime_error("cudanet_b200: head width must be 32 or 64");
+    if (dh != 64 && dh != 32) throw std::runtime_error("cudanet_b200: head width must be 32 or 64");
+    return make_map(qkv, type16(bf16), static_cast<uint64_t>(3 * d), static_cast<uint64_t>(rows),
+                    static_cast<uint64_t>(3 * d), static_cast<uint32_t>(dh), kAttRows, dh == 32);
+}
+
+template <typename T, typename TO, int DH>
+static void launch_attention_dh(const CUtensorMap& map, TO* att, int B, int d, int heads, float mul, uint32_t* err,
+                                cudaStream_t s)
+{
+    using C = AttCfg<DH>;
+    static int per_sm[64] = {};
+    static int sms[64] = {};
+    int dev = 0;
+    RT(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw std::runtime_error("cudanet_b200: device index out of range");
+    if (!per_sm[dev]) {
+        RT(cudaFuncSetAttribute(attention_kernel<T, TO, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)C::SMEM));
+        int k = 0;
+        RT(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, attention_kernel<T, TO, DH>, kAttWarps * 32,
+                                                         C::SMEM));
+        if (k < 1) throw std::runtime_error("cudanet_b200: the attention kernel does not fit on this device");
+        RT(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+        per_sm[dev] = k;
+    }
+    const int items = B * heads;
+    const int grid = std::min(items, per_sm[dev] * sms[dev]);
+    const float scale = 1.0f / std::sqrt(static_cast<float>(DH));
+    attention_kernel<T, TO, DH><<<grid, kAttWarps * 32, C::SMEM, s>>>(map, att, B, heads, d, scale, mul, err);
     RT(cudaGetLastError());
+}
+
+// att = attention(qkv) in TO (T, or e4m3 of att * mul); map from qkv_map over at least B * 65 rows
+template <typename T, typename TO>
+static void launch_attention(const CUtensorMap& map, TO* att, int B, int d, int heads, float mul, uint32_t* err,
+                             cudaStream_t s)
+{
+    if (B < 1 || heads < 1 || d % heads) throw std::runtime_error("cudanet_b200: bad attention sizes");
+    const int dh = d / heads;
+    if (dh == 64) launch_attention_dh<T, TO, 64>(map, att, B, d, heads, mul, err, s);
+    else if (dh == 32) launch_attention_dh<T, TO, 32>(map, att, B, d, heads, mul, err, s);
+    else throw std::runtime_error("cudanet_b200: head width must be 32 or 64");
 }
 
 // ------------------------------------------------------------------------------------------------ weights
@@ -651,7 +696,7 @@ private:
     cudaEvent_t done_[2] = {nullptr, nullptr};
     std::map<int, cudaGraphExec_t> graphs_;
     bool use_graph_ = true;
-    CUtensorMap map_h_, map_att_, map_ff_, map_cls_;
+    CUtensorMap map_h_, map_att_, map_ff_, map_cls_, map_qkv_;
     std::map<std::pair<const void*, int>, CUtensorMap> wmaps_;
     std::map<std::tuple<const void*, int, int, int>, CUtensorMap> omaps_;   // (out, epi, M, N)
 
@@ -795,6 +840,7 @@ void Net::init(const std::string& path, int device)
         map_att_ = operand_map(att_, act, d, rows_pad_, 128);
         map_ff_ = operand_map(ff_, act, ff, rows_pad_, 128);
         map_cls_ = operand_map(cls_, type16(bf16()), d, cls_pad_, 128);
+        map_qkv_ = qkv_map(qkv_, bf16(), static_cast<int>(rows_pad_), a.d, a.heads);
         const char* g = std::getenv("MAYFLY_CUDANET_GRAPH");
         use_graph_ = !(g && std::strcmp(g, "0") == 0);
         RT(cudaStreamSynchronize(stream_));
@@ -910,9 +956,9 @@ void Net::mark(int op, cudaStream_t s)
     ++prof_n_;
 }
 
-// The embedding fused with layer 0's first LayerNorm: x (f32) and h (T: 16-bit, or e4m3 of h * mul).
-template <typename T>
-static void launch_embed_ln(const Weights& w, const LayerW& l0, const uint8_t* d_in, int B, float* x, T* h,
+// The embedding fused with layer 0's first LayerNorm: x (XT: f32, or bf16) and h (T: 16-bit, or e4m3 of h * mul).
+template <typename T, typename XT = float>
+static void launch_embed_ln(const Weights& w, const LayerW& l0, const uint8_t* d_in, int B, XT* x, T* h,
                             float mul, cudaStream_t s)
 {
     const int rows = B * kTokens;
@@ -927,15 +973,15 @@ static void launch_embed_ln(const Weights& w, const LayerW& l0, const uint8_t* d
                 *ep_mark = w.ptr<float>("ep_mark");
     switch (w.a.d) {
         case 256:
-            embed_ln_kernel<T, 2><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
+            embed_ln_kernel<T, 2, XT><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
                                                           ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
             break;
         case 512:
-            embed_ln_kernel<T, 4><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
+            embed_ln_kernel<T, 4, XT><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
                                                           ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
             break;
         default:
-            embed_ln_kernel<T, 8><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
+            embed_ln_kernel<T, 8, XT><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
                                                           ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
     }
     RT(cudaGetLastError());
@@ -959,7 +1005,7 @@ template <typename T> void Net::forward_t(int B, cudaStream_t s)
         mark(kPQkv, s);
         gemm(kEpiBias, map_h_, l.qkv_w, false, rows, 3 * d, d, EpiArgs{l.qkv_b, nullptr, 1.f}, qkv_, 3 * d, s);
         mark(kPAtt, s);
-        launch_attention<T, T>(static_cast<const T*>(qkv_), static_cast<T*>(att_), B, d, a.heads, 1.f, s);
+        launch_attention<T, T>(map_qkv_, static_cast<T*>(att_), B, d, a.heads, 1.f, err_word(), s);
         amax(4 * i + 1, att_, nd, s);
         mark(kPOut, s);
         if (fuse) {
@@ -991,8 +1037,10 @@ template <typename T> void Net::forward_t(int B, cudaStream_t s)
 }
 
 // The FP8 pass: each layer product's input is written as e4m3 of x / act_scale by its producer (the
-// LayerNorms, attention, ff1's GELU epilogue) and the product scales its f32 accumulator per column; q, k, v,
-// the residual stream and the heads stay bf16 / f32 as in the 16-bit pass.
+// LayerNorms, attention, ff1's GELU epilogue) and the product scales its f32 accumulator per column; q, k, v
+// and the heads' input stay bf16, and so does the residual stream x (the FP8 configuration's bf16
+// activations: the residual adds are f32 sums rounded once to bf16, and x is read and written at half the
+// bytes of the 16-bit pass's f32 stream).
 void Net::forward_f8(int B, cudaStream_t s)
 {
     using T = __nv_bfloat16;
@@ -1000,28 +1048,29 @@ void Net::forward_f8(int B, cudaStream_t s)
     const Arch& a = w_.a;
     const int rows = B * kTokens, d = a.d, ff = a.ff;
     F8* h = static_cast<F8*>(h_);
+    T* x = reinterpret_cast<T*>(x_);
     mark(kPEmbed, s);
-    launch_embed_ln<F8>(w_, L_[0], d_in_, B, x_, h, L_[0].inv_qkv, s);
+    launch_embed_ln<F8, T>(w_, L_[0], d_in_, B, x, h, L_[0].inv_qkv, s);
     for (int i = 0; i < a.layers; ++i) {
         const LayerW& l = L_[static_cast<size_t>(i)];
         mark(kPLn1, s);
-        if (i > 0) launch_layernorm<F8>(x_, l.n1_g, l.n1_b, h, rows, d, 1, l.inv_qkv, s);
+        if (i > 0) launch_layernorm<F8, T>(x, l.n1_g, l.n1_b, h, rows, d, 1, l.inv_qkv, s);
         mark(kPQkv, s);
         gemm(kEpiBias, map_h_, l.qkv_w, true, rows, 3 * d, d, EpiArgs{l.qkv_b, l.qkv_cs, 1.f}, qkv_, 3 * d, s);
         mark(kPAtt, s);
-        launch_attention<T, F8>(static_cast<const T*>(qkv_), static_cast<F8*>(att_), B, d, a.heads, l.inv_out, s);
+        launch_attention<T, F8>(map_qkv_, static_cast<F8*>(att_), B, d, a.heads, l.inv_out, err_word(), s);
         mark(kPOut, s);
-        gemm(kEpiResidual, map_att_, l.out_w, true, rows, d, d, EpiArgs{l.out_b, l.out_cs, 1.f}, x_, d, s);
+        gemm(kEpiResidual16, map_att_, l.out_w, true, rows, d, d, EpiArgs{l.out_b, l.out_cs, 1.f}, x, d, s);
         mark(kPLn2, s);
-        launch_layernorm<F8>(x_, l.n2_g, l.n2_b, h, rows, d, 1, l.inv_ff1, s);
+        launch_layernorm<F8, T>(x, l.n2_g, l.n2_b, h, rows, d, 1, l.inv_ff1, s);
         mark(kPFf1, s);
         gemm(kEpiGeluE4m3, map_h_, l.ff1_w, true, rows, ff, d, EpiArgs{l.ff1_b, l.ff1_cs, l.inv_ff2}, ff_, ff, s);
         mark(kPFf2, s);
-        gemm(kEpiResidual, map_ff_, l.ff2_w, true, rows, d, ff, EpiArgs{l.ff2_b, l.ff2_cs, 1.f}, x_, d, s);
+        gemm(kEpiResidual16, map_ff_, l.ff2_w, true, rows, d, ff, EpiArgs{l.ff2_b, l.ff2_cs, 1.f}, x, d, s);
     }
     mark(kPCls, s);
-    launch_layernorm<T>(x_, w_.ptr<float>("ln_g"), w_.ptr<float>("ln_b"), static_cast<T*>(cls_), B, d, kTokens, 1.f,
-                        s);
+    launch_layernorm<T, T>(x, w_.ptr<float>("ln_g"), w_.ptr<float>("ln_b"), static_cast<T*>(cls_), B, d, kTokens, 1.f,
+                           s);
     mark(kPHeads, s);
     gemm(kEpiF32, map_cls_, w_.ptr("heads_w"), false, B, 2 * a.moves, d,
          EpiArgs{w_.ptr<float>("heads_b"), nullptr, 1.f}, logits_, 2 * a.moves, s);
@@ -1325,6 +1374,31 @@ static uint32_t* noalloc_scratch(int dev)
     return addr[dev];
 }
 
+// One attention launch of the unit-test entry points: its own error word, a map over exactly B * 65 rows.
+template <typename T, typename TO>
+static void attention_once(const void* qkv, void* att, int B, int d, int heads, float mul, cudaStream_t s,
+                           const char* who)
+{
+    if (B < 1 || heads < 1 || d % heads) throw std::runtime_error(std::string(who) + ": bad sizes");
+    if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(att)) & 15)
+        throw std::runtime_error(std::string(who) + ": qkv and att must be 16-byte aligned");
+    const CUtensorMap map = qkv_map(qkv, std::is_same<T, __nv_bfloat16>::value, B * kTokens, d, heads);
+    uint32_t* errw = nullptr;
+    RT(cudaMalloc(&errw, 4));
+    RT(cudaMemset(errw, 0, 4));
+    try {
+        launch_attention<T, TO>(map, static_cast<TO*>(att), B, d, heads, mul, errw, s);
+        RT(cudaStreamSynchronize(s));
+    } catch (...) {
+        cudaFree(errw);
+        throw;
+    }
+    uint32_t e = 0;
+    RT(cudaMemcpy(&e, errw, 4, cudaMemcpyDeviceToHost));
+    cudaFree(errw);
+    if (e) throw std::runtime_error(std::string(who) + ": device error: " + err_site_name(e >> 8));
+}
+
 }  // namespace mf
 
 using mf::Net;
@@ -1623,16 +1697,12 @@ CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B
 {
     return mf::guarded(err, err_len, "cudanet_k_attention: unknown exception", [&] {
         const cudaStream_t s = static_cast<cudaStream_t>(stream);
-        if (B < 1 || heads < 1 || d % heads) throw std::runtime_error("cudanet_k_attention: bad sizes");
         if (dtype == 1)
-            mf::launch_attention<__nv_bfloat16, __nv_bfloat16>(static_cast<const __nv_bfloat16*>(qkv),
-                                                               static_cast<__nv_bfloat16*>(att), B, d, heads, 1.f, s);
+            mf::attention_once<__nv_bfloat16, __nv_bfloat16>(qkv, att, B, d, heads, 1.f, s, "cudanet_k_attention");
         else if (dtype == 0)
-            mf::launch_attention<__half, __half>(static_cast<const __half*>(qkv), static_cast<__half*>(att), B, d,
-                                                 heads, 1.f, s);
+            mf::attention_once<__half, __half>(qkv, att, B, d, heads, 1.f, s, "cudanet_k_attention");
         else
             throw std::runtime_error("cudanet_k_attention: dtype must be 0 (f16) or 1 (bf16)");
-        mf::RT(cudaStreamSynchronize(s));
         return 0;
     });
 }
@@ -1660,9 +1730,10 @@ CUDANET_API int cudanet_k_gemm_f8(int epi, int bn, const void* A, const void* W,
                                   void* stream, char* err, int err_len)
 {
     return mf::guarded(err, err_len, "cudanet_k_gemm_f8: unknown exception", [&] {
-        if (epi != mf::kEpiBias && epi != mf::kEpiResidual && epi != mf::kEpiF32 && epi != mf::kEpiGeluE4m3)
-            throw std::runtime_error("cudanet_k_gemm_f8: epi must be 0 (bf16 out), 2 (residual), 3 (f32) or 4 "
-                                     "(GELU, e4m3 out)");
+        if (epi != mf::kEpiBias && epi != mf::kEpiResidual && epi != mf::kEpiF32 && epi != mf::kEpiGeluE4m3 &&
+            epi != mf::kEpiResidual16)
+            throw std::runtime_error("cudanet_k_gemm_f8: epi must be 0 (bf16 out), 2 (f32 residual), 3 (f32), 4 "
+                                     "(GELU, e4m3 out) or 5 (bf16 residual)");
         if (M < 1 || N < 1 || K < 128) throw std::runtime_error("cudanet_k_gemm_f8: bad sizes");
         int dev = 0;
         mf::RT(cudaGetDevice(&dev));
@@ -1705,21 +1776,25 @@ CUDANET_API int cudanet_k_attention_f8(const void* qkv, void* att, int B, int d,
 {
     return mf::guarded(err, err_len, "cudanet_k_attention_f8: unknown exception", [&] {
         const cudaStream_t s = static_cast<cudaStream_t>(stream);
-        if (B < 1 || heads < 1 || d % heads || d % 16) throw std::runtime_error("cudanet_k_attention_f8: bad sizes");
-        mf::launch_attention<__nv_bfloat16, __nv_fp8_e4m3>(static_cast<const __nv_bfloat16*>(qkv),
-                                                           static_cast<__nv_fp8_e4m3*>(att), B, d, heads, mul, s);
-        mf::RT(cudaStreamSynchronize(s));
+        mf::attention_once<__nv_bfloat16, __nv_fp8_e4m3>(qkv, att, B, d, heads, mul, s, "cudanet_k_attention_f8");
         return 0;
     });
 }
 
-CUDANET_API int cudanet_k_layernorm_f8(const float* x, const float* g, const float* b, void* h, int n, int d,
-                                       int row_stride, float mul, void* stream, char* err, int err_len)
+CUDANET_API int cudanet_k_layernorm_f8(int x_dtype, const void* x, const float* g, const float* b, void* h, int n,
+                                       int d, int row_stride, float mul, void* stream, char* err, int err_len)
 {
     return mf::guarded(err, err_len, "cudanet_k_layernorm_f8: unknown exception", [&] {
         const cudaStream_t s = static_cast<cudaStream_t>(stream);
         if (n < 1 || row_stride < 1) throw std::runtime_error("cudanet_k_layernorm_f8: bad sizes");
-        mf::launch_layernorm<__nv_fp8_e4m3>(x, g, b, static_cast<__nv_fp8_e4m3*>(h), n, d, row_stride, mul, s);
+        auto* hp = static_cast<__nv_fp8_e4m3*>(h);
+        if (x_dtype == 0)
+            mf::launch_layernorm<__nv_fp8_e4m3, float>(static_cast<const float*>(x), g, b, hp, n, d, row_stride, mul, s);
+        else if (x_dtype == 1)
+            mf::launch_layernorm<__nv_fp8_e4m3, __nv_bfloat16>(static_cast<const __nv_bfloat16*>(x), g, b, hp, n, d,
+                                                               row_stride, mul, s);
+        else
+            throw std::runtime_error("cudanet_k_layernorm_f8: x_dtype must be 0 (f32) or 1 (bf16)");
         mf::RT(cudaStreamSynchronize(s));
         return 0;
     });

@@ -76,20 +76,47 @@ __device__ __forceinline__ void ln_row_store(const float4 (&v)[V], int d, const 
     }
 }
 
+// The residual stream x: f32, or bf16 on the FP8 path. Four consecutive values at p (16 or 8 bytes).
+template <typename XT> __device__ __forceinline__ float4 load_x4(const XT* p)
+{
+    if constexpr (std::is_same<XT, float>::value) {
+        return *reinterpret_cast<const float4*>(p);
+    } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(p);
+        return make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+    }
+}
+
+// stores v in XT and returns the value stored (v itself for f32, its bf16 rounding otherwise)
+template <typename XT> __device__ __forceinline__ float4 store_x4(XT* p, float4 v)
+{
+    if constexpr (std::is_same<XT, float>::value) {
+        *reinterpret_cast<float4*>(p) = v;
+        return v;
+    } else {
+        uint2 u;
+        u.x = pack2<__nv_bfloat16>(v.x, v.y);
+        u.y = pack2<__nv_bfloat16>(v.z, v.w);
+        *reinterpret_cast<uint2*>(p) = u;
+        return make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ embed + LN1
 // mayfly/chess/chess_net.py:182-192 (cudanet/kernels_trunk.cu:74-122 embed), then layer 0's norm1:
 //   x[b*65]     = cls + (cast_b + cast_w . cast[b]) + hm_emb[hm[b]]
 //   x[b*65+1+s] = piece[ids[b*64+s]] + pos[s] (+ ep_mark when ep[b] > 0 and s == ep[b] - 1)
 //   h = LN(x; g, beta)
 // One warp per row, rows = B * 65. ids and hm are clamped to their tables (a bad input cannot read out of
-// bounds), as the reference kernel does. d = 128 * V. h is 16-bit, or e4m3 of h * mul (the FP8 path).
-template <typename T, int V>
+// bounds), as the reference kernel does. d = 128 * V. h is 16-bit, or e4m3 of h * mul (the FP8 path); x is
+// f32, or bf16 (the FP8 path), and h is the norm of x as stored.
+template <typename T, int V, typename XT = float>
 __global__ void __launch_bounds__(256) embed_ln_kernel(
     const int64_t* __restrict__ ids, const float* __restrict__ cast, const int64_t* __restrict__ hm,
     const int64_t* __restrict__ ep, const float* __restrict__ piece, const float* __restrict__ pos,
     const float* __restrict__ cls, const float* __restrict__ cast_w, const float* __restrict__ cast_b,
     const float* __restrict__ hm_emb, const float* __restrict__ ep_mark, const float* __restrict__ g,
-    const float* __restrict__ beta, float* __restrict__ x, T* __restrict__ h, int rows, float eps, float mul)
+    const float* __restrict__ beta, XT* __restrict__ x, T* __restrict__ h, int rows, float eps, float mul)
 {
     constexpr int d = 128 * V;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -138,18 +165,18 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(
             v[i] = r;
         }
     }
-    float4* xr = reinterpret_cast<float4*>(x + (size_t)row * d);
+    XT* xr = x + (size_t)row * d;
 #pragma unroll
-    for (int i = 0; i < V; ++i) xr[lane + 32 * i] = v[i];
+    for (int i = 0; i < V; ++i) v[i] = store_x4<XT>(xr + 4 * (lane + 32 * i), v[i]);
     ln_row_store<T, V>(v, d, g, beta, h + (size_t)row * d, eps, mul);
 }
 
 // ------------------------------------------------------------------------------------------------ LayerNorm
 // h[r] = LN(x[r]) for rows r = row0 + i * row_stride, i < n (row_stride 65 picks the CLS rows for the final
 // norm, chess_net.py:194 / cudanet/kernels_heads.cu:64-86). Output rows are dense: h row i. One warp per row.
-// h is 16-bit, or e4m3 of h * mul (the FP8 path).
-template <typename T, int V>
-__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
+// h is 16-bit, or e4m3 of h * mul (the FP8 path); x is f32, or bf16 (the FP8 path).
+template <typename T, int V, typename XT = float>
+__global__ void __launch_bounds__(256) layernorm_kernel(const XT* __restrict__ x, const float* __restrict__ g,
                                                         const float* __restrict__ b, T* __restrict__ h, int n,
                                                         int row_stride, float eps, float mul)
 {
@@ -157,10 +184,10 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
     const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (i >= n) return;
     const int lane = threadIdx.x & 31;
-    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)i * row_stride * d);
+    const XT* xr = x + (size_t)i * row_stride * d;
     float4 v[V];
 #pragma unroll
-    for (int k = 0; k < V; ++k) v[k] = xr[lane + 32 * k];
+    for (int k = 0; k < V; ++k) v[k] = load_x4<XT>(xr + 4 * (lane + 32 * k));
     ln_row_store<T, V>(v, d, g, b, h + (size_t)i * d, eps, mul);
 }
 
@@ -169,11 +196,15 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
 // mask; cudanet/kernels_trunk.cu:385-509 attention_mma). qkv [rows, 3*d] holds q, k, v column blocks; head j
 // owns columns j*DH..j*DH+DH-1 of each. att [rows, d] gets the heads concatenated.
 //
-// One CTA per (head, board), 5 warps; warp w owns query rows 16w..16w+15 (tokens padded 65 -> 80 with zero
-// rows, padded keys masked to -inf). Q, K, V are staged in shared memory (row pitch DH+8 elements, so
-// ldmatrix rows fall in distinct banks); S = Q K^T and O = P V run on mma.sync m16n8k16 with f32 accumulation;
-// the softmax runs on the S fragments in registers (row max and sum across the 4 lanes of a quad by shuffles);
-// P is rounded to the 16-bit type for the second product and O is divided by the f32 row sum at the end.
+// A persistent kernel: each CTA (5 warps) runs (board, head) items blockIdx.x, + gridDim.x, ... (heads of a
+// board on neighbouring CTAs). One thread streams each item's Q, K and V tiles (80 rows x DH from row 65*b,
+// three TMA loads with the 128-byte swizzle, or 64-byte for DH = 32) into one of two buffers while the warps
+// compute the previous item, so loads and math overlap. Rows 65..79 of a tile are the next board's rows (or
+// zeros past the end): finite values whose queries are discarded and whose keys are masked (P = 0 there).
+// Warp w owns query rows 16w..16w+15; S = Q K^T and O = P V run on mma.sync m16n8k16 with f32 accumulation
+// (ldmatrix addresses follow the swizzle, which keeps them free of bank conflicts); the softmax runs on the S
+// fragments in registers (row max and sum across the 4 lanes of a quad by shuffles); P is rounded to the
+// 16-bit type for the second product and O is divided by the f32 row sum at the end.
 // The output type TO is T, or e4m3 of O * mul (the FP8 path: the out-projection's input).
 template <typename T> struct MmaName;
 template <> struct MmaName<__half> {
@@ -222,167 +253,211 @@ __device__ __forceinline__ float ex2_approx(float x)
 constexpr int kAttRows = 80;     // 65 tokens padded to 5 tiles of 16
 constexpr int kAttWarps = 5;
 
-template <typename T, typename TO, int DH>
-__global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const T* __restrict__ qkv, TO* __restrict__ att,
-                                                                   int d, float scale, float mul)
+template <int DH> struct AttCfg {
+    static constexpr int ROWB = DH * 2;                                  // bytes of a 16-bit tile row
+    static constexpr uint32_t TILE = kAttRows * ROWB;                    // one of Q, K, V
+    static constexpr uint32_t SET = 3 * TILE;                            // one item's tiles
+    static constexpr size_t SMEM = 1024 + 2 * (size_t)SET + 64;          // two sets + barriers
+    static_assert(DH == 64 || DH == 32, "head width 32 or 64");
+};
+
+// byte offset of 16-byte chunk c of row r in a tile written by TMA with the 128-byte (DH 64) or 64-byte (DH 32)
+// swizzle
+template <int DH> __device__ __forceinline__ uint32_t att_off(int r, int c)
 {
-    constexpr int P = DH + 8;                 // smem row pitch in elements (16-byte multiple)
-    constexpr int CH = DH * 2 / 16;           // 16-byte chunks per row
+    if constexpr (DH == 64) return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
+    else return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+}
+
+template <typename T, typename TO, int DH>
+__global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const __grid_constant__ CUtensorMap tmQKV,
+                                                                   TO* __restrict__ att, int B, int heads, int d,
+                                                                   float scale, float mul, uint32_t* err)
+{
+    using C = AttCfg<DH>;
     constexpr int NT = kAttRows / 8;          // 10 key tiles of 8
     constexpr int DT = DH / 8;                // output column tiles of 8
-    __shared__ __align__(16) T sQ[kAttRows * P];
-    __shared__ __align__(16) T sK[kAttRows * P];
-    __shared__ __align__(16) T sV[kAttRows * P];
+    constexpr int CH = DH * 2 / 16;           // 16-byte chunks per 16-bit row
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + 2 * C::SET);
+    volatile uint32_t* ok_flag = reinterpret_cast<volatile uint32_t*>(full + 2);
 
-    const int head = blockIdx.x, b = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const size_t row0 = (size_t)b * kTokens;
-    const size_t ld = 3 * (size_t)d;
-
-    // stage Q, K, V: every 16-byte piece of the 65 live rows is an asynchronous copy (all in flight at once),
-    // rows 65..79 are zero
-    constexpr int LIVE = kTokens * CH * 3;
-    for (int i = tid; i < LIVE; i += kAttWarps * 32) {
-        const int which = i / (kTokens * CH);
-        const int rem = i % (kTokens * CH);
-        const int r = rem / CH, c = rem % CH;
-        T* dst = (which == 0 ? sQ : which == 1 ? sK : sV) + r * P + c * 8;
-        const T* src = qkv + (row0 + r) * ld + (size_t)which * d + (size_t)head * DH + c * 8;
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+    const int items = B * heads;
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&tmQKV);
     }
-    for (int i = tid; i < (kAttRows - kTokens) * CH * 3; i += kAttWarps * 32) {
-        const int which = i / ((kAttRows - kTokens) * CH);
-        const int rem = i % ((kAttRows - kTokens) * CH);
-        const int r = kTokens + rem / CH, c = rem % CH;
-        *reinterpret_cast<uint4*>((which == 0 ? sQ : which == 1 ? sK : sV) + r * P + c * 8) = make_uint4(0, 0, 0, 0);
-    }
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     __syncthreads();
+
+    auto issue = [&](int item, int buf) {
+        const int b = item / heads, h = item - b * heads;
+        uint8_t* s = base + buf * C::SET;
+        mbar_arrive_expect_tx(&full[buf], C::SET);
+#pragma unroll
+        for (int which = 0; which < 3; ++which)
+            tma_load_2d(s + which * C::TILE, &tmQKV, &full[buf], which * d + h * DH, b * kTokens);
+    };
+    int issued = 0;   // items whose loads thread 0 started (thread 0's count)
+    if (tid == 0 && (int)blockIdx.x < items) {
+        issue(blockIdx.x, 0);
+        issued = 1;
+    }
 
     const int g = lane >> 2, t = lane & 3;
     const int q0 = warp * 16;
-
-    // S = Q K^T for this warp's 16 rows and keys 0..71 (key tile 9, keys 72..79, is all padding: P = 0 there)
-    constexpr int NT_LIVE = (kTokens + 7) / 8;   // 9 key tiles hold the 65 live keys
-    float s[NT][4];
-#pragma unroll
-    for (int n = 0; n < NT; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
-#pragma unroll
-    for (int k0 = 0; k0 < DH; k0 += 16) {
-        uint32_t a[4];
-        ldsm_x4(smem_u32(sQ + (q0 + (lane & 15)) * P + k0 + (lane >> 4) * 8), a[0], a[1], a[2], a[3]);
-#pragma unroll
-        for (int n = 0; n < NT_LIVE; n += 2) {
-            // keys n*8 .. n*8+15: matrices (keys 0-7, k0), (keys 0-7, k0+8), (keys 8-15, k0), (keys 8-15, k0+8)
-            const int key = n * 8 + (lane & 7) + ((lane >> 4) << 3);
-            const int kk = k0 + ((lane >> 3) & 1) * 8;
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4(smem_u32(sK + key * P + kk), b0, b1, b2, b3);
-            MmaName<T>::mma(s[n], a, b0, b1);
-            if (n + 1 < NT_LIVE) MmaName<T>::mma(s[n + 1], a, b2, b3);
-        }
-    }
-
-    // softmax over keys 0..64 of rows g and g+8 (each row spread over the quad's 4 lanes), in base 2:
-    // exp(x * scale - m) = 2^(x * scale * log2(e) - m * log2(e)), with the hardware 2^x (ex2.approx, relative
-    // error near 2^-22, far below the 16-bit rounding P gets next)
     const float sl2 = scale * 1.4426950408889634f;
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int key = n * 8 + 2 * t + j;
-            const bool live = key < kTokens;
-            s[n][j] = live ? s[n][j] * sl2 : -INFINITY;
-            s[n][2 + j] = live ? s[n][2 + j] * sl2 : -INFINITY;
-            mx0 = fmaxf(mx0, s[n][j]);
-            mx1 = fmaxf(mx1, s[n][2 + j]);
+    int n = 0;   // items this CTA has computed
+    for (int item = blockIdx.x; item < items; item += gridDim.x, ++n) {
+        const int buf = n & 1;
+        if (tid == 0) {
+            if (item + (int)gridDim.x < items) {
+                issue(item + gridDim.x, buf ^ 1);   // that buffer's last reader finished before the last barrier
+                ++issued;
+            }
+            *ok_flag = mbar_wait(&full[buf], (n >> 1) & 1, err, kErrTmaFull) ? 1u : 0u;
         }
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            s[n][j] = ex2_approx(s[n][j] - mx0);
-            s[n][2 + j] = ex2_approx(s[n][2 + j] - mx1);
-            sum0 += s[n][j];
-            sum1 += s[n][2 + j];
-        }
-    }
-    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
-    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
-    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
-    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+        __syncthreads();
+        if (!*ok_flag) break;
+        const uint8_t* sQ = base + buf * C::SET;
+        const uint8_t* sK = sQ + C::TILE;
+        const uint8_t* sV = sK + C::TILE;
+        const int b = item / heads, h = item - b * heads;
 
-    // O = P V: P's fragments are S's accumulators (keys 16kk..16kk+15 = key tiles 2kk, 2kk+1)
-    float o[DT][4];
+        // S = Q K^T for this warp's 16 rows and keys 0..71 (key tile 9, keys 72..79, is all padding: P = 0)
+        constexpr int NT_LIVE = (kTokens + 7) / 8;   // 9 key tiles hold the 65 live keys
+        float s[NT][4];
 #pragma unroll
-    for (int n = 0; n < DT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+        for (int nn = 0; nn < NT; ++nn) s[nn][0] = s[nn][1] = s[nn][2] = s[nn][3] = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < kAttRows / 16; ++kk) {
-        uint32_t a[4];
-        a[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
-        a[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
-        a[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-        a[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+        for (int k0 = 0; k0 < DH; k0 += 16) {
+            uint32_t a[4];
+            ldsm_x4(smem_u32(sQ + att_off<DH>(q0 + (lane & 15), (k0 >> 3) + (lane >> 4))), a[0], a[1], a[2], a[3]);
 #pragma unroll
-        for (int n = 0; n < DT; n += 2) {
-            // V rows (keys) 16kk.., transposed: matrices (keys 0-7, cols n*8), (keys 8-15, cols n*8),
-            // (keys 0-7, cols n*8+8), (keys 8-15, cols n*8+8)
-            const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-            const int col = n * 8 + (lane >> 4) * 8;
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(smem_u32(sV + key * P + col), b0, b1, b2, b3);
-            MmaName<T>::mma(o[n], a, b0, b1);
-            MmaName<T>::mma(o[n + 1], a, b2, b3);
+            for (int nn = 0; nn < NT_LIVE; nn += 2) {
+                // keys nn*8 .. nn*8+15: matrices (keys 0-7, k0), (keys 0-7, k0+8), (keys 8-15, k0), (keys 8-15, k0+8)
+                const int key = nn * 8 + (lane & 7) + ((lane >> 4) << 3);
+                const int kc = (k0 >> 3) + ((lane >> 3) & 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(smem_u32(sK + att_off<DH>(key, kc)), b0, b1, b2, b3);
+                MmaName<T>::mma(s[nn], a, b0, b1);
+                if (nn + 1 < NT_LIVE) MmaName<T>::mma(s[nn + 1], a, b2, b3);
+            }
         }
-    }
 
-    // normalise, stage this warp's rows in sQ (its own rows only: no other warp reads them any more), store
-    const float inv0 = 1.f / sum0, inv1 = 1.f / sum1;
-    __syncwarp();
-    if constexpr (is_e4m3<TO>) {
-        // e4m3 rows of DH bytes, staged at the same row pitch (P * 2 bytes, a multiple of 16)
-        uint8_t* st = reinterpret_cast<uint8_t*>(sQ);
-        constexpr int PB = P * 2;
-        constexpr int CH8 = DH / 16;
-        const float m0 = inv0 * mul, m1 = inv1 * mul;
+        // softmax over keys 0..64 of rows g and g+8 (each row spread over the quad's 4 lanes), in base 2:
+        // exp(x * scale - m) = 2^(x * scale * log2(e) - m * log2(e)), with the hardware 2^x (ex2.approx, relative
+        // error near 2^-22, far below the 16-bit rounding P gets next)
+        float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-        for (int n = 0; n < DT; ++n) {
-            *reinterpret_cast<uint16_t*>(st + (q0 + g) * PB + n * 8 + 2 * t) = static_cast<uint16_t>(
-                __nv_cvt_float2_to_fp8x2(make_float2(o[n][0] * m0, o[n][1] * m0), __NV_SATFINITE, __NV_E4M3));
-            *reinterpret_cast<uint16_t*>(st + (q0 + g + 8) * PB + n * 8 + 2 * t) = static_cast<uint16_t>(
-                __nv_cvt_float2_to_fp8x2(make_float2(o[n][2] * m1, o[n][3] * m1), __NV_SATFINITE, __NV_E4M3));
-        }
-        __syncwarp();
-        for (int i = lane; i < 16 * CH8; i += 32) {
-            const int r = q0 + i / CH8, c = i % CH8;
-            if (r < kTokens)
-                *(reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(att) + (row0 + r) * d + (size_t)head * DH) + c) =
-                    *reinterpret_cast<const uint4*>(st + r * PB + c * 16);
-        }
-    } else {
+        for (int nn = 0; nn < NT; ++nn) {
 #pragma unroll
-        for (int n = 0; n < DT; ++n) {
-            *reinterpret_cast<uint32_t*>(sQ + (q0 + g) * P + n * 8 + 2 * t) =
-                pack2<T>(o[n][0] * inv0, o[n][1] * inv0);
-            *reinterpret_cast<uint32_t*>(sQ + (q0 + g + 8) * P + n * 8 + 2 * t) =
-                pack2<T>(o[n][2] * inv1, o[n][3] * inv1);
+            for (int j = 0; j < 2; ++j) {
+                const int key = nn * 8 + 2 * t + j;
+                const bool live = key < kTokens;
+                s[nn][j] = live ? s[nn][j] * sl2 : -INFINITY;
+                s[nn][2 + j] = live ? s[nn][2 + j] * sl2 : -INFINITY;
+                mx0 = fmaxf(mx0, s[nn][j]);
+                mx1 = fmaxf(mx1, s[nn][2 + j]);
+            }
         }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int nn = 0; nn < NT; ++nn) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                s[nn][j] = ex2_approx(s[nn][j] - mx0);
+                s[nn][2 + j] = ex2_approx(s[nn][2 + j] - mx1);
+                sum0 += s[nn][j];
+                sum1 += s[nn][2 + j];
+            }
+        }
+        sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+        sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+        sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+        sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+
+        // O = P V: P's fragments are S's accumulators (keys 16kk..16kk+15 = key tiles 2kk, 2kk+1)
+        float o[DT][4];
+#pragma unroll
+        for (int nn = 0; nn < DT; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < kAttRows / 16; ++kk) {
+            uint32_t a[4];
+            a[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
+            a[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
+            a[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            a[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+            for (int nn = 0; nn < DT; nn += 2) {
+                // V rows (keys) 16kk.., transposed: matrices (keys 0-7, cols nn*8), (keys 8-15, cols nn*8),
+                // (keys 0-7, cols nn*8+8), (keys 8-15, cols nn*8+8)
+                const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                const int vc = nn + (lane >> 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(smem_u32(sV + att_off<DH>(key, vc)), b0, b1, b2, b3);
+                MmaName<T>::mma(o[nn], a, b0, b1);
+                MmaName<T>::mma(o[nn + 1], a, b2, b3);
+            }
+        }
+
+        // normalise, stage this warp's rows in its own rows of the Q tile (no other warp reads them; the
+        // tile is not refilled before the barrier that ends this item), store
+        const float inv0 = 1.f / sum0, inv1 = 1.f / sum1;
+        uint8_t* st = base + buf * C::SET;
+        const size_t row0 = (size_t)b * kTokens;
         __syncwarp();
-        for (int i = lane; i < 16 * CH; i += 32) {
-            const int r = q0 + i / CH, c = i % CH;
-            if (r < kTokens)
-                *(reinterpret_cast<uint4*>(att + (row0 + r) * d + (size_t)head * DH) + c) =
-                    *reinterpret_cast<const uint4*>(sQ + r * P + c * 8);
+        if constexpr (is_e4m3<TO>) {
+            // e4m3 rows of DH bytes at a pitch of DH + 16 bytes, inside the warp's own 16 rows of the Q tile
+            constexpr int PB = DH + 16;
+            constexpr int CH8 = DH / 16;
+            static_assert(16 * PB <= 16 * C::ROWB, "staging stays inside the warp's rows");
+            uint8_t* wst = st + q0 * C::ROWB;
+            const float m0 = inv0 * mul, m1 = inv1 * mul;
+#pragma unroll
+            for (int nn = 0; nn < DT; ++nn) {
+                *reinterpret_cast<uint16_t*>(wst + g * PB + nn * 8 + 2 * t) = static_cast<uint16_t>(
+                    __nv_cvt_float2_to_fp8x2(make_float2(o[nn][0] * m0, o[nn][1] * m0), __NV_SATFINITE, __NV_E4M3));
+                *reinterpret_cast<uint16_t*>(wst + (g + 8) * PB + nn * 8 + 2 * t) = static_cast<uint16_t>(
+                    __nv_cvt_float2_to_fp8x2(make_float2(o[nn][2] * m1, o[nn][3] * m1), __NV_SATFINITE, __NV_E4M3));
+            }
+            __syncwarp();
+            for (int i = lane; i < 16 * CH8; i += 32) {
+                const int lr = i / CH8, c = i % CH8;
+                if (q0 + lr < kTokens)
+                    *(reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(att) + (row0 + q0 + lr) * d +
+                                               (size_t)h * DH) + c) =
+                        *reinterpret_cast<const uint4*>(wst + lr * PB + c * 16);
+            }
+        } else {
+#pragma unroll
+            for (int nn = 0; nn < DT; ++nn) {
+                *reinterpret_cast<uint32_t*>(st + att_off<DH>(q0 + g, nn) + 4 * t) =
+                    pack2<T>(o[nn][0] * inv0, o[nn][1] * inv0);
+                *reinterpret_cast<uint32_t*>(st + att_off<DH>(q0 + g + 8, nn) + 4 * t) =
+                    pack2<T>(o[nn][2] * inv1, o[nn][3] * inv1);
+            }
+            __syncwarp();
+            for (int i = lane; i < 16 * CH; i += 32) {
+                const int r = q0 + i / CH, c = i % CH;
+                if (r < kTokens)
+                    *(reinterpret_cast<uint4*>(att + (row0 + r) * d + (size_t)h * DH) + c) =
+                        *reinterpret_cast<const uint4*>(st + att_off<DH>(r, c));
+            }
         }
+        fence_proxy_async_smem();   // this thread's shared-memory reads and writes of the buffer come before
+        __syncthreads();            // the TMA writes that refill it next
     }
+    // the loads thread 0 started have landed before the CTA leaves (only after a failed wait are any pending)
+    if (tid == 0)
+        for (int k = n; k < issued; ++k) mbar_wait(&full[k & 1], (k >> 1) & 1, err, kErrTmaFull);
 }
 
 // ------------------------------------------------------------------------------------------------ calibration

@@ -91,7 +91,7 @@ def load(dll=None):
         lib.cudanet_k_gemm_f8.restype = i32
         lib.cudanet_k_attention_f8.argtypes = [vp, vp, i32, i32, i32, f32, vp, cp, i32]
         lib.cudanet_k_attention_f8.restype = i32
-        lib.cudanet_k_layernorm_f8.argtypes = [vp, vp, vp, vp, i32, i32, i32, f32, vp, cp, i32]
+        lib.cudanet_k_layernorm_f8.argtypes = [i32, vp, vp, vp, vp, i32, i32, i32, f32, vp, cp, i32]
         lib.cudanet_k_layernorm_f8.restype = i32
         _libs[path] = lib
         return lib
@@ -392,7 +392,7 @@ def _e4m3(t, name):
 
 def k_gemm_f8(A, W, colscale, bias, C, epi, out_scale_inv=1.0, bn=0, dll=None):
     """C = epilogue(A W^T * colscale + bias) with e4m3 A and W (epi 0 bf16 out, 2 C += (f32), 3 f32 out,
-    4 e4m3 out of gelu(.) * out_scale_inv)."""
+    4 e4m3 out of gelu(.) * out_scale_inv, 5 C += (bf16))."""
     _e4m3(A, "A")
     _e4m3(W, "W")
     lib = load(dll)
@@ -418,12 +418,15 @@ def k_attention_f8(qkv, att, B, d, heads, mul, dll=None):
 
 
 def k_layernorm_f8(x, g, b, h, n, d, mul, row_stride=1, dll=None):
-    """h (e4m3) = e4m3(LayerNorm(x) * mul)."""
+    """h (e4m3) = e4m3(LayerNorm(x) * mul), x float32 or bfloat16."""
+    import torch
     _e4m3(h, "h")
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError(f"x: float32 or bfloat16 only, got {x.dtype}")
     lib = load(dll)
     err = ctypes.create_string_buffer(ERR_LEN)
-    rc = lib.cudanet_k_layernorm_f8(x.data_ptr(), g.data_ptr(), b.data_ptr(), h.data_ptr(), n, d, row_stride,
-                                    float(mul), _stream(), err, ERR_LEN)
+    rc = lib.cudanet_k_layernorm_f8(int(x.dtype == torch.bfloat16), x.data_ptr(), g.data_ptr(), b.data_ptr(),
+                                    h.data_ptr(), n, d, row_stride, float(mul), _stream(), err, ERR_LEN)
     if rc != 0:
         raise RuntimeError(f"cudanet_k_layernorm_f8: {_msg(err)}")
     return h

@@ -18,7 +18,9 @@ The FP8 evaluator has no counterpart in the reference (its FP8 study was a simul
 mayfly/docs/cuda_backend.md:150-152). For it, forward takes two options: `act` [layers, 4] rounds the input
 of each layer's four products (qkv, out, ff1, ff2) to e4m3 at that static scale, as the evaluator's producers
 do (with the weight matrices already e4m3-rounded by weights.dequantised_state, this is the FP8 pass in fp32
-arithmetic); `record` [layers, 4] receives max |.| of those inputs (what the evaluator's calibration measures).
+arithmetic); `resid_bf16` rounds the residual stream to bf16 after the embedding and after every residual add,
+as the FP8 evaluator stores it; `record` [layers, 4] receives max |.| of those inputs (what the evaluator's
+calibration measures).
 """
 import math
 
@@ -48,8 +50,17 @@ def fq_e4m3(x, scale):
     return (x / scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn).float() * scale
 
 
-def layer(state, arch, i, x, act=None, record=None):
-    """One pre-norm encoder layer (chess_net.py:154-164); act / record as in the module docstring."""
+def _same(t):
+    return t
+
+
+def _bf16(t):
+    return t.bfloat16().float()
+
+
+def layer(state, arch, i, x, act=None, record=None, resid=_same):
+    """One pre-norm encoder layer (chess_net.py:154-164); act / record as in the module docstring, resid rounds
+    the residual stream after each add."""
     B, L, d = x.shape
     H, dh = arch.heads, arch.dh
     p = f"enc.layers.{i}."
@@ -64,22 +75,23 @@ def layer(state, arch, i, x, act=None, record=None):
     q, k, v = qkv.view(B, L, 3, H, dh).permute(2, 0, 3, 1, 4).unbind(0)         # each (B, H, L, dh)
     s = torch.matmul(q, k.transpose(-1, -2)) * (1.0 / math.sqrt(dh))
     o = torch.matmul(torch.softmax(s, dim=-1), v).transpose(1, 2).reshape(B, L, d)
-    x = x + F.linear(product_input(o, 1), state[p + "self_attn.out_proj.weight"],
-                     state[p + "self_attn.out_proj.bias"])
+    x = resid(x + F.linear(product_input(o, 1), state[p + "self_attn.out_proj.weight"],
+                           state[p + "self_attn.out_proj.bias"]))
     h = F.layer_norm(x, (d,), state[p + "norm2.weight"], state[p + "norm2.bias"], LN_EPS)
     f = F.gelu(F.linear(product_input(h, 2), state[p + "linear1.weight"], state[p + "linear1.bias"]))
-    return x + F.linear(product_input(f, 3), state[p + "linear2.weight"], state[p + "linear2.bias"])
+    return resid(x + F.linear(product_input(f, 3), state[p + "linear2.weight"], state[p + "linear2.bias"]))
 
 
 @torch.no_grad()
-def forward(state, arch, ids, cast, hm, ep, act=None, record=None):
+def forward(state, arch, ids, cast, hm, ep, act=None, record=None, resid_bf16=False):
     ids = torch.as_tensor(ids, dtype=torch.long)
     cast = torch.as_tensor(cast, dtype=torch.float32)
     hm = torch.as_tensor(hm, dtype=torch.long)
     ep = torch.as_tensor(ep, dtype=torch.long)
-    x = embed(state, arch, ids, cast, hm, ep)
+    resid = _bf16 if resid_bf16 else _same
+    x = resid(embed(state, arch, ids, cast, hm, ep))
     for i in range(arch.layers):
-        x = layer(state, arch, i, x, act, record)
+        x = layer(state, arch, i, x, act, record, resid)
     hc = F.layer_norm(x[:, 0], (arch.d,), state["ln.weight"], state["ln.bias"], LN_EPS)
     return (F.linear(hc, state["policy.weight"], state["policy.bias"]),
             F.linear(hc, state["qvalue.weight"], state["qvalue.bias"]))
@@ -101,9 +113,9 @@ def post(policy, qvalue, I, M):
     return pol.numpy(), val.numpy(), qv.numpy()
 
 
-def evaluate(state, arch, b, act=None):
+def evaluate(state, arch, b, act=None, resid_bf16=False):
     """The oracle's answer for one batch dict (ids, cast, hm, ep, I, M): (pol, val, qv) as the evaluator
     returns them, plus the full (policy, qvalue) logits."""
-    policy, qvalue = forward(state, arch, b["ids"], b["cast"], b["hm"], b["ep"], act)
+    policy, qvalue = forward(state, arch, b["ids"], b["cast"], b["hm"], b["ep"], act, resid_bf16=resid_bf16)
     pol, val, qv = post(policy, qvalue, b["I"], b["M"])
     return pol, val, qv, policy.numpy(), qvalue.numpy()
