@@ -375,9 +375,11 @@ static void launch_attention_dh(const CUtensorMap& map, TO* att, int B, int d, i
     if (!per_sm[dev]) {
         RT(cudaFuncSetAttribute(attention_kernel<T, TO, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)C::SMEM));
+        // the whole unified L1 / shared array as shared memory: three CTAs (two buffer sets each) per SM
+        RT(cudaFuncSetAttribute(attention_kernel<T, TO, DH>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                cudaSharedmemCarveoutMaxShared));
         int k = 0;
-        RT(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, attention_kernel<T, TO, DH>, kAttWarps * 32,
-                                                         C::SMEM));
+        RT(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, attention_kernel<T, TO, DH>, kAttWarps * 32, C::SMEM));
         if (k < 1) throw std::runtime_error("cudanet_b200: the attention kernel does not fit on this device");
         RT(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
         per_sm[dev] = k;

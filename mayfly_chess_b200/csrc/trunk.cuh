@@ -275,6 +275,7 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const __grid_
                                                                    float scale, float mul, uint32_t* err)
 {
     using C = AttCfg<DH>;
+    static_assert(kTokens == 65 && kAttRows == 80, "the softmax below hard-codes which key tiles are live");
     constexpr int NT = kAttRows / 8;          // 10 key tiles of 8
     constexpr int DT = DH / 8;                // output column tiles of 8
     constexpr int CH = DH * 2 / 16;           // 16-byte chunks per 16-bit row
@@ -349,36 +350,42 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const __grid_
         }
 
         // softmax over keys 0..64 of rows g and g+8 (each row spread over the quad's 4 lanes), in base 2:
-        // exp(x * scale - m) = 2^(x * scale * log2(e) - m * log2(e)), with the hardware 2^x (ex2.approx, relative
-        // error near 2^-22, far below the 16-bit rounding P gets next)
+        // exp(x * scale - m) = 2^(x * c - m * c), c = scale * log2(e), one FMA per score before the hardware 2^x
+        // (ex2.approx, relative error near 2^-22, far below the 16-bit rounding P gets next). Key tiles 0..7 are
+        // all live, tile 8 holds key 64 (lane t = 0, j = 0) and padding, tile 9 is padding: P = 0 there.
         float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-        for (int nn = 0; nn < NT; ++nn) {
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int key = nn * 8 + 2 * t + j;
-                const bool live = key < kTokens;
-                s[nn][j] = live ? s[nn][j] * sl2 : -INFINITY;
-                s[nn][2 + j] = live ? s[nn][2 + j] * sl2 : -INFINITY;
-                mx0 = fmaxf(mx0, s[nn][j]);
-                mx1 = fmaxf(mx1, s[nn][2 + j]);
-            }
+        for (int nn = 0; nn < 8; ++nn) {
+            mx0 = fmaxf(mx0, fmaxf(s[nn][0], s[nn][1]));
+            mx1 = fmaxf(mx1, fmaxf(s[nn][2], s[nn][3]));
+        }
+        if (t == 0) {
+            mx0 = fmaxf(mx0, s[8][0]);
+            mx1 = fmaxf(mx1, s[8][2]);
         }
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mc0 = mx0 * sl2, mc1 = mx1 * sl2;
         float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-        for (int nn = 0; nn < NT; ++nn) {
+        for (int nn = 0; nn < 8; ++nn) {
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                s[nn][j] = ex2_approx(s[nn][j] - mx0);
-                s[nn][2 + j] = ex2_approx(s[nn][2 + j] - mx1);
+                s[nn][j] = ex2_approx(fmaf(s[nn][j], sl2, -mc0));
+                s[nn][2 + j] = ex2_approx(fmaf(s[nn][2 + j], sl2, -mc1));
                 sum0 += s[nn][j];
                 sum1 += s[nn][2 + j];
             }
         }
+        s[8][0] = t == 0 ? ex2_approx(fmaf(s[8][0], sl2, -mc0)) : 0.f;
+        s[8][2] = t == 0 ? ex2_approx(fmaf(s[8][2], sl2, -mc1)) : 0.f;
+        s[8][1] = s[8][3] = 0.f;
+        sum0 += s[8][0];
+        sum1 += s[8][2];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[9][j] = 0.f;
         sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
         sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
         sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);

@@ -16,8 +16,9 @@ seed-1 positions that no parity case uses) end to end, against
     other e4m3 neighbour whenever the two straddle a rounding midpoint, which happens to a few percent of the
     elements, each then off by a whole e4m3 step (6-12%). Two FP8 passes that differ only in such rounding
     noise differ by about as much as the quantisation itself costs, so the bars are set at that size (the
-    146M net: 0.25 max, 0.04 mean on the policy logits) and every decided row's top move must agree; the
-    kernels' own arithmetic is held to one e4m3 ulp by the kernel tests above;
+    146M net: 0.25 max, 0.04 mean on the policy logits), at least 90% of the top moves must agree and every
+    row whose best move leads by more than twice the logit bar must; the kernels' own arithmetic is held to
+    one e4m3 ulp by the kernel tests above;
   * the float32 reference model, and the reference model with only its weights e4m3-rounded (golden
     pol_e4m3w, ...): what the quantisation itself costs. These are reported (printed) with loose sanity
     bars: rounding the weights alone already moves the 146M net's policy logits by up to 0.18, three times
@@ -234,12 +235,13 @@ def test_fp8_against_fp8_oracle(f8nets, tag):
     b, _ = golden_case(ORACLE_CASE[tag])
     ref = O.evaluate(W.dequantised_state(st, arch, "e4m3"), arch, b, act=act, resid_bf16=True)
     got = run(net, b)
-    m = metrics(ref[:3], got, b["widths"])
+    # a row whose best move leads by more than twice the logit bar cannot change its top move within the bar
+    m = metrics(ref[:3], got, b["widths"], decided_gap=2 * TOL_FQ[tag]["pol_max"])
     print(tag, "e4m3 vs FP8 oracle", m)
     for key, lim in TOL_FQ[tag].items():
         assert m[key] <= lim, (key, m[key])
     assert m["nonfinite"] == 0 and m["pad_nonzero"] == 0
-    assert m["top1_decided"] == 1.0, m
+    assert m["top1_decided"] == 1.0 and m["top1"] >= 0.9, m
 
 
 @pytest.mark.parametrize("tag", ["small", "full"])
