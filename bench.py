@@ -14,9 +14,12 @@ independent evaluator per GPU, no collective on the data path (weak scaling: 1,0
              The working set (285 MB of weights, ~1.2 GB of activations) is far larger than L2.
   e2e        the same metric through the reference-facing API, CudaNet.evaluate on host numpy arrays: each step
              copies the inputs into pinned staging and up, and the outputs down and out (wall clock).
-  roofline   the dominant kernel, the tcgen05 GEMM (all 64 trunk products of a pass): algorithmic FLOPs per
-             launch / mean launch time, from per-step CUDA events of an eager pass (cudanet_profile), against
-             the measured sustained bf16 peak.
+  roofline   the dominant kernel, the qkv product (the CTA-pair tcgen05 GEMM, 26% of device time in the ncu
+             launch list, profiles/launches_bf16_b1024.md): its algorithmic FLOPs per launch / its mean launch
+             time, from CUDA events around each step of an eager pass on the evaluator's stream
+             (cudanet_profile), against the measured sustained bf16 peak. `traffic` is its DRAM bytes per launch
+             from the ncu capture (profiles/gemm_qkv_pair_*), scaled by B / 1,024. The whole trunk-GEMM family is
+             reported beside it (`gemm_family`).
   cpu_baseline  the CPU fp32 restatement of the reference forward (oracle/, test infrastructure) on a bounded
              sample on this host's cores.
 
@@ -44,6 +47,9 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 METRIC = "NN positions evaluated/sec (146M trunk, bs1024, 1/2/4/8 B200); p50 latency at bs64"
+# DRAM bytes (read + write) of one qkv launch per position, from the ncu captures in profiles/
+# (gemm_qkv_pair_bf16_b1024.md: 142.9 + 355.6 MB at B = 1,024; gemm_qkv_pair_e4m3_b1024.md)
+QKV_TRAFFIC_PER_POS = {"bf16": (142905088 + 355564544) / 1024}
 CALIB_ROWS = (7936, 8192)   # positions_seed1.npz rows the e4m3 input scales are calibrated on
 POSITIONS = os.path.join(REPO, "tests", "golden", "positions_seed1.npz")
 PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
@@ -293,10 +299,13 @@ def main():
     # ---------------------------------------------------------------- roofline of the dominant kernel
     prof = net.profile(B, reps=3)
     fl_pos, gemm_fl_pos = flops_per_position()
+    qkv_flop = 2.0 * B * arch.tokens * 3 * arch.d * arch.d
+    achieved = qkv_flop / (prof["qkv"] / arch.layers / 1000.0) / 1e12
+    traffic = QKV_TRAFFIC_PER_POS.get(args.precision)
+    traffic = traffic * B if traffic is not None else None
     trunk_gemm_ms = prof["qkv"] + prof["out"] + prof["ff1"] + prof["ff2"]
     launches = 4 * arch.layers
-    per_launch_s = trunk_gemm_ms / 1000.0 / launches
-    achieved = gemm_fl_pos * B / launches / per_launch_s / 1e12
+    family = gemm_fl_pos * B / launches / (trunk_gemm_ms / 1000.0 / launches) / 1e12
     peaks, peak_kind = load_peaks()
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
     peak_source = f"{peak_kind} bf16 sustained"
@@ -348,10 +357,15 @@ def main():
                    "l2": "working set larger than L2 (285 MB weights + ~1.2 GB activations per pass)"},
         "e2e": {"value": e2e, "unit": "positions/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": (1 + 7 * arch.layers - 1 + 2 + 1) * args.steps,
-        "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (qkv, out, ff1, ff2 of every layer)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_tc_pair_kernel, the qkv product (one per layer)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                     "peak_source": peak_source, "traffic": None,
-                     "flop_per_launch": gemm_fl_pos * B / launches},
+                     "peak_source": peak_source, "traffic": traffic, "flop_per_launch": qkv_flop,
+                     "algorithmic_bytes_per_launch": B * arch.tokens * arch.d * (1 if args.precision == "e4m3" else 2)
+                                                     + 3 * arch.d * arch.d * (1 if args.precision == "e4m3" else 2)
+                                                     + B * arch.tokens * 3 * arch.d * 2,
+                     "timing": "CUDA events around each step of an eager pass (cudanet_profile), mean of 3"},
+        "gemm_family": {"kernels": "qkv, out, ff1, ff2 of every layer (64 launches)", "achieved": family,
+                        "unit": "TFLOP/s", "frac": family / peak, "flop_per_launch": gemm_fl_pos * B / launches},
         "pass": {"flop_per_position": fl_pos, "tflops_whole_pass": fl_pos * value / world / 1e12,
                  "frac_whole_pass": fl_pos * value / world / 1e12 / peak, "profile_ms": prof},
         "p50_latency_ms_bs64": sweep.get("64", {}).get("p50_ms"),
