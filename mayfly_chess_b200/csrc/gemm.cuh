@@ -7,11 +7,11 @@
 // the reference runs through cuBLASLt (cudanet/gemm.cpp:209-231) or mma.sync (cudanet/kernels_gemm.cu:99-302).
 // Epilogues (kEpi*), each the arithmetic of the reference's product plus what follows it:
 //   kEpiBias      C (16-bit) = acc + bias                            qkv (gemm.h F16_BIAS)
-//   kEpiBiasGelu  C (16-bit) = gelu_erf(acc + bias)                  ff1 + the GELU pass (kernels_trunk.cu:528-549)
+//   kEpiBiasGelu  C (16-bit) = gelu(acc + bias), exact-erf GELU      ff1 + the GELU pass (kernels_trunk.cu:528-549)
 //   kEpiResidual  X (f32)   = X + (acc + bias), in place             out and ff2 (gemm.h F32_BIAS_RESIDUAL)
 //   kEpiF32       C (f32)   = acc + bias                             heads
 // and for the FP8 path (no reference counterpart; acc scaled per column first):
-//   kEpiGeluE4m3  C (e4m3)  = e4m3(gelu_erf(acc + bias) / scale)     ff1, writing ff2's input
+//   kEpiGeluE4m3  C (e4m3)  = e4m3(gelu(acc + bias) / scale)         ff1, writing ff2's input
 //   kEpiResidual16 X (bf16) = X + (acc + bias), in place             out and ff2 on a bf16 residual stream
 //
 // Two kernels, both persistent over output tiles with one CTA per SM:
@@ -132,47 +132,89 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
     static_assert(!PAIR || BN == 256, "the pair kernel covers 256 columns");
 };
 
-// erf(x) by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26:
-//   erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2),  t = 1 / (1 + p x),  x >= 0,
-// |error| <= 1.5e-7, odd in x. The reciprocal and 2^x run on the special-function unit (rcp.approx and
-// ex2.approx, relative errors near 2^-23); the result feeds a 16-bit rounding (2^-9 or 2^-12 relative), so the
-// exact-erf GELU is kept to far below what the output can show, with fewer instructions than erff (the GELU
-// epilogue is the busiest of the four).
-__device__ __forceinline__ float erf_as(float x)
+// ------------------------------------------------------------------------------------------------ GELU
+// Packed f32 pairs: sm_100's f32x2 arithmetic does two IEEE round-to-nearest f32 operations per instruction
+// (the GELU epilogues are issue-bound, so halving their FMA-class instructions matters).
+__device__ __forceinline__ uint64_t pk2(float a, float b)
 {
-    const float ax = fabsf(x);
-    float t;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, ax, 1.0f)));
-    const float poly =
-        t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
-    float e;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-ax * ax * 1.4426950408889634f));
-    return copysignf(fmaf(-poly, e, 1.0f), x);
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float2 upk2(uint64_t r)
+{
+    float2 f;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(r));
+    return f;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b)
+{
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ float rcp_approx(float x)
+{
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float ex2_approx_f(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
-__device__ __forceinline__ float gelu_erf(float x)
-{
-    // F.gelu(approximate="none"): x * 0.5 * (1 + erf(x / sqrt(2)))
-    return x * 0.5f * (1.0f + erf_as(x * 0.70710678118654752440f));
-}
+// s * gelu(x) for the exact-erf GELU (F.gelu(approximate="none") = x * Phi(x), Phi the standard normal CDF).
+// With q = erfc(|x| / sqrt(2)) / 2, x * Phi(x) = relu(x) - |x| q for either sign of x, and q comes from
+// Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26 (|error of erfc| <= 1.5e-7):
+//   erfc(z) = (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),  t = 1 / (1 + p z),  z >= 0.
+// The reciprocal and 2^x run on the special-function unit (rcp.approx, ex2.approx: relative errors near
+// 2^-23), everything else two lanes at a time. No cancellation anywhere (the negative tail is -|x| q
+// directly), so the result is good to a few f32 ulps where |gelu| is not tiny, far below the 16-bit or e4m3
+// rounding that follows.
+struct GeluK {
+    uint64_t c, p, one, a5, a4, a3, a2, a1, nl2e, s;
+    __device__ __forceinline__ explicit GeluK(float scale)
+    {
+        const float h = -0.5f * scale;   // the polynomial carries -s / 2: h t P(t) e = -s q
+        c = pk2(0.70710678118654752440f, 0.70710678118654752440f);
+        p = pk2(0.3275911f, 0.3275911f);
+        one = pk2(1.0f, 1.0f);
+        a5 = pk2(1.061405429f * h, 1.061405429f * h);
+        a4 = pk2(-1.453152027f * h, -1.453152027f * h);
+        a3 = pk2(1.421413741f * h, 1.421413741f * h);
+        a2 = pk2(-0.284496736f * h, -0.284496736f * h);
+        a1 = pk2(0.254829592f * h, 0.254829592f * h);
+        nl2e = pk2(-1.4426950408889634f, -1.4426950408889634f);
+        s = pk2(scale, scale);
+    }
+};
 
-// gelu(x) * s = (x * s) * Phi(x), Phi the standard normal CDF, from the same formula 7.1.26 written for Phi:
-//   q = erfc(|x| / sqrt(2)) / 2 = (t P(t) / 2) exp(-x^2 / 2),  t = 1 / (1 + p |x| / sqrt(2)),
-//   Phi(x) = 1 - q for x >= 0, q for x < 0.
-// The same arithmetic as gelu_erf with the halving folded into the coefficients and no sign fix-up (fewer
-// instructions for the e4m3 epilogue, whose output scale s rides along), and no cancellation in the negative
-// tail, where Phi = q directly.
-__device__ __forceinline__ float gelu_scaled(float x, float s)
+// s * gelu of both lanes of x2
+__device__ __forceinline__ float2 gelu_pair(uint64_t x2, const GeluK& K)
 {
-    const float az = fabsf(x) * 0.70710678118654752440f;
-    float t;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, az, 1.0f)));
-    const float hp = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 0.5307027145f, -0.7265760135f), 0.7107068705f),
-                                        -0.142248368f), 0.127414796f);
-    float e;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(az * (az * -1.4426950408889634f)));
-    const float q = hp * e;
-    return (x * s) * (x >= 0.f ? 1.0f - q : q);
+    const float2 x = upk2(x2);
+    const uint64_t ax = pk2(fabsf(x.x), fabsf(x.y));
+    const uint64_t az = mul2(ax, K.c);                                   // |x| / sqrt(2)
+    const float2 den = upk2(fma2(K.p, az, K.one));
+    const uint64_t t = pk2(rcp_approx(den.x), rcp_approx(den.y));
+    uint64_t h = fma2(t, K.a5, K.a4);
+    h = fma2(t, h, K.a3);
+    h = fma2(t, h, K.a2);
+    h = fma2(t, h, K.a1);
+    h = mul2(t, h);                                                      // -s/2 t P(t)
+    const float2 arg = upk2(mul2(az, mul2(az, K.nl2e)));                 // -z^2 log2(e)
+    const uint64_t nq = mul2(h, pk2(ex2_approx_f(arg.x), ex2_approx_f(arg.y)));   // -s q
+    const float2 xs = upk2(mul2(x2, K.s));
+    return upk2(fma2(ax, nq, pk2(fmaxf(xs.x, 0.f), fmaxf(xs.y, 0.f))));  // s relu(x) - s |x| q
 }
 
 template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -219,10 +261,12 @@ __device__ __forceinline__ void scale_bias32(float (&v)[NV], int off, const floa
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const float4 sc = __ldg(s4 + i), b = __ldg(b4 + i);
-            v[off + 4 * i + 0] = fmaf(v[off + 4 * i + 0], sc.x, b.x);
-            v[off + 4 * i + 1] = fmaf(v[off + 4 * i + 1], sc.y, b.y);
-            v[off + 4 * i + 2] = fmaf(v[off + 4 * i + 2], sc.z, b.z);
-            v[off + 4 * i + 3] = fmaf(v[off + 4 * i + 3], sc.w, b.w);
+            const float2 lo = upk2(fma2(pk2(v[off + 4 * i + 0], v[off + 4 * i + 1]), pk2(sc.x, sc.y), pk2(b.x, b.y)));
+            const float2 hi = upk2(fma2(pk2(v[off + 4 * i + 2], v[off + 4 * i + 3]), pk2(sc.z, sc.w), pk2(b.z, b.w)));
+            v[off + 4 * i + 0] = lo.x;
+            v[off + 4 * i + 1] = lo.y;
+            v[off + 4 * i + 2] = hi.x;
+            v[off + 4 * i + 3] = hi.y;
         }
     } else {
 #pragma unroll
@@ -371,14 +415,20 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                 if constexpr (C::IS_F8) scale_bias32(v, off, colscale, bias, col0 + 32 * p, N);
                 else add_bias32(v, off, bias, col0 + 32 * p, N);
                 if constexpr (EPI == kEpiBiasGelu) {
+                    const GeluK K(1.0f);
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) q[16 * p + i] = pack2<T>(gelu_erf(v[2 * i]), gelu_erf(v[2 * i + 1]));
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 g = gelu_pair(pk2(v[2 * i], v[2 * i + 1]), K);
+                        q[16 * p + i] = pack2<T>(g.x, g.y);
+                    }
                 } else if constexpr (EPI == kEpiGeluE4m3) {
-                    const float inv = ep.out_scale_inv;
+                    const GeluK K(ep.out_scale_inv);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        q[8 * p + i] = pack_e4m3x4(gelu_scaled(v[4 * i], inv), gelu_scaled(v[4 * i + 1], inv),
-                                                   gelu_scaled(v[4 * i + 2], inv), gelu_scaled(v[4 * i + 3], inv));
+                    for (int i = 0; i < 8; ++i) {
+                        const float2 g0 = gelu_pair(pk2(v[4 * i], v[4 * i + 1]), K);
+                        const float2 g1 = gelu_pair(pk2(v[4 * i + 2], v[4 * i + 3]), K);
+                        q[8 * p + i] = pack_e4m3x4(g0.x, g0.y, g1.x, g1.y);
+                    }
                 } else if constexpr (EPI == kEpiBias) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) q[16 * p + i] = pack2<T>(v[2 * i], v[2 * i + 1]);
