@@ -330,6 +330,7 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
 {
     const float* __restrict__ bias = ep.bias;
     const float* __restrict__ colscale = ep.colscale;
+    griddep_wait();   // the output (and residual) buffers are the earlier kernels' until they complete
     constexpr int BN = C::NC * C::CHUNK_COLS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = (warp - 2) >> 2;                      // epilogue group: chunks grp, grp + EG, ...
@@ -558,6 +559,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *L.tmem_slot;
+    if (threadIdx.x == 0) griddep_launch();
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
@@ -567,6 +569,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             uint32_t issued = 0;       // bit s: stage s was loaded at least once
             uint32_t issued_par = 0;   // bit s: parity of the last load into stage s
             bool ok = true;
+            // the weight tiles of this CTA's first stages depend on no earlier kernel: they load while that
+            // kernel finishes; A (an earlier kernel's output) only after griddep_wait
+            const int pre = (int)blockIdx.x < num_tiles ? (k_iters < C::STAGES ? k_iters : C::STAGES) : 0;
+            for (int kb = 0; kb < pre; ++kb) {
+                mbar_arrive_expect_tx(&L.full[kb], C::STAGE_BYTES);
+                tma_load_2d(L.sB + kb * C::B_BYTES, &tmB, &L.full[kb], kb * C::BK, ((int)blockIdx.x % n_tiles) * BN);
+            }
+            griddep_wait();
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
                 const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
                 for (int kb = 0; kb < k_iters; ++kb) {
@@ -574,9 +584,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&L.full[stage], C::STAGE_BYTES);
+                    const bool early = tile == (int)blockIdx.x && kb < pre;   // weights already in flight
+                    if (!early) mbar_arrive_expect_tx(&L.full[stage], C::STAGE_BYTES);
                     tma_load_2d(L.sA + stage * C::A_BYTES, &tmA, &L.full[stage], kb * C::BK, m_blk * C::BM);
-                    tma_load_2d(L.sB + stage * C::B_BYTES, &tmB, &L.full[stage], kb * C::BK, n_blk * BN);
+                    if (!early) tma_load_2d(L.sB + stage * C::B_BYTES, &tmB, &L.full[stage], kb * C::BK, n_blk * BN);
                     issued |= 1u << stage;
                     issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
                     if (++stage == C::STAGES) {
@@ -694,6 +705,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     cluster_sync();   // both CTAs' barriers exist before either signals the other's
     tc_fence_after();
     const uint32_t tmem_base = *L.tmem_slot;
+    if (threadIdx.x == 0) griddep_launch();
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer (both CTAs)
@@ -702,6 +714,14 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             uint32_t phase = 0;
             uint32_t issued = 0, issued_par = 0;
             bool ok = true;
+            // this CTA's half of the first stages' weight tiles loads before griddep_wait (as in gemm_tc_kernel)
+            const int pre = pair < num_tiles ? (k_iters < C::STAGES ? k_iters : C::STAGES) : 0;
+            for (int kb = 0; kb < pre; ++kb) {
+                if (lead) mbar_arrive_expect_tx(&L.full[kb], 2 * C::STAGE_BYTES);
+                tma_load_2d_pair(L.sB + kb * C::B_BYTES, &tmB, mapa_shared(smem_u32(&L.full[kb]), 0), kb * C::BK,
+                                 (pair % n_tiles) * BN + (int)rank * C::B_ROWS);
+            }
+            griddep_wait();
             for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
                 const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
                 const int a_row = m_blk * 2 * C::BM + (int)rank * C::BM;
@@ -711,10 +731,11 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         ok = false;
                         break;
                     }
-                    if (lead) mbar_arrive_expect_tx(&L.full[stage], 2 * C::STAGE_BYTES);
+                    const bool early = tile == pair && kb < pre;   // weights already in flight
+                    if (lead && !early) mbar_arrive_expect_tx(&L.full[stage], 2 * C::STAGE_BYTES);
                     const uint32_t full_lead = mapa_shared(smem_u32(&L.full[stage]), 0);
                     tma_load_2d_pair(L.sA + stage * C::A_BYTES, &tmA, full_lead, kb * C::BK, a_row);
-                    tma_load_2d_pair(L.sB + stage * C::B_BYTES, &tmB, full_lead, kb * C::BK, b_row);
+                    if (!early) tma_load_2d_pair(L.sB + stage * C::B_BYTES, &tmB, full_lead, kb * C::BK, b_row);
                     issued |= 1u << stage;
                     issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
                     if (++stage == C::STAGES) {

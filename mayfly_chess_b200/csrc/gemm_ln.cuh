@@ -124,6 +124,8 @@ gemm_tc_resln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
     else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_wait();   // A, X and H belong to the earlier kernels until they complete
+    if (threadIdx.x == 0) griddep_launch();
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer

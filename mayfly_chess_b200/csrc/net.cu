@@ -131,6 +131,34 @@ static CUtensorMap output_map(void* base, int epi, MapType t16, int M, int N, in
 }
 
 // ------------------------------------------------------------------------------------------------ launchers
+// MAYFLY_CUDANET_PDL=0 launches without programmatic dependent launch (each kernel then starts only after the
+// previous one has completed); the default lets each kernel's prologue, and a product's first weight tiles,
+// overlap the previous kernel's tail (griddep_wait in the kernels keeps the data dependencies).
+static bool pdl_on()
+{
+    static bool on = [] {
+        const char* e = std::getenv("MAYFLY_CUDANET_PDL");
+        return !(e && std::strcmp(e, "0") == 0);
+    }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+static void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_on() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    RT(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
 template <typename TI, typename T, int BN, int EPI>
 static void launch_gemm_bn(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M, int N, int K,
                            const EpiArgs& ep, uint32_t* err, int num_sms, cudaStream_t s)
@@ -149,8 +177,7 @@ static void launch_gemm_bn(const CUtensorMap& ma, const CUtensorMap& mb, const C
     }
     const int tiles = ((M + C::BM - 1) / C::BM) * ((N + BN - 1) / BN);
     const int grid = std::min(tiles, num_sms);
-    gemm_tc_kernel<TI, T, BN, EPI><<<grid, C::THREADS, C::SMEM, s>>>(ma, mb, mc, M, N, K, ep, err);
-    RT(cudaGetLastError());
+    launch_k(gemm_tc_kernel<TI, T, BN, EPI>, dim3(grid), dim3(C::THREADS), C::SMEM, s, ma, mb, mc, M, N, K, ep, err);
 }
 
 // The CTA-pair kernel: 256 x 256 tiles, as many clusters as can be resident at once (a persistent grid must
@@ -180,8 +207,8 @@ static void launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const
     }
     const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
     const int pairs = std::min(tiles, max_pairs[dev]);
-    gemm_tc_pair_kernel<TI, T, EPI><<<2 * pairs, C::THREADS, C::SMEM, s>>>(ma, mb, mc, M, N, K, ep, err);
-    RT(cudaGetLastError());
+    launch_k(gemm_tc_pair_kernel<TI, T, EPI>, dim3(2 * pairs), dim3(C::THREADS), C::SMEM, s, ma, mb, mc, M, N, K, ep,
+             err);
 }
 
 // X += A W^T + bias, then H = LN(X) (gemm_ln.cuh): one cluster of d / 256 CTAs per 128-row block, as many
@@ -212,9 +239,8 @@ static void launch_gemm_resln_ncl(const CUtensorMap& ma, const CUtensorMap& mb, 
     }
     const int m_tiles = (M + 127) / 128;
     const int clusters = std::min(m_tiles, max_clusters[dev]);
-    gemm_tc_resln_kernel<T, NCL><<<clusters * NCL, C::THREADS, C::SMEM, s>>>(ma, mb, mx, mh, M, K, bias, g, b, 1e-5f,
-                                                                            err);
-    RT(cudaGetLastError());
+    launch_k(gemm_tc_resln_kernel<T, NCL>, dim3(clusters * NCL), dim3(C::THREADS), C::SMEM, s, ma, mb, mx, mh, M, K,
+             bias, g, b, 1e-5f, err);
 }
 
 template <typename T>
@@ -345,12 +371,11 @@ static void launch_layernorm(const XT* x, const float* g, const float* b, T* h, 
 {
     const dim3 grid((n + 7) / 8), block(256);
     switch (d) {
-        case 256: layernorm_kernel<T, 2, XT><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
-        case 512: layernorm_kernel<T, 4, XT><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
-        case 1024: layernorm_kernel<T, 8, XT><<<grid, block, 0, s>>>(x, g, b, h, n, row_stride, 1e-5f, mul); break;
+        case 256: launch_k(layernorm_kernel<T, 2, XT>, grid, block, 0, s, x, g, b, h, n, row_stride, 1e-5f, mul); break;
+        case 512: launch_k(layernorm_kernel<T, 4, XT>, grid, block, 0, s, x, g, b, h, n, row_stride, 1e-5f, mul); break;
+        case 1024: launch_k(layernorm_kernel<T, 8, XT>, grid, block, 0, s, x, g, b, h, n, row_stride, 1e-5f, mul); break;
         default: throw std::runtime_error("cudanet_b200: width must be 256, 512 or 1024");
     }
-    RT(cudaGetLastError());
 }
 
 // The TMA map attention reads qkv [rows, 3d] through: boxes of one head's DH columns x 80 rows.
@@ -387,8 +412,8 @@ static void launch_attention_dh(const CUtensorMap& map, TO* att, int B, int d, i
     const int items = B * heads;
     const int grid = std::min(items, per_sm[dev] * sms[dev]);
     const float scale = 1.0f / std::sqrt(static_cast<float>(DH));
-    attention_kernel<T, TO, DH><<<grid, kAttWarps * 32, C::SMEM, s>>>(map, att, B, heads, d, scale, mul, err);
-    RT(cudaGetLastError());
+    launch_k(attention_kernel<T, TO, DH>, dim3(grid), dim3(kAttWarps * 32), C::SMEM, s, map, att, B, heads, d, scale,
+             mul, err);
 }
 
 // att = attention(qkv) in TO (T, or e4m3 of att * mul); map from qkv_map over at least B * 65 rows
@@ -909,10 +934,11 @@ void Net::amax(int slot, const void* p, size_t n, cudaStream_t s)
 {
     if (!amax_) return;
     if (bf16())
-        absmax_kernel<__nv_bfloat16><<<4 * num_sms_, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(p), n, amax_ + slot);
+        launch_k(absmax_kernel<__nv_bfloat16>, dim3(4 * num_sms_), dim3(256), 0, s,
+                 static_cast<const __nv_bfloat16*>(p), n, amax_ + slot);
     else
-        absmax_kernel<__half><<<4 * num_sms_, 256, 0, s>>>(static_cast<const __half*>(p), n, amax_ + slot);
-    RT(cudaGetLastError());
+        launch_k(absmax_kernel<__half>, dim3(4 * num_sms_), dim3(256), 0, s, static_cast<const __half*>(p), n,
+                 amax_ + slot);
 }
 
 void Net::gemm_resln(const CUtensorMap& ma, const void* W, int M, int K, const float* bias, const float* g,
@@ -975,16 +1001,16 @@ static void launch_embed_ln(const Weights& w, const LayerW& l0, const uint8_t* d
                 *ep_mark = w.ptr<float>("ep_mark");
     switch (w.a.d) {
         case 256:
-            embed_ln_kernel<T, 2, XT><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
-                                                          ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
+            launch_k(embed_ln_kernel<T, 2, XT>, grid, block, 0, s, ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b,
+                     hm_emb, ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
             break;
         case 512:
-            embed_ln_kernel<T, 4, XT><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
-                                                          ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
+            launch_k(embed_ln_kernel<T, 4, XT>, grid, block, 0, s, ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b,
+                     hm_emb, ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
             break;
         default:
-            embed_ln_kernel<T, 8, XT><<<grid, block, 0, s>>>(ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb,
-                                                          ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
+            launch_k(embed_ln_kernel<T, 8, XT>, grid, block, 0, s, ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b,
+                     hm_emb, ep_mark, l0.n1_g, l0.n1_b, x, h, rows, 1e-5f, mul);
     }
     RT(cudaGetLastError());
 }
@@ -1156,8 +1182,8 @@ void Net::begin(int B, int wide, const int64_t* ids, const float* cast, const in
     float* pol_d = reinterpret_cast<float*>(d_out_ + kOutHeader);
     float* val_d = pol_d + b * wd;
     float* qv_d = val_d + b;
-    heads_post_kernel<<<(B + 7) / 8, 256, 0, stream_>>>(logits_, I_d, M_d, B, wide, w_.a.moves, pol_d, val_d, qv_d);
-    RT(cudaGetLastError());
+    launch_k(heads_post_kernel, dim3((B + 7) / 8), dim3(256), 0, stream_, static_cast<const float*>(logits_), I_d, M_d,
+             B, wide, w_.a.moves, pol_d, val_d, qv_d);
     RT(cudaMemcpyAsync(h_out_[slot], d_out_, kOutHeader + 4 * b * (2 * wd + 1), cudaMemcpyDeviceToHost, stream_));
     if (want_logits)
         RT(cudaMemcpyAsync(h_logits_[slot], logits_, 4 * b * 2 * w_.a.moves, cudaMemcpyDeviceToHost, stream_));
@@ -1219,8 +1245,8 @@ void Net::evaluate_device(int B, int wide, const int64_t* ids, const float* cast
     } else {
         forward(B, s);
     }
-    heads_post_kernel<<<(B + 7) / 8, 256, 0, s>>>(logits_, I, M, B, wide, w_.a.moves, pol, val, qv);
-    RT(cudaGetLastError());
+    launch_k(heads_post_kernel, dim3((B + 7) / 8), dim3(256), 0, s, static_cast<const float*>(logits_), I, M, B, wide,
+             w_.a.moves, pol, val, qv);
 }
 
 void Net::check(cudaStream_t s)

@@ -89,6 +89,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     }
 }
 
+// ------------------------------------------------------------------------------------------------ PDL
+// Programmatic dependent launch: the library launches every kernel with programmatic stream serialization, so
+// a kernel may start while the one before it finishes. griddep_wait blocks the calling thread until the kernels
+// it depends on have completed and their memory is visible (immediately when there are none); a thread calls it
+// before touching anything an earlier kernel writes or reads. griddep_launch lets the next kernel start
+// launching (its CTAs take whatever the SMs have free and wait in griddep_wait).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------------------------------------ TMA
 // A 2D tile load into shared memory that completes `bytes` of transaction on the barrier. x is the innermost
 // coordinate (elements); callers keep x a multiple of 16 bytes / element size.

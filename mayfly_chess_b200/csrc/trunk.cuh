@@ -119,6 +119,8 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(
     const float* __restrict__ beta, XT* __restrict__ x, T* __restrict__ h, int rows, float eps, float mul)
 {
     constexpr int d = 128 * V;
+    griddep_wait();
+    griddep_launch();
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;   // whole warp
     const int lane = threadIdx.x & 31;
@@ -181,6 +183,8 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const XT* __restrict__ x
                                                         int row_stride, float eps, float mul)
 {
     constexpr int d = 128 * V;
+    griddep_wait();
+    griddep_launch();
     const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (i >= n) return;
     const int lane = threadIdx.x & 31;
@@ -293,6 +297,8 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const __grid_
         tma_prefetch_desc(&tmQKV);
     }
     __syncthreads();
+    griddep_wait();   // qkv and att belong to the earlier kernels until they complete
+    if (tid == 0) griddep_launch();
 
     auto issue = [&](int item, int buf) {
         const int b = item / heads, h = item - b * heads;
@@ -479,6 +485,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ p, size_t n, unsigned int* __restrict__ out)
 {
     float m = 0.f;
+    griddep_wait();
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         m = fmaxf(m, fabsf(to_f32<T>(p[i])));
     m = warp_max(m);
@@ -498,6 +505,7 @@ __global__ void __launch_bounds__(256) heads_post_kernel(const float* __restrict
                                                          int moves, float* __restrict__ pol,
                                                          float* __restrict__ val, float* __restrict__ qv)
 {
+    griddep_wait();
     const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (b >= B) return;
     const int lane = threadIdx.x & 31;
