@@ -23,6 +23,10 @@ independent evaluator per GPU, no collective on the data path (weak scaling: 1,0
   cpu_baseline  the CPU fp32 restatement of the reference forward (oracle/, test infrastructure) on a bounded
              sample on this host's cores.
 
+--total 8192 is BASELINE config 5 as strong scaling: 8,192 positions per step split over the ranks (each rank's
+share from position rank * 8192 / N). The default keeps 1,024 positions per GPU (weak scaling), the metric's
+configuration.
+
 --precision e4m3 --batch 4096 is BASELINE config 4: the same net with e4m3 weight matrices (per-output-channel
 scales) and e4m3 product inputs at static per-layer scales calibrated on 256 seed-1 positions outside every
 rank's batch (mayfly_chess_b200.quant, one bf16 pass on the GPU before the file is written); its roofline
@@ -61,13 +65,6 @@ def flops_per_position(d=1024, layers=16, heads=16, ff=2048, tokens=65, moves=41
     gemm = tokens * layers * (3 * d * d + d * d + 2 * d * ff)
     att = layers * heads * 2 * tokens * tokens * (d // heads)
     return 2 * (gemm + att + 2 * moves * d), 2 * gemm
-
-
-def rank_env():
-    r = int(os.environ.get("RANK", "0"))
-    w = int(os.environ.get("WORLD_SIZE", "1"))
-    lr = int(os.environ.get("LOCAL_RANK", str(r)))
-    return r, w, lr
 
 
 class Clocks:
@@ -151,7 +148,8 @@ def bench_reference(args):
     """--impl reference: the reference's CPU implementation of the path (its fp32 forward and _collect
     arithmetic, restated in oracle/chessnet_oracle.py; the reference's own code cannot travel here) timed with
     every host thread; each step is a bounded sample of the workload's positions."""
-    rank, world, _ = rank_env()
+    from mayfly_chess_b200 import replicas
+    rank, world, _ = replicas.rank_env()
     if rank != 0:
         return
     import torch
@@ -191,6 +189,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1024)
+    ap.add_argument("--total", type=int, default=0,
+                    help="strong scaling (config 5): this many positions per step over all ranks (overrides --batch)")
     ap.add_argument("--precision", default="bf16", choices=["bf16", "f16", "e4m3"])
     ap.add_argument("--impl", default="own", choices=["own", "reference"])
     ap.add_argument("--ref-sample", type=int, default=16, help="positions per step of the reference arm")
@@ -208,8 +208,9 @@ def main():
     from mayfly_chess_b200 import weights as W
     from mayfly_chess_b200.cudanet_py import CudaNet
     from mayfly_chess_b200.inputs import PositionSet
+    from mayfly_chess_b200 import replicas
 
-    rank, world, local = rank_env()
+    rank, world, local = replicas.rank_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
     torch.cuda.set_device(local)
@@ -218,23 +219,21 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
 
     def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+        replicas.barrier(dist, torch.cuda.synchronize)
 
     def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return replicas.max_over_ranks(x, dist, "cuda")
 
-    B = args.batch
+    ps = PositionSet(POSITIONS)
+    try:
+        start, B = replicas.shard(rank, world, len(ps), total=args.total or None,
+                                  per_rank=None if args.total else args.batch)
+    except ValueError as e:
+        raise SystemExit(str(e))
     arch = W.FULL
     st = W.random_state(arch, 1)
     tmp = tempfile.mkdtemp(prefix="mayfly_b200_")
     path = os.path.join(tmp, f"net_{args.precision}_{rank}.cnw")
-    ps = PositionSet(POSITIONS)
     os.environ.setdefault("MAYFLY_CUDANET_MAX_BATCH", str(max(B, 1024)))
     if args.precision == "e4m3":
         from mayfly_chess_b200 import quant
@@ -244,10 +243,6 @@ def main():
         W.write_cnw(path, st, arch, args.precision)
     net = CudaNet(path, device=local)
     os.remove(path)
-    if B > len(ps):
-        raise SystemExit(f"--batch {B}: the position set holds {len(ps)}")
-    start = (rank * B) % len(ps)
-    start = start if start + B <= len(ps) else 0
     b = ps.batch(start, B)
     wide = b["I"].shape[1]
 
@@ -346,7 +341,8 @@ def main():
         return
     out = {
         "metric": METRIC, "value": value, "unit": "positions/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong" if args.total else "weak",
         "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
         "config": {"workload": ("config 4 (e4m3 layer products, calibrated static input scales)"
                                 if args.precision == "e4m3" else "config 2") +
