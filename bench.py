@@ -61,10 +61,17 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 
 def flops_per_position(d=1024, layers=16, heads=16, ff=2048, tokens=65, moves=4162):
-    """Algorithmic FLOPs of one position (multiply-add = 2): the four trunk products, attention, the heads."""
-    gemm = tokens * layers * (3 * d * d + d * d + 2 * d * ff)
-    att = layers * heads * 2 * tokens * tokens * (d // heads)
-    return 2 * (gemm + att + 2 * moves * d), 2 * gemm
+    """FLOPs of one position (multiply-add = 2): (algorithmic, executed, executed by the trunk products).
+    Algorithmic: the four trunk products, attention and the heads of every token. Executed: the evaluator runs
+    the last layer past its qkv product for the CLS row alone (the heads read nothing else), so that layer's
+    attention, out and FFN count one query / one row."""
+    dh = d // heads
+    layer = 3 * d * d + d * d + 2 * d * ff
+    gemm = tokens * layers * layer
+    att = layers * heads * 2 * tokens * tokens * dh
+    gemm_x = tokens * (layers - 1) * layer + tokens * 3 * d * d + (d * d + 2 * d * ff)
+    att_x = (layers - 1) * heads * 2 * tokens * tokens * dh + heads * 2 * tokens * dh
+    return 2 * (gemm + att + 2 * moves * d), 2 * (gemm_x + att_x + 2 * moves * d), 2 * gemm_x
 
 
 class Clocks:
@@ -293,14 +300,14 @@ def main():
 
     # ---------------------------------------------------------------- roofline of the dominant kernel
     prof = net.profile(B, reps=3)
-    fl_pos, gemm_fl_pos = flops_per_position()
+    fl_alg, fl_pos, gemm_fl_pos = flops_per_position()
     qkv_flop = 2.0 * B * arch.tokens * 3 * arch.d * arch.d
     achieved = qkv_flop / (prof["qkv"] / arch.layers / 1000.0) / 1e12
     traffic = QKV_TRAFFIC_PER_POS.get(args.precision)
     traffic = traffic * B if traffic is not None else None
     trunk_gemm_ms = prof["qkv"] + prof["out"] + prof["ff1"] + prof["ff2"]
     launches = 4 * arch.layers
-    family = gemm_fl_pos * B / launches / (trunk_gemm_ms / 1000.0 / launches) / 1e12
+    family = gemm_fl_pos * B / (trunk_gemm_ms / 1000.0) / 1e12
     peaks, peak_kind = load_peaks()
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
     peak_source = f"{peak_kind} bf16 sustained"
@@ -362,7 +369,8 @@ def main():
                      "timing": "CUDA events around each step of an eager pass (cudanet_profile), mean of 3"},
         "gemm_family": {"kernels": "qkv, out, ff1, ff2 of every layer (64 launches)", "achieved": family,
                         "unit": "TFLOP/s", "frac": family / peak, "flop_per_launch": gemm_fl_pos * B / launches},
-        "pass": {"flop_per_position": fl_pos, "tflops_whole_pass": fl_pos * value / world / 1e12,
+        "pass": {"flop_per_position": fl_pos, "flop_per_position_algorithmic": fl_alg,
+                 "tflops_whole_pass": fl_pos * value / world / 1e12,
                  "frac_whole_pass": fl_pos * value / world / 1e12 / peak, "profile_ms": prof},
         "p50_latency_ms_bs64": sweep.get("64", {}).get("p50_ms"),
         "clocks": clk,

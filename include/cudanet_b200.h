@@ -138,6 +138,11 @@ CUDANET_API int cudanet_k_gemm_resln(int dtype, const void* A, const void* W, co
 CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,
                                     char* err, int err_len);
 
+/* att[b, :] = the attention output of board b's CLS query only (token 0 of each board), att dense [B, d]: what
+ * the last layer needs, since the heads read the CLS row alone. No counterpart in the reference. */
+CUDANET_API int cudanet_k_attention_cls(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,
+                                        char* err, int err_len);
+
 /* h[i] = LayerNorm(x[i * row_stride]) (f32 in, 16-bit out), i < n, eps 1e-5. */
 CUDANET_API int cudanet_k_layernorm(int dtype, const float* x, const float* g, const float* b, void* h, int n,
                                     int d, int row_stride, void* stream, char* err, int err_len);

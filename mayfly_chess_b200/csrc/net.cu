@@ -428,6 +428,19 @@ static void launch_attention(const CUtensorMap& map, TO* att, int B, int d, int 
     else throw std::runtime_error("cudanet_b200: head width must be 32 or 64");
 }
 
+// att_cls [B, d] = attention of the CLS query of every board (TO: T, or e4m3 of att * mul)
+template <typename T, typename TO>
+static void launch_attention_cls(const T* qkv, TO* att, int B, int d, int heads, float mul, cudaStream_t s)
+{
+    if (B < 1 || heads < 1 || d % heads) throw std::runtime_error("cudanet_b200: bad attention sizes");
+    const int dh = d / heads;
+    const dim3 grid((B * heads + 7) / 8), block(256);
+    const float scale = 1.0f / std::sqrt(static_cast<float>(dh));
+    if (dh == 64) launch_k(attention_cls_kernel<T, TO, 64>, grid, block, 0, s, qkv, att, B, heads, d, scale, mul);
+    else if (dh == 32) launch_k(attention_cls_kernel<T, TO, 32>, grid, block, 0, s, qkv, att, B, heads, d, scale, mul);
+    else throw std::runtime_error("cudanet_b200: head width must be 32 or 64");
+}
+
 // ------------------------------------------------------------------------------------------------ weights
 struct Arch {
     int d = 0, layers = 0, heads = 0, ff = 0, tokens = 0, moves = 0;
@@ -725,7 +738,7 @@ private:
     bool use_graph_ = true;
     CUtensorMap map_h_, map_att_, map_ff_, map_cls_, map_qkv_;
     std::map<std::pair<const void*, int>, CUtensorMap> wmaps_;
-    std::map<std::tuple<const void*, int, int, int>, CUtensorMap> omaps_;   // (out, epi, M, N)
+    std::map<std::tuple<const void*, int, int, int, int>, CUtensorMap> omaps_;   // (out, epi, M, N, ldc)
 
     struct Fly {
         int B, wide, slot;
@@ -919,7 +932,7 @@ void Net::gemm(int epi, const CUtensorMap& ma, const void* W, bool w_f8, int M, 
 {
     const int bn = pick_bn(M, N, K, epi, num_sms_);
     const CUtensorMap& mb = wmap(W, w_f8 ? MapType::U8 : type16(bf16()), N, K, static_cast<int>(w_box_rows(bn)));
-    const auto okey = std::make_tuple(static_cast<const void*>(out), epi, M, N);
+    const auto okey = std::make_tuple(static_cast<const void*>(out), epi, M, N, ldc);
     auto it = omaps_.find(okey);
     if (it == omaps_.end()) it = omaps_.emplace(okey, output_map(out, epi, type16(bf16()), M, N, ldc)).first;
     if (w_f8)
@@ -946,10 +959,10 @@ void Net::gemm_resln(const CUtensorMap& ma, const void* W, int M, int K, const f
 {
     const int d = w_.a.d;
     const CUtensorMap& mb = wmap(W, type16(bf16()), d, K, 256);
-    const auto xkey = std::make_tuple(static_cast<const void*>(x_), static_cast<int>(kEpiResidual), M, d);
+    const auto xkey = std::make_tuple(static_cast<const void*>(x_), static_cast<int>(kEpiResidual), M, d, d);
     auto ix = omaps_.find(xkey);
     if (ix == omaps_.end()) ix = omaps_.emplace(xkey, output_map(x_, kEpiResidual, type16(bf16()), M, d, d)).first;
-    const auto hkey = std::make_tuple(static_cast<const void*>(h_), static_cast<int>(kEpiBias), M, d);
+    const auto hkey = std::make_tuple(static_cast<const void*>(h_), static_cast<int>(kEpiBias), M, d, d);
     auto ih = omaps_.find(hkey);
     if (ih == omaps_.end()) ih = omaps_.emplace(hkey, output_map(h_, kEpiBias, type16(bf16()), M, d, d)).first;
     if (bf16())
@@ -966,6 +979,18 @@ static bool fuse_ln()
     static bool on = [] {
         const char* e = std::getenv("MAYFLY_CUDANET_FUSE_LN");
         return e && std::strcmp(e, "1") == 0;
+    }();
+    return on;
+}
+
+// The heads read the CLS row alone (chess_net.py:194), so after the last layer's qkv product the pass computes
+// the CLS rows only: attention for the CLS query, then out, LN2 and the FFN on B rows (the residual stream's
+// CLS rows through a 65-row pitch). Exact; MAYFLY_CUDANET_CLS_ONLY=0 runs the whole last layer instead.
+static bool cls_only()
+{
+    static bool on = [] {
+        const char* e = std::getenv("MAYFLY_CUDANET_CLS_ONLY");
+        return !(e && std::strcmp(e, "0") == 0);
     }();
     return on;
 }
@@ -1033,6 +1058,20 @@ template <typename T> void Net::forward_t(int B, cudaStream_t s)
         mark(kPQkv, s);
         gemm(kEpiBias, map_h_, l.qkv_w, false, rows, 3 * d, d, EpiArgs{l.qkv_b, nullptr, 1.f}, qkv_, 3 * d, s);
         mark(kPAtt, s);
+        if (last && cls_only() && !amax_) {
+            // the CLS rows only (cls_only): dense [B, ...] operands in att_, h_, ff_; x's CLS rows at pitch 65 d
+            const int xp = kTokens * d;
+            launch_attention_cls<T, T>(static_cast<const T*>(qkv_), static_cast<T*>(att_), B, d, a.heads, 1.f, s);
+            mark(kPOut, s);
+            gemm(kEpiResidual, map_att_, l.out_w, false, B, d, d, EpiArgs{l.out_b, nullptr, 1.f}, x_, xp, s);
+            mark(kPLn2, s);
+            launch_layernorm<T>(x_, l.n2_g, l.n2_b, h, B, d, kTokens, 1.f, s);
+            mark(kPFf1, s);
+            gemm(kEpiBiasGelu, map_h_, l.ff1_w, false, B, ff, d, EpiArgs{l.ff1_b, nullptr, 1.f}, ff_, ff, s);
+            mark(kPFf2, s);
+            gemm(kEpiResidual, map_ff_, l.ff2_w, false, B, d, ff, EpiArgs{l.ff2_b, nullptr, 1.f}, x_, xp, s);
+            continue;
+        }
         launch_attention<T, T>(map_qkv_, static_cast<T*>(att_), B, d, a.heads, 1.f, err_word(), s);
         amax(4 * i + 1, att_, nd, s);
         mark(kPOut, s);
@@ -1086,6 +1125,21 @@ void Net::forward_f8(int B, cudaStream_t s)
         mark(kPQkv, s);
         gemm(kEpiBias, map_h_, l.qkv_w, true, rows, 3 * d, d, EpiArgs{l.qkv_b, l.qkv_cs, 1.f}, qkv_, 3 * d, s);
         mark(kPAtt, s);
+        if (i + 1 == a.layers && cls_only()) {
+            // the CLS rows only, as in forward_t
+            const int xp = kTokens * d;
+            launch_attention_cls<T, F8>(static_cast<const T*>(qkv_), static_cast<F8*>(att_), B, d, a.heads, l.inv_out,
+                                        s);
+            mark(kPOut, s);
+            gemm(kEpiResidual16, map_att_, l.out_w, true, B, d, d, EpiArgs{l.out_b, l.out_cs, 1.f}, x, xp, s);
+            mark(kPLn2, s);
+            launch_layernorm<F8, T>(x, l.n2_g, l.n2_b, h, B, d, kTokens, l.inv_ff1, s);
+            mark(kPFf1, s);
+            gemm(kEpiGeluE4m3, map_h_, l.ff1_w, true, B, ff, d, EpiArgs{l.ff1_b, l.ff1_cs, l.inv_ff2}, ff_, ff, s);
+            mark(kPFf2, s);
+            gemm(kEpiResidual16, map_ff_, l.ff2_w, true, B, d, ff, EpiArgs{l.ff2_b, l.ff2_cs, 1.f}, x, xp, s);
+            continue;
+        }
         launch_attention<T, F8>(map_qkv_, static_cast<F8*>(att_), B, d, a.heads, l.inv_out, err_word(), s);
         mark(kPOut, s);
         gemm(kEpiResidual16, map_att_, l.out_w, true, rows, d, d, EpiArgs{l.out_b, l.out_cs, 1.f}, x, d, s);
@@ -1731,6 +1785,26 @@ CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B
             mf::attention_once<__half, __half>(qkv, att, B, d, heads, 1.f, s, "cudanet_k_attention");
         else
             throw std::runtime_error("cudanet_k_attention: dtype must be 0 (f16) or 1 (bf16)");
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_k_attention_cls(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,
+                                        char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_k_attention_cls: unknown exception", [&] {
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(att)) & 15)
+            throw std::runtime_error("cudanet_k_attention_cls: qkv and att must be 16-byte aligned");
+        if (dtype == 1)
+            mf::launch_attention_cls<__nv_bfloat16, __nv_bfloat16>(static_cast<const __nv_bfloat16*>(qkv),
+                                                                   static_cast<__nv_bfloat16*>(att), B, d, heads, 1.f, s);
+        else if (dtype == 0)
+            mf::launch_attention_cls<__half, __half>(static_cast<const __half*>(qkv), static_cast<__half*>(att), B, d,
+                                                     heads, 1.f, s);
+        else
+            throw std::runtime_error("cudanet_k_attention_cls: dtype must be 0 (f16) or 1 (bf16)");
+        mf::RT(cudaStreamSynchronize(s));
         return 0;
     });
 }

@@ -255,13 +255,17 @@ __device__ __forceinline__ float ex2_approx(float x)
 }
 
 constexpr int kAttRows = 80;     // 65 tokens padded to 5 tiles of 16
+#ifndef MF_ATT_BUFFERS
+#define MF_ATT_BUFFERS 2
+#endif
+constexpr int kAttBuffers = MF_ATT_BUFFERS;   // Q/K/V tile sets per CTA: 2 streams the next item during the math
 constexpr int kAttWarps = 5;
 
 template <int DH> struct AttCfg {
     static constexpr int ROWB = DH * 2;                                  // bytes of a 16-bit tile row
     static constexpr uint32_t TILE = kAttRows * ROWB;                    // one of Q, K, V
     static constexpr uint32_t SET = 3 * TILE;                            // one item's tiles
-    static constexpr size_t SMEM = 1024 + 2 * (size_t)SET + 64;          // two sets + barriers
+    static constexpr size_t SMEM = 1024 + kAttBuffers * (size_t)SET + 64;   // the sets + barriers
     static_assert(DH == 64 || DH == 32, "head width 32 or 64");
 };
 
@@ -285,14 +289,14 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const __grid_
     constexpr int CH = DH * 2 / 16;           // 16-byte chunks per 16-bit row
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(base + 2 * C::SET);
+    constexpr int NB = kAttBuffers;
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + NB * C::SET);
     volatile uint32_t* ok_flag = reinterpret_cast<volatile uint32_t*>(full + 2);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int items = B * heads;
     if (tid == 0) {
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
+        for (int i = 0; i < NB; ++i) mbar_init(&full[i], 1);
         fence_barrier_init();
         tma_prefetch_desc(&tmQKV);
     }
@@ -319,13 +323,13 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const __grid_
     const float sl2 = scale * 1.4426950408889634f;
     int n = 0;   // items this CTA has computed
     for (int item = blockIdx.x; item < items; item += gridDim.x, ++n) {
-        const int buf = n & 1;
+        const int buf = n % NB;
         if (tid == 0) {
-            if (item + (int)gridDim.x < items) {
+            if (NB == 2 && item + (int)gridDim.x < items) {
                 issue(item + gridDim.x, buf ^ 1);   // that buffer's last reader finished before the last barrier
                 ++issued;
             }
-            *ok_flag = mbar_wait(&full[buf], (n >> 1) & 1, err, kErrTmaFull) ? 1u : 0u;
+            *ok_flag = mbar_wait(&full[buf], (n / NB) & 1, err, kErrTmaFull) ? 1u : 0u;
         }
         __syncthreads();
         if (!*ok_flag) break;
@@ -467,20 +471,109 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const __grid_
         }
         fence_proxy_async_smem();   // this thread's shared-memory reads and writes of the buffer come before
         __syncthreads();            // the TMA writes that refill it next
+        if (NB == 1 && tid == 0 && item + (int)gridDim.x < items) {
+            issue(item + gridDim.x, 0);
+            ++issued;
+        }
     }
     // the loads thread 0 started have landed before the CTA leaves (only after a failed wait are any pending)
     if (tid == 0)
-        for (int k = n; k < issued; ++k) mbar_wait(&full[k & 1], (k >> 1) & 1, err, kErrTmaFull);
+        for (int k = n; k < issued; ++k) mbar_wait(&full[k % NB], (k / NB) & 1, err, kErrTmaFull);
+}
+
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+
+// ------------------------------------------------------------------------------------------------ CLS attention
+// The last layer needs attention for the CLS query only (the heads read the CLS row alone, chess_net.py:194):
+// att_cls[b, head] = softmax(q_cls k^T / sqrt(DH)) v over the 65 keys of board b. One warp per (board, head):
+// lane j scores keys j, j + 32 and j + 64 (q broadcast to every lane in registers, each key row read whole),
+// the softmax is a warp reduction, then lane j accumulates output dims 2j, 2j + 1 over the 65 keys (each key's
+// probability broadcast by a shuffle). att_cls [B, d] is dense; TO is T, or e4m3 of att * mul (the FP8 path).
+template <typename T, typename TO, int DH>
+__global__ void __launch_bounds__(256) attention_cls_kernel(const T* __restrict__ qkv, TO* __restrict__ att,
+                                                            int B, int heads, int d, float scale, float mul)
+{
+    static_assert(DH == 64 || DH == 32, "head width 32 or 64");
+    griddep_wait();
+    griddep_launch();
+    const int item = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (item >= B * heads) return;   // whole warp
+    const int lane = threadIdx.x & 31;
+    const int b = item / heads, h = item - b * heads;
+    const size_t ld = 3 * (size_t)d;
+    const T* q = qkv + (size_t)b * kTokens * ld + (size_t)h * DH;   // token 0's q
+    const T* kb = q + d;                                              // token 0's k; token t at + t * ld
+    const T* vb = q + 2 * (size_t)d;
+
+    float qf[DH];
+#pragma unroll
+    for (int c = 0; c < DH / 8; ++c) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(q) + c);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            qf[8 * c + 2 * i] = to_f32<T>(reinterpret_cast<const T*>(&w[i])[0]);
+            qf[8 * c + 2 * i + 1] = to_f32<T>(reinterpret_cast<const T*>(&w[i])[1]);
+        }
+    }
+    const float sl2 = scale * 1.4426950408889634f;
+    float sc[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+        const int key = lane + 32 * j;
+        sc[j] = -INFINITY;
+        if (key < kTokens) {
+            const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)key * ld);
+            float acc = 0.f;
+#pragma unroll
+            for (int c = 0; c < DH / 8; ++c) {
+                const uint4 u = __ldg(kr + c);
+                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc = fmaf(qf[8 * c + 2 * i], to_f32<T>(reinterpret_cast<const T*>(&w[i])[0]), acc);
+                    acc = fmaf(qf[8 * c + 2 * i + 1], to_f32<T>(reinterpret_cast<const T*>(&w[i])[1]), acc);
+                }
+            }
+            sc[j] = acc * sl2;
+        }
+    }
+    const float mx = warp_max(fmaxf(fmaxf(sc[0], sc[1]), sc[2]));
+    float p[3], sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+        p[j] = ex2_approx(sc[j] - mx);   // 2^-inf = 0 for the keys past 64
+        sum += p[j];
+    }
+    sum = warp_sum(sum);
+    float o0 = 0.f, o1 = 0.f;
+    const bool owns = 2 * lane < DH;   // lane j: output dims 2j, 2j + 1
+    for (int key = 0; key < kTokens; ++key) {
+        const float pk = __shfl_sync(0xffffffffu, p[key >> 5], key & 31);
+        if (owns) {
+            const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(vb + (size_t)key * ld) + lane);
+            o0 = fmaf(pk, to_f32<T>(reinterpret_cast<const T*>(&w)[0]), o0);
+            o1 = fmaf(pk, to_f32<T>(reinterpret_cast<const T*>(&w)[1]), o1);
+        }
+    }
+    if (!owns) return;
+    const float inv = 1.f / sum;
+    const size_t oc = (size_t)b * d + (size_t)h * DH + 2 * lane;
+    if constexpr (is_e4m3<TO>) {
+        *reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(att) + oc) = static_cast<uint16_t>(
+            __nv_cvt_float2_to_fp8x2(make_float2(o0 * inv * mul, o1 * inv * mul), __NV_SATFINITE, __NV_E4M3));
+    } else {
+        *reinterpret_cast<uint32_t*>(att + oc) = pack2<T>(o0 * inv, o1 * inv);
+    }
 }
 
 // ------------------------------------------------------------------------------------------------ calibration
 // out = max(out, max |p[i]|) over i < n (out holds the f32 bits: non-negative floats order like their bits).
 // Records the ranges of the four product inputs in a 16-bit pass, from which the FP8 path's static input
 // scales are set.
-template <typename T> __device__ __forceinline__ float to_f32(T v);
-template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
-template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
-
 template <typename T>
 __global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ p, size_t n, unsigned int* __restrict__ out)
 {

@@ -82,6 +82,8 @@ def load(dll=None):
         lib.cudanet_k_gemm_resln.restype = i32
         lib.cudanet_k_attention.argtypes = [i32, vp, vp, i32, i32, i32, vp, cp, i32]
         lib.cudanet_k_attention.restype = i32
+        lib.cudanet_k_attention_cls.argtypes = [i32, vp, vp, i32, i32, i32, vp, cp, i32]
+        lib.cudanet_k_attention_cls.restype = i32
         lib.cudanet_k_layernorm.argtypes = [i32, vp, vp, vp, vp, i32, i32, i32, vp, cp, i32]
         lib.cudanet_k_layernorm.restype = i32
         f32 = ctypes.c_float
@@ -370,6 +372,17 @@ def k_attention(qkv, att, B, d, heads, dll=None):
                                  ERR_LEN)
     if rc != 0:
         raise RuntimeError(f"cudanet_k_attention: {_msg(err)}")
+    return att
+
+
+def k_attention_cls(qkv, att, B, d, heads, dll=None):
+    """att [B, d] = attention of each board's CLS query (token 0) over its 65 tokens."""
+    lib = load(dll)
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_k_attention_cls(_dtype_code(qkv), qkv.data_ptr(), att.data_ptr(), B, d, heads, _stream(), err,
+                                     ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_k_attention_cls: {_msg(err)}")
     return att
 
 

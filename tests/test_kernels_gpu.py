@@ -111,6 +111,26 @@ def test_attention(k, dtype, d, heads, B):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("d,heads", [(1024, 16), (256, 8)])
+@pytest.mark.parametrize("B", [1, 3, 300])
+def test_attention_cls(k, dtype, d, heads, B):
+    """The last layer's attention for each board's CLS query only, against the full attention's row 0."""
+    rows = B * 65
+    qkv = torch.randn(rows, 3 * d, device="cuda").to(dtype)
+    att = torch.full((B, d), float("nan"), device="cuda", dtype=dtype)
+    k.k_attention_cls(qkv, att, B, d, heads)
+    torch.cuda.synchronize()
+    dh = d // heads
+    q, kk, v = qkv.float().view(B, 65, 3, heads, dh).permute(2, 0, 3, 1, 4).unbind(0)
+    o = torch.softmax(q[:, :, :1] @ kk.transpose(-1, -2) / math.sqrt(dh), -1) @ v     # (B, heads, 1, dh)
+    ref = o.reshape(B, d)
+    # f32 dot products and probabilities (no 16-bit rounding of P), one rounding of the output
+    rel = 2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11
+    excess = ((att.float() - ref).abs() - (1e-4 + rel * ref.abs())).max().item()
+    assert math.isfinite(excess) and excess <= 0, excess
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("d", [256, 1024])
 @pytest.mark.parametrize("stride", [1, 65])
 def test_layernorm(k, dtype, d, stride):
