@@ -28,6 +28,7 @@
 #include <vector>
 
 #include "../../include/cudanet_b200.h"
+#include "attention_tc.cuh"
 #include "gemm_ln.cuh"
 #include "json_min.h"
 #include "trunk.cuh"
@@ -416,6 +417,38 @@ static void launch_attention_dh(const CUtensorMap& map, TO* att, int B, int d, i
              mul, err);
 }
 
+// MAYFLY_CUDANET_ATT_TC=0 runs head width 64 on the mma.sync kernel instead of the tensor-memory one.
+static bool att_tc()
+{
+    static bool on = [] {
+        const char* e = std::getenv("MAYFLY_CUDANET_ATT_TC");
+        return !(e && std::strcmp(e, "0") == 0);
+    }();
+    return on;
+}
+
+// the tcgen05 attention (attention_tc.cuh): one CTA per SM, persistent over the (board, head) items
+template <typename T, typename TO>
+static void launch_attention_tc(const CUtensorMap& map, TO* att, int B, int d, int heads, float mul, uint32_t* err,
+                                cudaStream_t s)
+{
+    using C = AttTcCfg;
+    static bool attr[64] = {};
+    static int sms[64] = {};
+    int dev = 0;
+    RT(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw std::runtime_error("cudanet_b200: device index out of range");
+    if (!attr[dev]) {
+        RT(cudaFuncSetAttribute(attention_tc_kernel<T, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+        RT(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+        attr[dev] = true;
+    }
+    const int items = B * heads;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(C::DH));
+    launch_k(attention_tc_kernel<T, TO>, dim3(std::min(items, sms[dev])), dim3(C::THREADS), C::SMEM, s, map, att, B,
+             heads, d, scale, mul, err);
+}
+
 // att = attention(qkv) in TO (T, or e4m3 of att * mul); map from qkv_map over at least B * 65 rows
 template <typename T, typename TO>
 static void launch_attention(const CUtensorMap& map, TO* att, int B, int d, int heads, float mul, uint32_t* err,
@@ -423,7 +456,8 @@ static void launch_attention(const CUtensorMap& map, TO* att, int B, int d, int 
 {
     if (B < 1 || heads < 1 || d % heads) throw std::runtime_error("cudanet_b200: bad attention sizes");
     const int dh = d / heads;
-    if (dh == 64) launch_attention_dh<T, TO, 64>(map, att, B, d, heads, mul, err, s);
+    if (dh == 64 && att_tc()) launch_attention_tc<T, TO>(map, att, B, d, heads, mul, err, s);
+    else if (dh == 64) launch_attention_dh<T, TO, 64>(map, att, B, d, heads, mul, err, s);
     else if (dh == 32) launch_attention_dh<T, TO, 32>(map, att, B, d, heads, mul, err, s);
     else throw std::runtime_error("cudanet_b200: head width must be 32 or 64");
 }
