@@ -138,6 +138,11 @@ CUDANET_API int cudanet_k_gemm_resln(int dtype, const void* A, const void* W, co
 CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,
                                     char* err, int err_len);
 
+/* cudanet_k_attention on the tensor-memory kernel (tcgen05 products, head width 64 only), whichever kernel the
+ * evaluator picks for this output type. */
+CUDANET_API int cudanet_k_attention_tc(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,
+                                       char* err, int err_len);
+
 /* att[b, :] = the attention output of board b's CLS query only (token 0 of each board), att dense [B, d]: what
  * the last layer needs, since the heads read the CLS row alone. No counterpart in the reference. */
 CUDANET_API int cudanet_k_attention_cls(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,

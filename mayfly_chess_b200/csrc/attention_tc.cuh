@@ -3,19 +3,22 @@
 // as tcgen05.mma and the scores and outputs in tensor memory.
 //
 // Per item (board b, head h), with the 65 tokens of board b as rows 0..64:
-//   S [128 x 80]  = Q K^T        A = Q tile (rows 0..79 from TMA, 80..127 zero), B = K tile (80 keys), K-major
-//   P             = 2^(S * scale * log2 e - row max), keys 65..79 masked to 0 (bf16 or f16, in shared memory)
-//   O [128 x 64]  = P V          A = P (K = 80 keys), B = the V tile read MN-major (its natural layout)
-//   att row r     = O[r] / sum(P[r]), r < 65
-// One CTA per SM, persistent over items blockIdx.x, + gridDim.x, ...; a ring of four Q/K/V tile sets keeps the
-// loads several items ahead, and two compute slots (a P tile and tensor-memory columns for S and O) let the MMAs
-// and the softmax of neighbouring items overlap:
-//   warp 0       one thread TMA-loads Q, K, V of item n into load slot n % 4 (boxes of 64 columns x 80 rows)
-//   warp 1       one thread issues S(n), then P(n-1) V(n-1); commits signal S ready, O ready, tiles free
-//   warps 2..5   group 0, items of slot 0; warps 6..9 group 1, slot 1: thread = tensor-memory lane = query row:
-//                the row's 80 scores come in with tcgen05.ld, the softmax runs in registers with no shuffles,
-//                P goes to shared memory in the 128-byte-swizzled layout the second MMA reads, then the row of O
-//                comes back, is normalised and stored.
+//   S [128 x 80] = Q K^T       A = Q tile (rows 0..79 from TMA, 80..127 zero), B = K tile (keys 0..79), K-major
+//                  (rows past 64 are padding: the warp of rows 96..127 skips them)
+//   P            = 2^(S * scale * log2 e - row max), keys 65..79 masked to 0, rounded to the 16-bit type
+//   O [128 x 64] = P[:, 0:64] V[0:64] + P[:, 64] V[64]
+//                  the first term a tcgen05.mma (A = P in the Q tile's place, B = the V tile read MN-major, its
+//                  natural layout), the second, the last live key, a rank-1 update on the CUDA cores
+//   att row r    = O[r] / sum(P[r]), r < 65
+// One CTA per SM, persistent over items blockIdx.x, + gridDim.x, ...:
+//   warp 0       one thread TMA-loads Q, K, V of item n into load slot n % LS (boxes of 64 columns x 80 rows)
+//   warp 1       one thread issues S(n) into tensor-memory slot n % 4, then P(n-1) V(n-1) into the same
+//                columns as S(n-1) (read by then); commits signal S ready and O ready
+//   warps 2..9   two groups of 4 warps, group g the items n = g mod 2; thread = tensor-memory lane = query row.
+//                A group writes P(i), then finishes item i-1 (its O is ready by then): the row's 80 scores come
+//                in with tcgen05.ld and the softmax runs in registers, P goes over the item's Q tile (free once S
+//                is done) in the 128-byte-swizzled layout the second MMA reads; the row of O is normalised and
+//                stored, and the load slot and tensor-memory slot are handed back.
 // Every wait is bounded and every decision of a group is taken by its leader and broadcast, as in gemm.cuh.
 #pragma once
 #include "trunk.cuh"
@@ -24,33 +27,20 @@ namespace mf {
 
 struct AttTcCfg {
     static constexpr int DH = 64;
-#ifndef MF_ATT_LS
-#define MF_ATT_LS 4
-#endif
-#ifndef MF_ATT_CS
-#define MF_ATT_CS 2
-#endif
-    static constexpr int LS = MF_ATT_LS;                     // load slots (Q, K, V tile sets)
-    static constexpr int CS = MF_ATT_CS;                     // compute slots (P tile, S and O columns), one
-                                                             // softmax group of 4 warps each
+    static constexpr int LS = 6;                             // load slots (Q, K, V tile sets)
+    static constexpr int TS = 4;                             // tensor-memory slots (two per softmax group)
     static constexpr int KEYS = 80;                          // 65 keys padded to a multiple of 16
-    static constexpr uint32_t Q_BYTES = 128 * 128;           // 128 rows x 64 x 16-bit
+    static constexpr uint32_t Q_BYTES = 128 * 128;           // 128 rows x 64 x 16-bit; P[:, 0:64] afterwards
     static constexpr uint32_t KV_BYTES = KEYS * 128;
     static constexpr uint32_t Q_OFF = 0, K_OFF = Q_BYTES, V_OFF = K_OFF + KV_BYTES;
     static constexpr uint32_t LOAD_SLOT = V_OFF + KV_BYTES;  // 36 KB, a multiple of 1024
-    static constexpr uint32_t P_CHUNK = 128 * 128;           // keys 0..63; a second chunk holds keys 64..79
-    static constexpr uint32_t P_SLOT = 2 * P_CHUNK;
-    static constexpr uint32_t P_BASE = LS * LOAD_SLOT;
     static constexpr uint32_t LOAD_BYTES = 3 * KEYS * 128;
-    static constexpr size_t SMEM = 1024 + (size_t)P_BASE + CS * (size_t)P_SLOT + 256;
-    static constexpr int THREADS = 64 + 128 * CS;
+    static constexpr size_t SMEM = 1024 + LS * (size_t)LOAD_SLOT + 256;
+    static constexpr int THREADS = 64 + 256;
     static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr uint32_t T_STRIDE = CS == 2 ? 256 : 160;   // per compute slot: S (80 columns) at
-    static constexpr uint32_t O_COL = CS == 2 ? 128 : 96;       // T_STRIDE * slot, O (64) at + O_COL
-    static_assert(CS * T_STRIDE <= TMEM_COLS, "tensor memory per compute slot");
-    static_assert(LOAD_SLOT % 1024 == 0 && K_OFF % 1024 == 0 && V_OFF % 1024 == 0 && P_BASE % 1024 == 0,
-                  "swizzled tiles start on 1024-byte boundaries");
-    static_assert(SMEM <= 232448, "shared memory over the per-block limit");
+    static constexpr uint32_t T_STRIDE = 128;                // slot t: S at 128 t (80 columns), then O there (64)
+    static_assert(LOAD_SLOT % 1024 == 0 && K_OFF % 1024 == 0 && V_OFF % 1024 == 0, "1024-byte aligned tiles");
+    static_assert(TS * T_STRIDE <= TMEM_COLS && SMEM <= 232448, "resources");
 };
 
 template <typename T, typename TO>
@@ -59,24 +49,25 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ 
                     float scale, float mul, uint32_t* err)
 {
     using C = AttTcCfg;
-    constexpr int LS = C::LS, S = C::CS;
+    constexpr int LS = C::LS, TS = C::TS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(base + C::P_BASE + S * C::P_SLOT);   // [LS] Q, K, V landed
-    uint64_t* empty = full + LS;    // [LS] the load slot's tiles are read (the P V commit)
-    uint64_t* sfull = empty + LS;   // [CS] S in tensor memory
-    uint64_t* pready = sfull + S;   // [CS] P in shared memory (the group's 4 warps)
-    uint64_t* ofull = pready + S;   // [CS] O in tensor memory
-    uint64_t* tfree = ofull + S;    // [CS] the compute slot's tensor-memory columns are read (the group's 4 warps)
-    uint64_t* mma_done = tfree + S;
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + LS * C::LOAD_SLOT);   // [LS] Q, K, V landed
+    uint64_t* empty = full + LS;     // [LS] the load slot is finished with (its group's 4 warps)
+    uint64_t* sfull = empty + LS;    // [TS] S in tensor memory
+    uint64_t* pready = sfull + TS;   // [TS] P in shared memory (the group's 4 warps)
+    uint64_t* ofull = pready + TS;   // [TS] O in tensor memory
+    uint64_t* tfree = ofull + TS;    // [TS] the slot's columns are read (the group's 4 warps)
+    uint64_t* mma_done = tfree + TS;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
-    volatile uint32_t* ok = tmem_slot + 1;   // per group: its leader's broadcast
+    volatile uint32_t* ok = tmem_slot + 1;   // [2 groups x 2]: the leaders' broadcasts
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int items = B * heads;
     const int my = (int)blockIdx.x < items ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
-    // Q rows 80..127 are never loaded: zero them once (the MMA reads all 128 rows; their results are unused)
+    // Q rows 80..127 are never loaded: zero them once (the MMA reads all 128 rows; their results are unused;
+    // P overwrites them with the probabilities of those rows, finite too)
     for (int i = threadIdx.x; i < LS * 48 * 8; i += blockDim.x) {
         const int sl = i / 384, rem = i % 384;
         *reinterpret_cast<uint4*>(base + sl * C::LOAD_SLOT + C::Q_OFF + (80 + rem / 8) * 128 + (rem % 8) * 16) =
@@ -86,9 +77,9 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ 
     if (threadIdx.x == 0) {
         for (int i = 0; i < LS; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
+            mbar_init(&empty[i], 4);
         }
-        for (int i = 0; i < S; ++i) {
+        for (int i = 0; i < TS; ++i) {
             mbar_init(&sfull[i], 1);
             mbar_init(&pready[i], 4);
             mbar_init(&ofull[i], 1);
@@ -114,17 +105,17 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ 
         if (lane == 0) {
             uint32_t issued = 0, issued_par = 0;
             for (int n = 0; n < my; ++n) {
-                const int slot = n % LS, use = n / LS;
-                if (use > 0 && !mbar_wait(&empty[slot], (use - 1) & 1, err, kErrSmemEmpty)) break;
+                const int ls = n % LS, use = n / LS;
+                if (use > 0 && !mbar_wait(&empty[ls], (use - 1) & 1, err, kErrSmemEmpty)) break;
                 const int item = (int)blockIdx.x + n * (int)gridDim.x;
                 const int b = item / heads, h = item - b * heads;
-                uint8_t* sb = base + slot * C::LOAD_SLOT;
-                mbar_arrive_expect_tx(&full[slot], C::LOAD_BYTES);
-                tma_load_2d(sb + C::Q_OFF, &tmQKV, &full[slot], h * C::DH, b * kTokens);
-                tma_load_2d(sb + C::K_OFF, &tmQKV, &full[slot], d + h * C::DH, b * kTokens);
-                tma_load_2d(sb + C::V_OFF, &tmQKV, &full[slot], 2 * d + h * C::DH, b * kTokens);
-                issued |= 1u << slot;
-                issued_par = (issued_par & ~(1u << slot)) | ((uint32_t)(use & 1) << slot);
+                uint8_t* sb = base + ls * C::LOAD_SLOT;
+                mbar_arrive_expect_tx(&full[ls], C::LOAD_BYTES);
+                tma_load_2d(sb + C::Q_OFF, &tmQKV, &full[ls], h * C::DH, b * kTokens);
+                tma_load_2d(sb + C::K_OFF, &tmQKV, &full[ls], d + h * C::DH, b * kTokens);
+                tma_load_2d(sb + C::V_OFF, &tmQKV, &full[ls], 2 * d + h * C::DH, b * kTokens);
+                issued |= 1u << ls;
+                issued_par = (issued_par & ~(1u << ls)) | ((uint32_t)(use & 1) << ls);
             }
             for (int sl = 0; sl < LS; ++sl)
                 if (issued & (1u << sl)) mbar_wait(&full[sl], (issued_par >> sl) & 1, err, kErrTmaFull);
@@ -136,33 +127,28 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ 
             constexpr uint32_t idO = Operand<T>::idesc(128, C::DH) | (1u << 16);   // B (V) MN-major
             for (int n = 0; n <= my; ++n) {
                 if (n < my) {
-                    const int slot = n % S, use = n / S, ls = n % LS;
+                    const int ts = n % TS, ls = n % LS;
                     if (!mbar_wait(&full[ls], (n / LS) & 1, err, kErrTmaFull)) break;
-                    if (use > 0 && !mbar_wait(&tfree[slot], (use - 1) & 1, err, kErrTmemEmpty)) break;
+                    if (n >= TS && !mbar_wait(&tfree[ts], (n / TS - 1) & 1, err, kErrTmemEmpty)) break;
                     tc_fence_after();
                     const uint32_t sb = smem_u32(base + ls * C::LOAD_SLOT);
 #pragma unroll
                     for (int k = 0; k < C::DH / 16; ++k)
-                        umma_f16(tmem + C::T_STRIDE * slot, sdesc_sw128(sb + C::Q_OFF + 32u * k),
+                        umma_f16(tmem + C::T_STRIDE * ts, sdesc_sw128(sb + C::Q_OFF + 32u * k),
                                  sdesc_sw128(sb + C::K_OFF + 32u * k), idS, k > 0 ? 1u : 0u);
-                    umma_commit(&sfull[slot]);
+                    umma_commit(&sfull[ts]);
                 }
                 if (n >= 1) {
-                    const int m = n - 1, slot = m % S, use = m / S, ls = m % LS;
-                    if (!mbar_wait(&pready[slot], use & 1, err, kErrTmaFull)) break;
+                    const int m = n - 1, ts = m % TS, ls = m % LS;
+                    if (!mbar_wait(&pready[ts], (m / TS) & 1, err, kErrTmaFull)) break;
                     tc_fence_after();
                     const uint32_t sb = smem_u32(base + ls * C::LOAD_SLOT);
-                    const uint32_t pb = smem_u32(base + C::P_BASE + slot * C::P_SLOT);
-                    // K = 80 keys: steps 0..3 in P's first chunk (32 bytes a step), step 4 in the second; V's
-                    // step is 16 keys = two 8-row swizzle atoms = 2048 bytes
+                    // keys 0..63: P over the Q tile (32 bytes a 16-key step), V's step 16 keys = 2048 bytes
 #pragma unroll
-                    for (int k = 0; k < C::KEYS / 16; ++k) {
-                        const uint32_t pa = pb + (k < 4 ? 32u * k : C::P_CHUNK);
-                        umma_f16(tmem + C::T_STRIDE * slot + C::O_COL, sdesc_sw128(pa), sdesc_sw128(sb + C::V_OFF + 2048u * k),
-                                 idO, k > 0 ? 1u : 0u);
-                    }
-                    umma_commit(&ofull[slot]);
-                    umma_commit(&empty[ls]);
+                    for (int k = 0; k < 4; ++k)
+                        umma_f16(tmem + C::T_STRIDE * ts, sdesc_sw128(sb + C::Q_OFF + 32u * k),
+                                 sdesc_sw128(sb + C::V_OFF + 2048u * k), idO, k > 0 ? 1u : 0u);
+                    umma_commit(&ofull[ts]);
                 }
             }
             // every MMA issued has completed before tensor memory is freed
@@ -171,29 +157,109 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ 
         }
     } else {
         // ---------------------------------------------------------------- softmax and output (two groups)
-        const int grp = (warp - 2) >> 2;                 // group g takes the items of compute slot g
+        const int grp = (warp - 2) >> 2;                 // group g takes the items n = g mod 2
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;             // tensor-memory lane = query row
+        // rows 96..127 are padding: their warp only keeps the handshakes (the MMA reads their P rows, which hold
+        // finite leftovers, and their O rows are never stored)
+        const bool live = quarter < 3;
         const bool leader = threadIdx.x == 64 + 128 * grp;
         const uint32_t bar_id = 1 + grp;
         const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         const float sl2 = scale * 1.4426950408889634f;
-        for (int n = grp; n < my; n += S) {
-            const int slot = grp, use = n / S;
-            const int item = (int)blockIdx.x + n * (int)gridDim.x;
-            const int b = item / heads, h = item - b * heads;
-            if (leader) ok[grp] = mbar_wait(&sfull[slot], use & 1, err, kErrTmemFull) ? 1u : 0u;
+        float inv_prev = 0.f, p64_prev = 0.f;           // the pending item's 1 / sum and P[row, 64]
+        int prev = -1;                                   // the pending item (its O not yet read)
+
+        // item m's O row: + P[row, 64] V[64], / sum, stored; then its slots handed back
+        auto finish = [&](int m, float inv, float p64) -> bool {
+            const int ts = m % TS, ls = m % LS;
+            if (leader) ok[2 * grp + 1] = mbar_wait(&ofull[ts], (m / TS) & 1, err, kErrTmemFull) ? 1u : 0u;
             named_barrier(bar_id, 128);
-            if (!ok[grp]) break;
+            if (!ok[2 * grp + 1]) return false;
+            if (!live) {
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&tfree[ts]);
+                    mbar_arrive(&empty[ls]);
+                }
+                return true;
+            }
+            tc_fence_after();
+            uint32_t o0[32], o1[32];
+            tmem_ld_32x32b_x32(t_lane + C::T_STRIDE * ts, o0);
+            tmem_ld_32x32b_x32(t_lane + C::T_STRIDE * ts + 32u, o1);
+            tmem_ld_wait();
+            tc_fence_before();
+            // V[64] (row 64 of the V tile: swizzle row 64 % 8 = 0, so its 16-byte units are in order)
+            const uint4* v64 = reinterpret_cast<const uint4*>(base + ls * C::LOAD_SLOT + C::V_OFF + 64 * 128);
+            float o[C::DH];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const uint4 q = v64[u];
+                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int c = 8 * u + 2 * i;
+                    const uint32_t* src = c < 32 ? o0 + c : o1 + (c - 32);
+                    o[c] = fmaf(p64, to_f32<T>(reinterpret_cast<const T*>(&w[i])[0]), __uint_as_float(src[0])) * inv;
+                    o[c + 1] =
+                        fmaf(p64, to_f32<T>(reinterpret_cast<const T*>(&w[i])[1]), __uint_as_float(src[1])) * inv;
+                }
+            }
+            fence_proxy_async_smem();   // the TMA refill of the load slot comes after these reads
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&tfree[ts]);   // the slot's columns are read
+                mbar_arrive(&empty[ls]);   // and the load slot (P, V[64]) too
+            }
+            if (row < kTokens) {
+                const int item = (int)blockIdx.x + m * (int)gridDim.x;
+                const int b = item / heads, h = item - b * heads;
+                const size_t orow = (size_t)b * kTokens + row;
+                if constexpr (is_e4m3<TO>) {
+                    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(att) + orow * d + (size_t)h * C::DH);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            w[i] = pack_e4m3x4(o[16 * u + 4 * i] * mul, o[16 * u + 4 * i + 1] * mul,
+                                               o[16 * u + 4 * i + 2] * mul, o[16 * u + 4 * i + 3] * mul);
+                        dst[u] = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                } else {
+                    uint4* dst = reinterpret_cast<uint4*>(att + orow * d + (size_t)h * C::DH);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        dst[u] = make_uint4(pack2<T>(o[8 * u], o[8 * u + 1]), pack2<T>(o[8 * u + 2], o[8 * u + 3]),
+                                            pack2<T>(o[8 * u + 4], o[8 * u + 5]), pack2<T>(o[8 * u + 6], o[8 * u + 7]));
+                }
+            }
+            return true;
+        };
+
+        bool good = true;
+        for (int n = grp; n < my && good; n += 2) {
+            const int ts = n % TS, ls = n % LS;
+            if (leader) ok[2 * grp] = mbar_wait(&sfull[ts], (n / TS) & 1, err, kErrTmemFull) ? 1u : 0u;
+            named_barrier(bar_id, 128);
+            if (!ok[2 * grp]) break;
+            if (!live) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&pready[ts]);
+                if (prev >= 0) good = finish(prev, 0.f, 0.f);
+                prev = n;
+                continue;
+            }
             tc_fence_after();
             // this row's 80 scores
             float sc[C::KEYS];
             {
                 uint32_t r0[32], r1[32], r2[16];
-                const uint32_t ts = t_lane + C::T_STRIDE * slot;
-                tmem_ld_32x32b_x32(ts, r0);
-                tmem_ld_32x32b_x32(ts + 32, r1);
-                tmem_ld_32x32b_x16(ts + 64, r2);
+                const uint32_t tsa = t_lane + C::T_STRIDE * ts;
+                tmem_ld_32x32b_x32(tsa, r0);
+                tmem_ld_32x32b_x32(tsa + 32, r1);
+                tmem_ld_32x32b_x16(tsa + 64, r2);
                 tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
@@ -203,73 +269,45 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ 
 #pragma unroll
                 for (int j = 0; j < 16; ++j) sc[64 + j] = __uint_as_float(r2[j]);
             }
-            float mx = sc[0];
+            // row max over the 65 live keys (eight independent chains), then the exponentials and their sum
+            float m8[8];
 #pragma unroll
-            for (int j = 1; j < kTokens; ++j) mx = fmaxf(mx, sc[j]);
+            for (int i = 0; i < 8; ++i) m8[i] = sc[i];
+#pragma unroll
+            for (int j = 8; j < 64; ++j) m8[j & 7] = fmaxf(m8[j & 7], sc[j]);
+            m8[0] = fmaxf(m8[0], sc[64]);
+            const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             const float mc = mx * sl2;
-            float sum = 0.f;
-            uint32_t pk[C::KEYS / 2];
+            float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            uint32_t pk[32];
 #pragma unroll
-            for (int j = 0; j < C::KEYS; j += 2) {
-                const float p0 = j < kTokens ? ex2_approx(fmaf(sc[j], sl2, -mc)) : 0.f;
-                const float p1 = j + 1 < kTokens ? ex2_approx(fmaf(sc[j + 1], sl2, -mc)) : 0.f;
-                sum += p0 + p1;
+            for (int j = 0; j < 64; j += 2) {
+                const float p0 = ex2_approx(fmaf(sc[j], sl2, -mc));
+                const float p1 = ex2_approx(fmaf(sc[j + 1], sl2, -mc));
+                // P goes to the MMA rounded to the 16-bit type; the sum is of the f32 probabilities
                 pk[j / 2] = pack2<T>(p0, p1);
+                s8[(j / 2) & 7] += p0 + p1;
             }
-            // P row into the slot's P tile: keys 0..63 in chunk 0 (8 units of 16 bytes), 64..79 in chunk 1
-            uint8_t* pb = base + C::P_BASE + slot * C::P_SLOT;
+            const float p64 = ex2_approx(fmaf(sc[64], sl2, -mc));
+            const float sum = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])) + p64;
+            // P[:, 0:64] over the Q tile (free: S is done)
+            uint8_t* pb = base + ls * C::LOAD_SLOT + C::Q_OFF;
 #pragma unroll
             for (int u = 0; u < 8; ++u)
                 *reinterpret_cast<uint4*>(pb + swz<128>(row, u)) =
                     make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-#pragma unroll
-            for (int u = 0; u < 2; ++u)
-                *reinterpret_cast<uint4*>(pb + C::P_CHUNK + swz<128>(row, u)) =
-                    make_uint4(pk[32 + 4 * u], pk[33 + 4 * u], pk[34 + 4 * u], pk[35 + 4 * u]);
             fence_proxy_async_smem();   // the MMA (async proxy) reads what these generic stores wrote
+            tc_fence_before();          // and overwrites the S columns this thread has read
             __syncwarp();
-            if (lane == 0) mbar_arrive(&pready[slot]);
-
-            if (leader) ok[grp] = mbar_wait(&ofull[slot], use & 1, err, kErrTmemFull) ? 1u : 0u;
-            named_barrier(bar_id, 128);
-            if (!ok[grp]) break;
-            tc_fence_after();
-            uint32_t o0[32], o1[32];
-            tmem_ld_32x32b_x32(t_lane + C::T_STRIDE * slot + C::O_COL, o0);
-            tmem_ld_32x32b_x32(t_lane + C::T_STRIDE * slot + C::O_COL + 32u, o1);
-            tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tfree[slot]);   // S and O of this slot are read
-            if (row < kTokens) {
-                const float inv = 1.f / sum;
-                const size_t orow = (size_t)b * kTokens + row;
-                if constexpr (is_e4m3<TO>) {
-                    const float m = inv * mul;
-                    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(att) + orow * d + (size_t)h * C::DH);
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const uint32_t* src = u < 2 ? o0 + 16 * u : o1 + 16 * (u - 2);
-                        uint32_t w[4];
-#pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            w[i] = pack_e4m3x4(__uint_as_float(src[4 * i]) * m, __uint_as_float(src[4 * i + 1]) * m,
-                                               __uint_as_float(src[4 * i + 2]) * m, __uint_as_float(src[4 * i + 3]) * m);
-                        dst[u] = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                } else {
-                    uint4* dst = reinterpret_cast<uint4*>(att + orow * d + (size_t)h * C::DH);
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        const uint32_t* src = u < 4 ? o0 + 8 * u : o1 + 8 * (u - 4);
-                        dst[u] = make_uint4(pack2<T>(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv),
-                                            pack2<T>(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv),
-                                            pack2<T>(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv),
-                                            pack2<T>(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv));
-                    }
-                }
-            }
+            if (lane == 0) mbar_arrive(&pready[ts]);
+            // the previous item's O is ready by now
+            if (prev >= 0) good = finish(prev, inv_prev, p64_prev);
+            prev = n;
+            inv_prev = 1.f / sum;
+            p64_prev = p64;
         }
+        if (good && prev >= 0) finish(prev, inv_prev, p64_prev);
     }
 
     __syncwarp();

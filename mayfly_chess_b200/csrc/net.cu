@@ -417,14 +417,20 @@ static void launch_attention_dh(const CUtensorMap& map, TO* att, int B, int d, i
              mul, err);
 }
 
-// MAYFLY_CUDANET_ATT_TC=0 runs head width 64 on the mma.sync kernel instead of the tensor-memory one.
-static bool att_tc()
+// Which attention kernel runs head width 64: measured on a B200, the tensor-memory kernel (attention_tc.cuh) is
+// faster where attention writes e4m3 (the FP8 pass: 8.5-8.9 vs 9.2-9.8 ms per 4,096-position pass) and the
+// mma.sync kernel where it writes 16-bit values (2.54 vs 2.79 ms per 1,024-position pass): the tensor-memory
+// kernel spends its time in the per-item handshakes between its softmax warps and the MMA thread, the mma.sync
+// kernel in keeping more items in flight. MAYFLY_CUDANET_ATT_TC=1 / 0 forces one of them.
+static int att_tc_mode()
 {
-    static bool on = [] {
+    static int mode = [] {
         const char* e = std::getenv("MAYFLY_CUDANET_ATT_TC");
-        return !(e && std::strcmp(e, "0") == 0);
+        if (e && std::strcmp(e, "1") == 0) return 1;
+        if (e && std::strcmp(e, "0") == 0) return 0;
+        return -1;
     }();
-    return on;
+    return mode;
 }
 
 // the tcgen05 attention (attention_tc.cuh): one CTA per SM, persistent over the (board, head) items
@@ -456,7 +462,9 @@ static void launch_attention(const CUtensorMap& map, TO* att, int B, int d, int 
 {
     if (B < 1 || heads < 1 || d % heads) throw std::runtime_error("cudanet_b200: bad attention sizes");
     const int dh = d / heads;
-    if (dh == 64 && att_tc()) launch_attention_tc<T, TO>(map, att, B, d, heads, mul, err, s);
+    const int mode = att_tc_mode();
+    const bool tc = mode == 1 || (mode == -1 && is_e4m3<TO>);
+    if (dh == 64 && tc) launch_attention_tc<T, TO>(map, att, B, d, heads, mul, err, s);
     else if (dh == 64) launch_attention_dh<T, TO, 64>(map, att, B, d, heads, mul, err, s);
     else if (dh == 32) launch_attention_dh<T, TO, 32>(map, att, B, d, heads, mul, err, s);
     else throw std::runtime_error("cudanet_b200: head width must be 32 or 64");
@@ -1493,7 +1501,7 @@ static uint32_t* noalloc_scratch(int dev)
 // One attention launch of the unit-test entry points: its own error word, a map over exactly B * 65 rows.
 template <typename T, typename TO>
 static void attention_once(const void* qkv, void* att, int B, int d, int heads, float mul, cudaStream_t s,
-                           const char* who)
+                           const char* who, bool force_tc = false)
 {
     if (B < 1 || heads < 1 || d % heads) throw std::runtime_error(std::string(who) + ": bad sizes");
     if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(att)) & 15)
@@ -1503,7 +1511,12 @@ static void attention_once(const void* qkv, void* att, int B, int d, int heads, 
     RT(cudaMalloc(&errw, 4));
     RT(cudaMemset(errw, 0, 4));
     try {
-        launch_attention<T, TO>(map, static_cast<TO*>(att), B, d, heads, mul, errw, s);
+        if (force_tc) {
+            if (d / heads != 64) throw std::runtime_error(std::string(who) + ": head width must be 64");
+            launch_attention_tc<T, TO>(map, static_cast<TO*>(att), B, d, heads, mul, errw, s);
+        } else {
+            launch_attention<T, TO>(map, static_cast<TO*>(att), B, d, heads, mul, errw, s);
+        }
         RT(cudaStreamSynchronize(s));
     } catch (...) {
         cudaFree(errw);
@@ -1819,6 +1832,22 @@ CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B
             mf::attention_once<__half, __half>(qkv, att, B, d, heads, 1.f, s, "cudanet_k_attention");
         else
             throw std::runtime_error("cudanet_k_attention: dtype must be 0 (f16) or 1 (bf16)");
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_k_attention_tc(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,
+                                       char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_k_attention_tc: unknown exception", [&] {
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (dtype == 1)
+            mf::attention_once<__nv_bfloat16, __nv_bfloat16>(qkv, att, B, d, heads, 1.f, s, "cudanet_k_attention_tc",
+                                                             true);
+        else if (dtype == 0)
+            mf::attention_once<__half, __half>(qkv, att, B, d, heads, 1.f, s, "cudanet_k_attention_tc", true);
+        else
+            throw std::runtime_error("cudanet_k_attention_tc: dtype must be 0 (f16) or 1 (bf16)");
         return 0;
     });
 }

@@ -82,6 +82,8 @@ def load(dll=None):
         lib.cudanet_k_gemm_resln.restype = i32
         lib.cudanet_k_attention.argtypes = [i32, vp, vp, i32, i32, i32, vp, cp, i32]
         lib.cudanet_k_attention.restype = i32
+        lib.cudanet_k_attention_tc.argtypes = [i32, vp, vp, i32, i32, i32, vp, cp, i32]
+        lib.cudanet_k_attention_tc.restype = i32
         lib.cudanet_k_attention_cls.argtypes = [i32, vp, vp, i32, i32, i32, vp, cp, i32]
         lib.cudanet_k_attention_cls.restype = i32
         lib.cudanet_k_layernorm.argtypes = [i32, vp, vp, vp, vp, i32, i32, i32, vp, cp, i32]
@@ -372,6 +374,17 @@ def k_attention(qkv, att, B, d, heads, dll=None):
                                  ERR_LEN)
     if rc != 0:
         raise RuntimeError(f"cudanet_k_attention: {_msg(err)}")
+    return att
+
+
+def k_attention_tc(qkv, att, B, d, heads, dll=None):
+    """k_attention on the tensor-memory (tcgen05) kernel, head width 64."""
+    lib = load(dll)
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_k_attention_tc(_dtype_code(qkv), qkv.data_ptr(), att.data_ptr(), B, d, heads, _stream(), err,
+                                    ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_k_attention_tc: {_msg(err)}")
     return att
 
 
