@@ -29,9 +29,11 @@
 //               column chunks), bias / GELU / residual, then the row goes into a 128-row staging chunk in shared
 //               memory (128-byte rows with the 128-byte swizzle, or 64-byte rows with the 64-byte swizzle for the
 //               4-group GELU epilogues) and one thread stores the chunk with a TMA tensor store (coalesced,
-//               asynchronous). For the residual the chunk of X is first TMA-loaded into the
-//               same staging buffer, several chunks ahead (also across tiles), so the read-modify-write of the
-//               f32 residual stream is pure bulk traffic.
+//               asynchronous). The f32 residual stages acc + bias alone and adds it into X with a TMA
+//               reduction (cp.reduce.async.bulk.tensor .add, done at L2): X is never read into the SM, and the
+//               shared-memory traffic per tile halves against a read-modify-write through the staging chunk.
+//               The bf16 residual (X + v rounded once) TMA-loads the chunk of X into the staging buffer, several
+//               chunks ahead (also across tiles), and adds in registers.
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1. Tiles run M-block-major (all
 // N blocks of an M block back to back), so an A block is read from HBM once and the weights stay in L2.
 // Out-of-range rows and columns (M and N tails) are zero-filled by TMA loads and clipped by TMA stores.
@@ -47,6 +49,18 @@
 #include <cuda_fp8.h>
 
 #include "ptx.cuh"
+
+// Staging buffers per CTA for the bf16 residual epilogue (each 16 KB; what they take from the operand ring).
+#ifndef MF_RESID_BUFFERS
+#define MF_RESID_BUFFERS 4
+#endif
+// Epilogue groups and staging buffers per group of the f32 residual (added into X by TMA reductions).
+#ifndef MF_REDUCE_EG
+#define MF_REDUCE_EG 2
+#endif
+#ifndef MF_REDUCE_NBUF
+#define MF_REDUCE_NBUF 1
+#endif
 
 namespace mf {
 
@@ -99,6 +113,10 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
     static constexpr int KSTEPS = 4;                    // MMA instructions per stage (K = 16 or 32 each, 32 bytes)
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;   // rows of W per CTA per stage
     static constexpr bool RESID = EPI == kEpiResidual || EPI == kEpiResidual16;
+    // the bf16 residual reads X back into the staging chunk (X + v is rounded once); the f32 residual is added
+    // into X by a TMA reduction at L2 (the same f32 add), so it neither reads X nor stages it
+    static constexpr bool XLOAD = EPI == kEpiResidual16;
+    static constexpr bool REDUCE = EPI == kEpiResidual;
     static constexpr bool IS_F8 = F8;
     static constexpr bool HEAVY = EPI == kEpiBiasGelu || EPI == kEpiGeluE4m3;   // GELU's erf per element
     static constexpr int OUT_BYTES = (EPI == kEpiResidual || EPI == kEpiF32) ? 4 : (EPI == kEpiGeluE4m3 ? 1 : 2);
@@ -114,9 +132,11 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
     // staging buffers per CTA in flight)
     // (the bf16 residual, 4 chunks a tile, measured faster with two groups of two buffers; the f32 residual,
     // 8 chunks a tile, with one group of four)
-    static constexpr int EG = RESID ? ((EPI == kEpiResidual16 && NC % 2 == 0) ? 2 : 1)
-                                    : (HEAVY && NC % 4 == 0) ? 4 : (NC % 2 == 0 ? 2 : 1);
-    static constexpr int NBUF = RESID ? 4 / EG : (EG >= 2 ? 1 : 2);   // staging buffers per group
+    static constexpr int EG = XLOAD ? (NC % 2 == 0 ? 2 : 1)
+                              : REDUCE ? ((NC % MF_REDUCE_EG == 0) ? MF_REDUCE_EG : 1)
+                                       : (HEAVY && NC % 4 == 0) ? 4 : (NC % 2 == 0 ? 2 : 1);
+    static constexpr int NBUF = XLOAD ? MF_RESID_BUFFERS / EG
+                                      : REDUCE ? MF_REDUCE_NBUF : (EG >= 2 ? 1 : 2);   // staging buffers per group
     static constexpr uint32_t A_BYTES = BM * 128;
     static constexpr uint32_t B_BYTES = B_ROWS * 128;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -350,7 +370,7 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
         y = origin_row(h / CPG);
     };
     int loads = 0;    // residual chunks whose load the leader issued
-    if constexpr (C::RESID) {
+    if constexpr (C::XLOAD) {
         if (leader)
             for (; loads < C::NBUF && loads < total_chunks; ++loads) {
                 int x, y;
@@ -435,8 +455,8 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                     for (int i = 0; i < 16; ++i) q[16 * p + i] = pack2<T>(v[2 * i], v[2 * i + 1]);
                 }
             }
-            // the staging buffer must be ready: loaded (residual) or no longer read by its last store
-            if constexpr (C::RESID) {
+            // the staging buffer must be ready: loaded (bf16 residual) or no longer read by its last store
+            if constexpr (C::XLOAD) {
                 if (leader) L.epi_ok[grp] = mbar_wait(&xfull[b], (g / C::NBUF) & 1u, err, kErrTmaFull) ? 1u : 0u;
             } else {
                 if (leader) bulk_wait_read<C::NBUF - 1>();
@@ -447,21 +467,7 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                 break;
             }
             constexpr int RB = C::ROW_BYTES;
-            if constexpr (EPI == kEpiResidual) {
-                // all 8 loads first, then the adds, then the stores (no load waits behind a store)
-                float4 xs[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) xs[j] = *reinterpret_cast<const float4*>(buf + swz<RB>(row, j));
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    xs[j].x += v[4 * j + 0];
-                    xs[j].y += v[4 * j + 1];
-                    xs[j].z += v[4 * j + 2];
-                    xs[j].w += v[4 * j + 3];
-                }
-#pragma unroll
-                for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(buf + swz<RB>(row, j)) = xs[j];
-            } else if constexpr (EPI == kEpiResidual16) {
+            if constexpr (EPI == kEpiResidual16) {
                 // X (bf16) + v in f32, rounded once to bf16
                 uint4 xs[8];
 #pragma unroll
@@ -490,9 +496,10 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
             fence_proxy_async_smem();
             named_barrier(bar_id, 128);
             if (leader) {
-                tma_store_2d(tmC, buf, col0, row0);
+                if constexpr (C::REDUCE) tma_reduce_add_2d(tmC, buf, col0, row0);   // X += acc + bias
+                else tma_store_2d(tmC, buf, col0, row0);
                 bulk_commit();
-                if constexpr (C::RESID) {
+                if constexpr (C::XLOAD) {
                     // refill the previous chunk's buffer (its store has been read) NBUF chunks ahead
                     const int next = g - 1 + C::NBUF;
                     if (g >= 1 && next < total_chunks && next >= loads) {
@@ -513,7 +520,7 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
     if (leader) {
         bulk_wait_all();
         // residual loads issued but never consumed (only after a failure) land before the CTA leaves
-        if constexpr (C::RESID)
+        if constexpr (C::XLOAD)
             for (int h = g; h < loads; ++h) mbar_wait(&xfull[h % C::NBUF], (h / C::NBUF) & 1u, err, kErrTmaFull);
     }
 }

@@ -303,10 +303,10 @@ static void launch_gemm_pair_if(const CUtensorMap& ma, const CUtensorMap& mb, co
 }
 
 // Tile choice: kPairTile (a CTA pair per 256 x 256 tile) when there are at least as many pair tiles as pairs
-// fit and the epilogue is light next to the MMAs (bias-only or f32 outputs, or K >= 2048: measured on a B200,
-// the pair kernel is faster for qkv and ff2 and slower for out and ff1, whose epilogues gate both CTAs of a
-// pair), else the widest single-CTA tile that still gives every SM a tile (weights stream through fewer SMs
-// otherwise).
+// fit and the epilogue is light next to the MMAs (bias-only, f32 outputs, the f32 residual's TMA reduction, or
+// K >= 2048: measured on a B200, the pair kernel is faster for qkv, out and ff2 and slower for ff1, whose GELU
+// epilogue gates both CTAs of a pair, and for the bf16 residual's read-modify-write), else the widest single-CTA
+// tile that still gives every SM a tile (weights stream through fewer SMs otherwise).
 constexpr int kPairTile = 2;
 
 // MAYFLY_CUDANET_TILE: "pair" or "single" forces the CTA-pair or the single-CTA kernels, anything else (the
@@ -325,7 +325,7 @@ static int tile_mode()
 static int pick_bn(int M, int N, int K, int epi, int num_sms)
 {
     const int mode = tile_mode();
-    const bool light = epi == kEpiBias || epi == kEpiF32 || K >= 2048;
+    const bool light = epi == kEpiBias || epi == kEpiF32 || epi == kEpiResidual || K >= 2048;
     if (mode == 1 || (mode == 0 && light && ((M + 255) / 256) * ((N + 255) / 256) >= num_sms / 2)) return kPairTile;
     const int m_tiles = (M + 127) / 128;
     for (int bn : {256, 128})

@@ -118,6 +118,16 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                  : "memory");
 }
 
+// Add a 2D shared-memory tile into global memory element by element (dst = dst + src, f32 add rounded to
+// nearest, done at L2): a bulk reduction, tracked by the same bulk groups as tma_store_2d. Each element of the
+// tile is added once, so the result is the same as a read, an f32 add and a write.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y)
+{
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
 // Bring a 2D tile of a tensor into L2 ahead of its use (no shared memory, no completion to wait for).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y)
 {
