@@ -14,8 +14,8 @@ independent evaluator per GPU, no collective on the data path (weak scaling: 1,0
              The working set (285 MB of weights, ~1.2 GB of activations) is far larger than L2.
   e2e        the same metric through the reference-facing API, CudaNet.evaluate on host numpy arrays: each step
              copies the inputs into pinned staging and up, and the outputs down and out (wall clock).
-  roofline   the dominant kernel, the qkv product (the CTA-pair tcgen05 GEMM, 26% of device time in the ncu
-             launch list, profiles/launches_bf16_b1024.md): its algorithmic FLOPs per launch / its mean launch
+  roofline   the dominant product, qkv (the CTA-pair tcgen05 GEMM, one launch per layer, 28.7% of device time in
+             the ncu launch list, profiles/launches_bf16_b1024.md): its algorithmic FLOPs per launch / its mean launch
              time, from CUDA events around each step of an eager pass on the evaluator's stream
              (cudanet_profile), against the measured sustained bf16 peak. `traffic` is its DRAM bytes per launch
              from the ncu capture (profiles/gemm_qkv_pair_*), scaled by B / 1,024. The whole trunk-GEMM family is
@@ -52,8 +52,8 @@ sys.path.insert(0, REPO)
 
 METRIC = "NN positions evaluated/sec (146M trunk, bs1024, 1/2/4/8 B200); p50 latency at bs64"
 # DRAM bytes (read + write) of one qkv launch per position, from the ncu captures in profiles/
-# (gemm_qkv_pair_bf16_b1024.md: 142.9 + 355.6 MB at B = 1,024; gemm_qkv_pair_e4m3_b1024.md)
-QKV_TRAFFIC_PER_POS = {"bf16": (142905088 + 355564544) / 1024}
+# (gemm_qkv_pair_bf16_b1024.md: 142.9 + 355.6 MB at B = 1,024; gemm_qkv_pair_e4m3_b1024.md: 71.5 + 351.2 MB)
+QKV_TRAFFIC_PER_POS = {"bf16": (142905088 + 355564544) / 1024, "e4m3": (71469312 + 351151104) / 1024}
 CALIB_ROWS = (7936, 8192)   # positions_seed1.npz rows the e4m3 input scales are calibrated on
 POSITIONS = os.path.join(REPO, "tests", "golden", "positions_seed1.npz")
 PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")

@@ -128,7 +128,7 @@ static CUtensorMap output_map(void* base, int epi, MapType t16, int M, int N, in
     if (epi == kEpiGeluE4m3) return make_map(base, MapType::U8, N, M, ldc, 64, 128, true);
     if (epi == kEpiBiasGelu) return make_map(base, t16, N, M, ldc, 32, 128, true);
     if (epi == kEpiResidual16) return make_map(base, MapType::BF16, N, M, ldc, 64, 128);
-    return make_map(base, t16, N, M, ldc, 64, 128);
+    return make_map(base, t16, N, M, ldc, MF_BIAS_ROWB / 2, 128, MF_BIAS_ROWB == 64);
 }
 
 // ------------------------------------------------------------------------------------------------ launchers
