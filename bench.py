@@ -60,6 +60,26 @@ PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
+def keys_of_inputs(b):
+    """White-to-move transposition keys whose encoding is exactly this batch's inputs (the position files keep
+    the encoded inputs, not the keys): piece boards from ids, castling-rights bits on the rook corners for each
+    right cast sets (the king sits on its back rank whenever one is set), the en passant square from ep, the
+    clock from hm. Checked against the GPU encoder before use."""
+    ids = b["ids"]
+    B = ids.shape[0]
+    sq = np.uint64(1) << np.arange(64, dtype=np.uint64)
+    keys = np.zeros((B, 10), np.uint64)
+    for t in range(6):
+        keys[:, t] = ((ids == t + 1) | (ids == t + 7)) @ sq
+    keys[:, 6] = ((ids >= 1) & (ids <= 6)) @ sq
+    keys[:, 7] = (ids >= 7) @ sq
+    keys[:, 8] = 1
+    corner = np.array([1 << 7, 1 << 0, 1 << 63, 1 << 56], np.uint64)
+    keys[:, 9] = (b["cast"] > 0) @ corner
+    ep_sq = np.where(b["ep"] > 0, b["ep"] - 1, -1).astype(np.int64)
+    return keys, ep_sq, b["hm"].astype(np.int64)
+
+
 def flops_per_position(d=1024, layers=16, heads=16, ff=2048, tokens=65, moves=4162):
     """FLOPs of one position (multiply-add = 2): (algorithmic, executed, executed by the trunk products).
     Algorithmic: the four trunk products, attention and the heads of every token. Executed: the evaluator runs
@@ -213,6 +233,7 @@ def main():
     import torch
     import torch.distributed as dist
     from mayfly_chess_b200 import weights as W
+    from mayfly_chess_b200 import cudanet_py
     from mayfly_chess_b200.cudanet_py import CudaNet
     from mayfly_chess_b200.inputs import PositionSet
     from mayfly_chess_b200 import replicas
@@ -298,6 +319,50 @@ def main():
     h2d = B * (64 * 8 + 8 + 8 + 16) + B * wide * 9
     d2h = 256 + 4 * B * (2 * wide + 1)
 
+    # ---------------------------------------------------------------- the key-fed path (encode on the GPU)
+    keys, ep_sq, clock = keys_of_inputs(b)
+    kd = [torch.from_numpy(a.view(np.int64)).cuda() for a in (keys, ep_sq, clock)]
+    enc = cudanet_py.encode_keys_device(*kd)
+    for k, t in zip(("ids", "cast", "hm", "ep"), enc):
+        if not np.array_equal(t.cpu().numpy(), b[k]):
+            raise SystemExit(f"the GPU encoder disagrees with the batch's {k}")
+    # device time per launch: 50 launches queued behind a sleep kernel, so host pacing does not count
+    lib = cudanet_py.load()
+    errb = cudanet_py.ctypes.create_string_buffer(256)
+    cs = cudanet_py.ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    outp = [t.data_ptr() for t in enc]
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    torch.cuda._sleep(20_000_000)
+    ev[0].record()
+    for _ in range(50):
+        if lib.cudanet_encode_keys(kd[0].data_ptr(), kd[1].data_ptr(), kd[2].data_ptr(), B, *outp, cs, errb, 256):
+            raise SystemExit(f"cudanet_encode_keys: {errb.value.decode()}")
+    ev[1].record()
+    torch.cuda.synchronize()
+    enc_us = ev[0].elapsed_time(ev[1]) * 1000 / 50
+    cpu_enc_us = None
+    if rank == 0 and not args.no_cpu:
+        from oracle import encode_oracle     # the numpy restatement of encode.py encode_keys, timed on the host
+        t0 = time.perf_counter()
+        for _ in range(20):
+            encode_oracle.encode_keys(keys, ep_sq, clock)
+        cpu_enc_us = (time.perf_counter() - t0) / 20 * 1e6
+    for _ in range(2):
+        net.evaluate_keys(keys, ep_sq, clock, b["I"], b["M"])
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        net.evaluate_keys(keys, ep_sq, clock, b["I"], b["M"])
+    e2e_keys_s = max_over_ranks(time.perf_counter() - t0)
+    encoder = {"kernel": "encode_keys_kernel (one launch per batch, 64 threads a board)",
+               "kernel_us": enc_us, "bytes_per_launch": 644 * B,
+               "achieved_gbs": 644 * B / (enc_us * 1e-6) / 1e9,
+               "cpu_numpy_us": cpu_enc_us, "cpu_numpy": "encode.py encode_keys restated on arrays (oracle/), "
+                                                        "one host thread, same batch",
+               "e2e_keys": {"value": world * B * args.steps / e2e_keys_s, "unit": "positions/s",
+                            "h2d_bytes_per_step": B * 96 + B * wide * 9, "d2h_bytes_per_step": d2h}}
+
     # ---------------------------------------------------------------- roofline of the dominant kernel
     prof = net.profile(B, reps=3)
     fl_alg, fl_pos, gemm_fl_pos = flops_per_position()
@@ -375,6 +440,7 @@ def main():
         "p50_latency_ms_bs64": sweep.get("64", {}).get("p50_ms"),
         "clocks": clk,
         "latency_sweep": sweep,
+        "encoder": encoder,
         "cpu_baseline": cpu,
     }
     print(json.dumps(out), flush=True)

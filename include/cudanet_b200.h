@@ -80,6 +80,28 @@ CUDANET_API int cudanet_begin(void* handle, int B, int wide, const int64_t* ids,
                               char* err, int err_len);
 CUDANET_API int cudanet_end(void* handle, float* pol, float* val, float* qv, char* err, int err_len);
 
+/* Positions as transposition keys instead of encoded inputs (no counterpart in the C ABI; the reference's
+ * encoder is mayfly/chess/encode.py:73-100 encode_keys, which MCTS._prepare runs on the host before
+ * CudaNet.evaluate). Per board: keys[10 b .. 10 b + 9] = pawns, knights, bishops, rooks, queens, kings, white,
+ * black (64-bit boards, a1 = bit 0), turn (nonzero: white to move), clean castling rights, i.e.
+ * Board._transposition_key()[0:10]; ep_sq[b] the key's legal en passant square, negative for None; clock[b] the
+ * halfmove clock. 96 bytes a board cross PCIe instead of 548; the GPU encodes them (encode_keys_kernel) into the
+ * inputs cudanet_evaluate takes, with encode_keys' exact values, then runs the same pass. I, M and the outputs
+ * are cudanet_evaluate's. Returns 0, or -1 with the reason in err. */
+CUDANET_API int cudanet_evaluate_keys(void* handle, int B, int wide, const uint64_t* keys, const int64_t* ep_sq,
+                                      const int64_t* clock, const int64_t* I, const uint8_t* M, float* pol,
+                                      float* val, float* qv, char* err, int err_len);
+/* cudanet_begin from transposition keys (finish with cudanet_end). */
+CUDANET_API int cudanet_begin_keys(void* handle, int B, int wide, const uint64_t* keys, const int64_t* ep_sq,
+                                   const int64_t* clock, const int64_t* I, const uint8_t* M, char* err,
+                                   int err_len);
+/* The encoder alone, on device memory and a caller stream (NULL: the default stream): keys, ep_sq and clock as
+ * above (B boards) to ids [B * 64] int64, cast [B * 4] f32, hm [B] int64, ep [B] int64, exactly what
+ * encode.py:73-100 encode_keys returns. Asynchronous on `stream`; returns 0, or -1 with the reason in err. */
+CUDANET_API int cudanet_encode_keys(const uint64_t* keys, const int64_t* ep_sq, const int64_t* clock, int B,
+                                    int64_t* ids, float* cast, int64_t* hm, int64_t* ep, void* stream, char* err,
+                                    int err_len);
+
 /* The arithmetic the handle runs its products in: "f16", "bf16" or "e4m3" (the layer products on e4m3
  * operands, the heads in bf16). Returns the length, -1 on a null handle. */
 CUDANET_API int cudanet_precision(void* handle, char* buf, int buf_len);

@@ -16,7 +16,7 @@ REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libcudanet_b200.so")
 SOURCES = ["net.cu"]
-HEADERS = ["ptx.cuh", "gemm.cuh", "gemm_ln.cuh", "trunk.cuh", "attention_tc.cuh", "json_min.h"]
+HEADERS = ["ptx.cuh", "gemm.cuh", "gemm_ln.cuh", "trunk.cuh", "attention_tc.cuh", "encode.cuh", "json_min.h"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-shared", "-cudart", "static"]
 

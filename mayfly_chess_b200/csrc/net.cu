@@ -29,6 +29,7 @@
 
 #include "../../include/cudanet_b200.h"
 #include "attention_tc.cuh"
+#include "encode.cuh"
 #include "gemm_ln.cuh"
 #include "json_min.h"
 #include "trunk.cuh"
@@ -751,6 +752,9 @@ public:
 
     void begin(int B, int wide, const int64_t* ids, const float* cast, const int64_t* hm, const int64_t* ep,
                const int64_t* I, const uint8_t* M, bool queued, bool want_logits);
+    // begin from transposition keys: the keys cross PCIe and encode_keys_kernel fills the input slots
+    void begin_keys(int B, int wide, const uint64_t* keys, const int64_t* ep_sq, const int64_t* clock,
+                    const int64_t* I, const uint8_t* M, bool queued, bool want_logits);
     void end(float* pol, float* val, float* qv, float* logits);
     void evaluate_device(int B, int wide, const int64_t* ids, const float* cast, const int64_t* hm,
                          const int64_t* ep, const int64_t* I, const uint8_t* M, float* pol, float* val, float* qv,
@@ -786,6 +790,9 @@ private:
         int B, wide, slot;
         bool queued, logits;
     };
+    size_t key_off_ = 0;   // the key block (96 bytes a board) in the staging buffers, after the encoded inputs
+    int begin_checks(int B, int wide, bool queued);
+    void begin_run(int B, int wide, int slot, bool queued, bool want_logits);
     Fly fly_[2];
     int fly_n_ = 0;
 
@@ -903,7 +910,8 @@ void Net::init(const std::string& path, int device)
         RT(cudaMemset(att_, 0, rows_pad_ * d * 2));
         RT(cudaMemset(ff_, 0, rows_pad_ * ff * 2));
         RT(cudaMemset(cls_, 0, cls_pad_ * d * 2));
-        const size_t in_bytes = in_layout(max_batch_, kMaxWide).total;
+        key_off_ = (in_layout(max_batch_, kMaxWide).total + 255) & ~size_t(255);
+        const size_t in_bytes = key_off_ + 96 * static_cast<size_t>(max_batch_);
         const size_t out_bytes = kOutHeader + 4 * static_cast<size_t>(max_batch_) * (2 * kMaxWide + 1);
         RT(cudaMalloc(&d_in_, in_bytes));
         RT(cudaMalloc(&d_out_, out_bytes));
@@ -1250,17 +1258,23 @@ void Net::forward(int B, cudaStream_t s)
     }
 }
 
-void Net::begin(int B, int wide, const int64_t* ids, const float* cast, const int64_t* hm, const int64_t* ep,
-                const int64_t* I, const uint8_t* M, bool queued, bool want_logits)
+// The checks every begin makes; returns the staging slot the batch takes.
+int Net::begin_checks(int B, int wide, bool queued)
 {
     check_batch(B);
     if (wide < 1 || wide > kMaxWide)
         throw std::runtime_error("cudanet_b200: wide " + std::to_string(wide) + " outside 1.." +
                                  std::to_string(kMaxWide));
-    if (!ids || !cast || !hm || !ep || !I || !M) throw std::runtime_error("cudanet_b200: a null input pointer");
     if (fly_n_ == 2) throw std::runtime_error("cudanet_b200: begin with two batches already in flight");
     if (fly_n_ && !queued) throw std::runtime_error("cudanet_b200: evaluate while a batch is in flight");
-    const int slot = fly_n_ ? 1 - fly_[0].slot : 0;
+    return fly_n_ ? 1 - fly_[0].slot : 0;
+}
+
+void Net::begin(int B, int wide, const int64_t* ids, const float* cast, const int64_t* hm, const int64_t* ep,
+                const int64_t* I, const uint8_t* M, bool queued, bool want_logits)
+{
+    if (!ids || !cast || !hm || !ep || !I || !M) throw std::runtime_error("cudanet_b200: a null input pointer");
+    const int slot = begin_checks(B, wide, queued);
     RT(cudaSetDevice(device_));
     const size_t b = static_cast<size_t>(B), wd = static_cast<size_t>(wide);
     const InLayout lay = in_layout(B, wide);
@@ -1272,6 +1286,39 @@ void Net::begin(int B, int wide, const int64_t* ids, const float* cast, const in
     std::memcpy(hin + lay.I, I, 8 * b * wd);
     std::memcpy(hin + lay.M, M, b * wd);
     RT(cudaMemcpyAsync(d_in_, hin, lay.total, cudaMemcpyHostToDevice, stream_));
+    begin_run(B, wide, slot, queued, want_logits);
+}
+
+void Net::begin_keys(int B, int wide, const uint64_t* keys, const int64_t* ep_sq, const int64_t* clock,
+                     const int64_t* I, const uint8_t* M, bool queued, bool want_logits)
+{
+    if (!keys || !ep_sq || !clock || !I || !M) throw std::runtime_error("cudanet_b200: a null input pointer");
+    const int slot = begin_checks(B, wide, queued);
+    RT(cudaSetDevice(device_));
+    const size_t b = static_cast<size_t>(B), wd = static_cast<size_t>(wide);
+    const InLayout lay = in_layout(B, wide);
+    uint8_t* hin = h_in_[slot];
+    std::memcpy(hin + key_off_, keys, 80 * b);
+    std::memcpy(hin + key_off_ + 80 * b, ep_sq, 8 * b);
+    std::memcpy(hin + key_off_ + 88 * b, clock, 8 * b);
+    std::memcpy(hin + lay.I, I, 8 * b * wd);
+    std::memcpy(hin + lay.M, M, b * wd);
+    RT(cudaMemcpyAsync(d_in_ + key_off_, hin + key_off_, 96 * b, cudaMemcpyHostToDevice, stream_));
+    RT(cudaMemcpyAsync(d_in_ + lay.I, hin + lay.I, lay.total - lay.I, cudaMemcpyHostToDevice, stream_));
+    const uint8_t* kd = d_in_ + key_off_;
+    launch_k(encode_keys_kernel, dim3((B + kEncodeBoardsPerBlock - 1) / kEncodeBoardsPerBlock),
+             dim3(64 * kEncodeBoardsPerBlock), 0, stream_, reinterpret_cast<const uint64_t*>(kd),
+             reinterpret_cast<const int64_t*>(kd + 80 * b), reinterpret_cast<const int64_t*>(kd + 88 * b), B,
+             reinterpret_cast<int64_t*>(d_in_ + lay.ids), reinterpret_cast<float*>(d_in_ + lay.cast),
+             reinterpret_cast<int64_t*>(d_in_ + lay.hm), reinterpret_cast<int64_t*>(d_in_ + lay.ep));
+    begin_run(B, wide, slot, queued, want_logits);
+}
+
+// The pass, the search's reduction and the copies back, once the inputs are in d_in_ (stream order).
+void Net::begin_run(int B, int wide, int slot, bool queued, bool want_logits)
+{
+    const size_t b = static_cast<size_t>(B), wd = static_cast<size_t>(wide);
+    const InLayout lay = in_layout(B, wide);
     forward(B, stream_);
     const int64_t* I_d = reinterpret_cast<const int64_t*>(d_in_ + lay.I);
     const uint8_t* M_d = d_in_ + lay.M;
@@ -1561,6 +1608,50 @@ CUDANET_API int cudanet_evaluate(void* handle, int B, int wide, const int64_t* i
         std::lock_guard<std::mutex> lock(n->mu);
         n->begin(B, wide, ids, cast, hm, ep, I, M, false, false);
         n->end(pol, val, qv, nullptr);
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_evaluate_keys(void* handle, int B, int wide, const uint64_t* keys, const int64_t* ep_sq,
+                                      const int64_t* clock, const int64_t* I, const uint8_t* M, float* pol,
+                                      float* val, float* qv, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_evaluate_keys: unknown exception", [&] {
+        if (!handle) throw std::runtime_error("cudanet_evaluate_keys: null handle");
+        Net* n = static_cast<Net*>(handle);
+        std::lock_guard<std::mutex> lock(n->mu);
+        n->begin_keys(B, wide, keys, ep_sq, clock, I, M, false, false);
+        n->end(pol, val, qv, nullptr);
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_begin_keys(void* handle, int B, int wide, const uint64_t* keys, const int64_t* ep_sq,
+                                   const int64_t* clock, const int64_t* I, const uint8_t* M, char* err,
+                                   int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_begin_keys: unknown exception", [&] {
+        if (!handle) throw std::runtime_error("cudanet_begin_keys: null handle");
+        Net* n = static_cast<Net*>(handle);
+        std::lock_guard<std::mutex> lock(n->mu);
+        n->begin_keys(B, wide, keys, ep_sq, clock, I, M, true, false);
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_encode_keys(const uint64_t* keys, const int64_t* ep_sq, const int64_t* clock, int B,
+                                    int64_t* ids, float* cast, int64_t* hm, int64_t* ep, void* stream, char* err,
+                                    int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_encode_keys: unknown exception", [&] {
+        if (B < 0) throw std::runtime_error("cudanet_encode_keys: negative batch");
+        if (B == 0) return 0;
+        if (!keys || !ep_sq || !clock || !ids || !cast || !hm || !ep)
+            throw std::runtime_error("cudanet_encode_keys: a null pointer");
+        mf::launch_k(mf::encode_keys_kernel,
+                     dim3(static_cast<unsigned>((B + mf::kEncodeBoardsPerBlock - 1) / mf::kEncodeBoardsPerBlock)),
+                     dim3(64 * mf::kEncodeBoardsPerBlock), 0, static_cast<cudaStream_t>(stream), keys, ep_sq, clock,
+                     B, ids, cast, hm, ep);
         return 0;
     });
 }

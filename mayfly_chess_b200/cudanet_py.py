@@ -97,6 +97,12 @@ def load(dll=None):
         lib.cudanet_k_attention_f8.restype = i32
         lib.cudanet_k_layernorm_f8.argtypes = [i32, vp, vp, vp, vp, i32, i32, i32, f32, vp, cp, i32]
         lib.cudanet_k_layernorm_f8.restype = i32
+        lib.cudanet_evaluate_keys.argtypes = [vp, i32, i32] + [vp] * 8 + [cp, i32]
+        lib.cudanet_evaluate_keys.restype = i32
+        lib.cudanet_begin_keys.argtypes = [vp, i32, i32] + [vp] * 5 + [cp, i32]
+        lib.cudanet_begin_keys.restype = i32
+        lib.cudanet_encode_keys.argtypes = [vp, vp, vp, i32, vp, vp, vp, vp, vp, cp, i32]
+        lib.cudanet_encode_keys.restype = i32
         _libs[path] = lib
         return lib
 
@@ -165,6 +171,49 @@ class CudaNet:
         if rc != 0:
             raise RuntimeError(f"cudanet_evaluate: {_msg(err)}")
         return pol, val, qv
+
+    def _key_inputs(self, keys, ep_sq, clock, I, M):
+        if self._h is None:
+            raise RuntimeError("CudaNet is closed")
+        I = np.asarray(I)
+        if I.ndim != 2:
+            raise ValueError(f"I: shape {I.shape}, expected (B, wide)")
+        B, wide = I.shape
+        if not 1 <= B <= self.max_batch:
+            raise ValueError(f"batch {B}: cudanet takes 1 to {self.max_batch} (env MAYFLY_CUDANET_MAX_BATCH)")
+        if wide < 1:
+            raise ValueError("wide must be at least 1")
+        return (B, wide, _arr(keys, np.uint64, (B, 10), "keys"), _arr(ep_sq, np.int64, (B,), "ep_sq"),
+                _arr(clock, np.int64, (B,), "clock"), _arr(I, np.int64, (B, wide), "I"),
+                _arr(M, np.uint8, (B, wide), "M"))
+
+    def evaluate_keys(self, keys, ep_sq, clock, I, M):
+        """evaluate from transposition keys: keys (B, 10) uint64 = Board._transposition_key()[0:10] (turn and
+        castling rights as integers), ep_sq (B,) the key's en passant square or -1 for None, clock (B,) the
+        halfmove clocks. The GPU encodes them exactly as mayfly/chess/encode.py encode_keys does."""
+        B, wide, keys, ep_sq, clock, I, M = self._key_inputs(keys, ep_sq, clock, I, M)
+        pol = np.zeros((B, wide), np.float32)
+        val = np.zeros(B, np.float32)
+        qv = np.zeros((B, wide), np.float32)
+        err = ctypes.create_string_buffer(ERR_LEN)
+        with self._lock:
+            rc = self._lib.cudanet_evaluate_keys(self._h, B, wide, _p(keys), _p(ep_sq), _p(clock), _p(I), _p(M),
+                                                 _p(pol), _p(val), _p(qv), err, ERR_LEN)
+        if rc != 0:
+            raise RuntimeError(f"cudanet_evaluate_keys: {_msg(err)}")
+        return pol, val, qv
+
+    def begin_keys(self, keys, ep_sq, clock, I, M):
+        """begin from transposition keys (see evaluate_keys); end() returns the outputs."""
+        B, wide, keys, ep_sq, clock, I, M = self._key_inputs(keys, ep_sq, clock, I, M)
+        err = ctypes.create_string_buffer(ERR_LEN)
+        with self._lock:
+            rc = self._lib.cudanet_begin_keys(self._h, B, wide, _p(keys), _p(ep_sq), _p(clock), _p(I), _p(M), err,
+                                              ERR_LEN)
+            if rc == 0:
+                self._fly = getattr(self, "_fly", []) + [(B, wide)]
+        if rc != 0:
+            raise RuntimeError(f"cudanet_begin_keys: {_msg(err)}")
 
     def evaluate_logits(self, ids, cast, hm, ep, I, M):
         """evaluate, plus the full logits (B, 2 * 4162) float32: policy, then qvalue."""
@@ -324,6 +373,53 @@ def _dtype_code(t):
 def _stream():
     import torch
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def encode_keys_device(keys, ep_sq, clock, dll=None):
+    """The GPU batch encoder on torch CUDA tensors: keys (B, 10) int64/uint64 words, ep_sq (B,) int64 (-1 for
+    None), clock (B,) int64, on the current stream. Returns (ids (B, 64) int64, cast (B, 4) float32, hm (B,)
+    int64, ep (B,) int64), encode.py encode_keys' values."""
+    import torch
+    lib = load(dll)
+    B = keys.shape[0]
+    for name, t in (("keys", keys), ("ep_sq", ep_sq), ("clock", clock)):
+        if not t.is_cuda or t.element_size() != 8 or not t.is_contiguous():
+            raise ValueError(f"{name}: needs a contiguous CUDA tensor of 64-bit words")
+    if tuple(keys.shape) != (B, 10) or tuple(ep_sq.shape) != (B,) or tuple(clock.shape) != (B,):
+        raise ValueError("keys (B, 10), ep_sq (B,), clock (B,)")
+    dev = keys.device
+    ids = torch.empty(B, 64, dtype=torch.int64, device=dev)
+    cast = torch.empty(B, 4, dtype=torch.float32, device=dev)
+    hm = torch.empty(B, dtype=torch.int64, device=dev)
+    ep = torch.empty(B, dtype=torch.int64, device=dev)
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_encode_keys(keys.data_ptr(), ep_sq.data_ptr(), clock.data_ptr(), B, ids.data_ptr(),
+                                 cast.data_ptr(), hm.data_ptr(), ep.data_ptr(), _stream(), err, ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_encode_keys: {_msg(err)}")
+    return ids, cast, hm, ep
+
+
+def keys_from_tuples(keys):
+    """Board._transposition_key() tuples (pawns .. castling rights, en passant square or None) as the arrays
+    the key entry points take: (keys (B, 10) uint64, ep_sq (B,) int64 with -1 for None)."""
+    B = len(keys)
+    K = np.array([[int(k[j]) for j in range(10)] for k in keys], dtype=np.uint64).reshape(B, 10)
+    ep = np.array([-1 if k[10] is None else int(k[10]) for k in keys], dtype=np.int64)
+    return K, ep
+
+
+def encode_keys(keys, hms, device=0, dll=None):
+    """mayfly/chess/encode.py:73-100 encode_keys(keys, hms) with the same arguments and results (numpy ids
+    (B, 64) int64, cast (B, 4) float32, hm (B,) int64, ep (B,) int64), computed by the GPU encoder."""
+    import torch
+    K, ep_sq = keys_from_tuples(keys)
+    clock = np.asarray(hms, np.int64).reshape(len(keys))
+    with torch.cuda.device(device):
+        t = [torch.from_numpy(a.view(np.int64) if a.dtype == np.uint64 else a).cuda() for a in (K, ep_sq, clock)]
+        out = encode_keys_device(*t, dll=dll)
+        torch.cuda.current_stream().synchronize()
+    return tuple(o.cpu().numpy() for o in out)
 
 
 def k_gemm(A, W, bias, C, epi, bn=0, dll=None):

@@ -85,4 +85,17 @@ int cc_turn(const void* pos)
     return p.turn;
 }
 
+// chess_core.cpp make_key: python-chess's Board._transposition_key() (chess_core.h:15-27) as the ten 64-bit words
+// encode.py:48 packs (pawns, knights, bishops, rooks, queens, kings, white, black, turn 1/0, clean castling
+// rights) and the legal en passant square (-1 for None)
+void cc_key(const void* pos, uint64_t* k10, int* ep)
+{
+    Pos p;
+    std::memcpy(&p, pos, sizeof(Pos));
+    const mayfly::Key k = mayfly::make_key(p);
+    const uint64_t v[10] = {k.P, k.N, k.B, k.R, k.Q, k.K, k.W, k.Bk, (uint64_t)(k.turn ? 1 : 0), k.castle};
+    std::memcpy(k10, v, sizeof(v));
+    *ep = k.ep;
+}
+
 }  // extern "C"

@@ -52,6 +52,8 @@ def lib():
         L.cc_halfmove.restype = i32
         L.cc_turn.argtypes = [vp]
         L.cc_turn.restype = i32
+        L.cc_key.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_int)]
+        L.cc_key.restype = None
         L.cc_init()
         _lib = L
     return _lib
@@ -84,6 +86,17 @@ class Position:
     def push(self, code):
         lib().cc_push(self.buf, int(code))
 
+    def key(self):
+        """The transposition key (chess_core make_key = Board._transposition_key()): ten uint64 words in
+        encode.py's _KEY10 order and the legal en passant square (-1 for None)."""
+        k = np.zeros(10, np.uint64)
+        ep = ctypes.c_int(0)
+        lib().cc_key(self.buf, k.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), ctypes.byref(ep))
+        return k, int(ep.value)
+
+    def halfmove(self):
+        return int(lib().cc_halfmove(self.buf))
+
     def encode(self):
         ids = np.zeros(64, np.int64)
         cast = np.zeros(4, np.float32)
@@ -110,6 +123,18 @@ def random_playouts(n, seed, max_plies):
             p = nxt
         out.append(p)
     return out
+
+
+def key_batch(positions):
+    """(keys uint64 (B, 10), ep int64 (B,) with -1 for None, clock int64 (B,)): what encode_keys reads."""
+    B = len(positions)
+    keys = np.zeros((B, 10), np.uint64)
+    ep = np.zeros(B, np.int64)
+    clock = np.zeros(B, np.int64)
+    for i, p in enumerate(positions):
+        keys[i], ep[i] = p.key()
+        clock[i] = p.halfmove()
+    return keys, ep, clock
 
 
 def encode_batch(positions):

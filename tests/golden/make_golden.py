@@ -27,7 +27,14 @@ Fixtures (all small .npz):
   full_seed1_b64.npz          the 146M net (d 1024, 16 layers, 16 heads, FFN 2048), seed-1 weights, the first 64
                               seed-1 positions
   full_seed1_fixed.npz        the 146M net on the fixed edge-case positions
+  keys_seed1.npz              the batch encoder from transposition keys (encode.py:73-100 encode_keys, run
+                              itself): the first 2,048 seed-1 positions, the fixed positions and 4,096 seeded
+                              synthetic keys (random bitboards, kings on the corners, castling bits, black to
+                              move, clocks past 100), with encode_keys' ids, cast, hm and ep for each; the real
+                              positions are also checked against chess_core.cpp:582-612 encode
   meta.json                   fingerprints, state dict names and shapes, how each case was made
+
+    python tests/golden/make_golden.py --only keys     regenerates keys_seed1.npz alone (seconds)
 """
 import argparse
 import ast
@@ -129,6 +136,76 @@ def reference_outputs(chess_net, export_ts, arch, state, batch):
     return P, r["val"].astype(np.float32), Q, pol.numpy(), qval.numpy()
 
 
+def synthetic_keys(n, seed):
+    """n seeded transposition keys that stress encode_keys' bit arithmetic: random piece bitboards split between
+    the colours, kings on a1/h1/a8/h8 or anywhere, random castling-rights bits on both back ranks, either side
+    to move, en passant squares or None, clocks 0..300. Not all are legal chess positions; the encoder's
+    arithmetic is defined on any key."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    keys = np.zeros((n, 10), np.uint64)
+    ep = np.full(n, -1, np.int64)
+    corners = np.array([0, 7, 56, 63], np.uint64)
+    for i in range(n):
+        occ = rng.integers(0, 2**63, dtype=np.uint64) & rng.integers(0, 2**63, dtype=np.uint64)
+        types = rng.integers(0, 6, 64)
+        bb = [np.uint64(0)] * 6
+        for sq in range(64):
+            if (int(occ) >> sq) & 1:
+                bb[types[sq]] |= np.uint64(1) << np.uint64(sq)
+        kings = np.uint64(0)
+        for c in range(2):
+            sq = corners[rng.integers(0, 4)] if rng.random() < 0.5 else np.uint64(rng.integers(0, 64))
+            kings |= np.uint64(1) << sq
+        for t in range(5):
+            bb[t] &= ~kings
+        bb[5] = kings
+        allp = np.uint64(0)
+        for t in range(6):
+            allp |= bb[t]
+        white_mask = rng.integers(0, 2**63, dtype=np.uint64) | (np.uint64(rng.integers(0, 2)) << np.uint64(63))
+        keys[i, :6] = bb
+        keys[i, 6] = allp & white_mask
+        keys[i, 7] = allp & ~white_mask
+        keys[i, 8] = rng.integers(0, 2)
+        cr = np.uint64(0)
+        for sq in (0, 7, 56, 63, int(rng.integers(0, 8)), 56 + int(rng.integers(0, 8))):
+            if rng.random() < 0.5:
+                cr |= np.uint64(1) << np.uint64(sq)
+        keys[i, 9] = cr
+        if rng.random() < 0.3:
+            ep[i] = int(rng.integers(16, 24)) if keys[i, 8] == 0 else int(rng.integers(40, 48))
+    clock = rng.integers(0, 301, n).astype(np.int64)
+    return keys, ep, clock
+
+
+def keys_case(ref, meta):
+    """keys_seed1.npz: encode.py's own encode_keys on keys from chess_core positions and on synthetic keys."""
+    from oracle import positions as P
+    import encode   # noqa: E402  (mayfly/chess/encode.py, with the constants stub as `chess`)
+    pos = P.random_playouts(2048, seed=1, max_plies=120) + [p for _, _, p in fixed_fens(ref)]
+    k_pos, ep_pos, clock_pos = P.key_batch(pos)
+    k_syn, ep_syn, clock_syn = synthetic_keys(4096, seed=7)
+    keys = np.concatenate([k_pos, k_syn])
+    ep_sq = np.concatenate([ep_pos, ep_syn])
+    clock = np.concatenate([clock_pos, clock_syn])
+    tuples = [tuple(bool(k[8]) if j == 8 else int(k[j]) for j in range(10)) + (None if e < 0 else int(e),)
+              for k, e in zip(keys, ep_sq)]
+    ids, cast, hm, ep = encode.encode_keys(tuples, [int(c) for c in clock])
+    for i, p in enumerate(pos):   # the reference's two encoders agree on real positions
+        e_ids, e_cast, e_hm, e_ep = p.encode()
+        if not (np.array_equal(e_ids, ids[i]) and np.array_equal(e_cast, cast[i]) and e_hm == hm[i]
+                and e_ep == ep[i]):
+            raise SystemExit(f"encode_keys and chess_core encode differ at position {i}")
+    np.savez_compressed(os.path.join(HERE, "keys_seed1.npz"), keys=keys, ep_sq=ep_sq, clock=clock,
+                        ids=ids.astype(np.int64), cast=cast.astype(np.float32), hm=hm.astype(np.int64),
+                        ep=ep.astype(np.int64), n_positions=np.int64(len(pos)))
+    meta["cases"]["keys_seed1"] = {
+        "B": int(keys.shape[0]), "positions": len(pos),
+        "note": "encode.py encode_keys outputs: 2,048 seed-1 positions (positions_seed1 rows 0..2047), the fixed "
+                "positions, then 4,096 synthetic keys (seed 7); real positions checked against chess_core encode"}
+    print(f"keys_seed1: {keys.shape[0]} keys ({len(pos)} positions)")
+
+
 def check_state_spec(chess_net, arch):
     m = chess_net.ChessNet(d=arch.d, nhead=arch.heads, layers=arch.layers, dim_ff=arch.ff, qhead=True)
     ref = [(k, tuple(v.shape)) for k, v in m.state_dict().items() if v.is_floating_point()]
@@ -155,11 +232,19 @@ def save_case(name, arch, seed, batch, outs, note, meta, full_rows=4, rounded=No
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", choices=["keys"], help="regenerate one fixture alone")
     args = ap.parse_args()
     subprocess.run(["make", "-C", os.path.join(REPO, "oracle"), f"REF={args.ref}"], check=True)
     from oracle import positions as P
 
     chess_net, export_ts = import_reference(args.ref)
+    if args.only == "keys":
+        with open(os.path.join(HERE, "meta.json")) as f:
+            meta = json.load(f)
+        keys_case(args.ref, meta)
+        with open(os.path.join(HERE, "meta.json"), "w") as f:
+            json.dump(meta, f, indent=1)
+        return
     meta = {"generator": "tests/golden/make_golden.py", "torch": torch.__version__, "cases": {}}
     for tag, arch in (("small", W.SMALL), ("full", W.FULL)):
         meta[f"state_keys_{tag}"] = check_state_spec(chess_net, arch)
@@ -203,6 +288,7 @@ def main():
     o, rd = run(W.FULL, st, fixed_batch)
     save_case("full_seed1_fixed", W.FULL, 1, fixed_batch, o, "fixed edge cases", meta, rounded=rd)
     print(f"146M reference forward: {time.time() - t:.1f} s")
+    keys_case(args.ref, meta)
     with open(os.path.join(HERE, "meta.json"), "w") as f:
         json.dump(meta, f, indent=1)
     print("done")
