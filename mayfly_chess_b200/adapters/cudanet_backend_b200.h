@@ -1,10 +1,11 @@
-// mayfly2::Net (the reference's C++ search, mayfly/chess/cpp/search2.h:55-88) on libcudanet_b200.so.
+// The C++ search's two network interfaces on libcudanet_b200.so: mayfly2::Net (mayfly/chess/cpp/search2.h:55-88,
+// the persistent tree) and mayfly::NetBackend (cpp/netbackend.h:43-48). A drop-in for the reference's
+// cudanet/cudanet_backend.h: the same three factory functions (make_cuda_net, cuda_net_fingerprint,
+// make_cuda_backend) with the same meaning, so cpp/pyext.cpp:195-203 builds unchanged against this header. Put the
+// reference's cpp/ folder and this repository's include/ on the include path and link libcudanet_b200.so.
+// Header-only.
 //
-// The reference builds its search extension with its own CUDA backend behind this interface
-// (mayfly/chess/cudanet/cudanet_backend.cpp:42-102 CudaNetAdapter, chosen by cpp/pyext.cpp:195-203 for ".cnw"
-// paths). This is the same adapter over this library's C ABI: include it after search2.h, with include/ of this
-// repository on the include path, and link libcudanet_b200.so. Header-only.
-//
+// mayfly2::CudaB200Net (cudanet_backend.cpp:42-102 CudaNetAdapter):
 //   evaluate       cudanet_evaluate: the batch search2 encoded (Batch: ids, cast, hm, ep, I, M), the policy
 //                  logits cut to each row's legal moves, the value and the per-move q back (Out), which is
 //                  exactly what search2 expects (the reference adapter passes them through the same way)
@@ -13,13 +14,19 @@
 //                  two in flight, as search2 keeps them.
 // Errors come back from the library as -1 with a message and are thrown as std::runtime_error, as search2's
 // Net contract asks ("throws on failure").
+// mayfly::CudaB200Backend (cudanet_backend.cpp:105-151 CudaBackend): the same pass, then the cut policy scattered
+// into full B x 4162 rows at each row's legal moves (policy[b*4162 + I[b*wide+j]], j < widths[b]), every other
+// entry 0 — all the search reads, as the reference's CUDA backend documents (cudanet_backend.h:25-30).
 #pragma once
 #include <deque>
 #include <stdexcept>
 #include <string>
 #include <utility>
+#include <vector>
 
 #include "cudanet_b200.h"
+#include "netbackend.h"
+#include "search2.h"
 
 namespace mayfly2 {
 
@@ -97,4 +104,66 @@ private:
     std::deque<std::pair<int, int>> fly_;   // (B, wide) of each batch submitted and not yet collected
 };
 
+// cudanet_backend.h:13-17: the evaluator on `device` from a .cnw file, behind mayfly2::Net
+inline Net* make_cuda_net(const std::string& weights_path, int device)
+{
+    return new CudaB200Net(weights_path, device);
+}
+
+// cudanet_backend.h:19-21: the weight file's fingerprint for a Net made above, empty for any other Net
+inline std::string cuda_net_fingerprint(Net* net)
+{
+    CudaB200Net* a = dynamic_cast<CudaB200Net*>(net);
+    return a ? a->fingerprint() : std::string();
+}
+
 }  // namespace mayfly2
+
+namespace mayfly {
+
+class CudaB200Backend : public NetBackend {
+public:
+    CudaB200Backend(const std::string& weights_path, int device) : net_(weights_path, device) {}
+
+    void evaluate(const NetBatch& in, NetResult& out) override
+    {
+        if (in.widths.size() != static_cast<size_t>(in.B))
+            throw std::runtime_error("cudanet_b200: widths has the wrong size");
+        mayfly2::Batch b;
+        b.B = in.B;
+        b.wide = in.wide;
+        b.ids = in.ids;
+        b.cast = in.cast;
+        b.hm = in.hm;
+        b.ep = in.ep;
+        b.I = in.I;
+        b.M = in.M;
+        mayfly2::Out o;
+        net_.evaluate(b, o);
+        const size_t B = static_cast<size_t>(in.B), W = static_cast<size_t>(in.wide);
+        out.val = std::move(o.val);
+        out.qv = std::move(o.qv);
+        out.policy.assign(B * static_cast<size_t>(kMoves), 0.0f);
+        for (size_t r = 0; r < B; ++r) {
+            const size_t n = static_cast<size_t>(in.widths[r]);
+            if (n > W) throw std::runtime_error("cudanet_b200: a row is wider than wide");
+            float* row = out.policy.data() + r * static_cast<size_t>(kMoves);
+            for (size_t j = 0; j < n; ++j) {
+                const int64_t m = in.I[r * W + j];
+                if (m < 0 || m >= kMoves) throw std::runtime_error("cudanet_b200: a move index is out of range");
+                row[m] = o.pol[r * W + j];
+            }
+        }
+    }
+
+private:
+    mayfly2::CudaB200Net net_;
+};
+
+// cudanet_backend.h:23-31
+inline NetBackend* make_cuda_backend(const std::string& weights_path, int device)
+{
+    return new CudaB200Backend(weights_path, device);
+}
+
+}  // namespace mayfly

@@ -1,6 +1,6 @@
 // TEST INFRASTRUCTURE ONLY. The reference's own C++ search (mayfly/chess/cpp/search2.{h,cpp}, compiled from its
 // sources by oracle/Makefile into oracle/_ref/libsearch2_b200.so together with chess_core.cpp) driving this
-// repository's evaluator through the product adapter mayfly_chess_b200/adapters/search2_net.h. A flat C
+// repository's evaluator through the product adapter mayfly_chess_b200/adapters/cudanet_backend_b200.h. A flat C
 // interface for tests/test_search2_gpu.py:
 //
 //   s2_open     a CudaB200Net on a weight file, wrapped in a recorder that can keep every batch search2 sends and
@@ -11,6 +11,7 @@
 //               pipeline, expand_root when needed, step() until the root has `target` visits or the tree is
 //               saturated, finish(); the root's moves, visit counts, choose() and the tree's counters out.
 //   s2_record / s2_recorded / s2_get   the recorded batches and outputs.
+//   s2_backend  one batch through mayfly::NetBackend (make_cuda_backend): full policy rows, val, qv.
 #include <cstdint>
 #include <cstring>
 #include <deque>
@@ -19,8 +20,7 @@
 #include <string>
 #include <vector>
 
-#include "search2.h"
-#include "../mayfly_chess_b200/adapters/search2_net.h"
+#include "../mayfly_chess_b200/adapters/cudanet_backend_b200.h"
 
 namespace {
 
@@ -67,8 +67,11 @@ private:
 };
 
 struct Handle {
-    std::unique_ptr<mayfly2::CudaB200Net> net;
+    std::unique_ptr<mayfly2::Net> net;
     std::unique_ptr<Recorder> rec;
+    std::unique_ptr<mayfly::NetBackend> backend;
+    std::string weights;
+    int device = 0;
 };
 
 void put(char* err, int len, const char* msg)
@@ -87,8 +90,11 @@ void* s2_open(const char* weights, int device, int mode, char* err, int err_len)
 {
     try {
         auto h = std::make_unique<Handle>();
-        h->net = std::make_unique<mayfly2::CudaB200Net>(weights, device);
+        h->net.reset(mayfly2::make_cuda_net(weights, device));
+        if (mayfly2::cuda_net_fingerprint(h->net.get()).empty()) throw std::runtime_error("no fingerprint");
         h->rec = std::make_unique<Recorder>(h->net.get(), mode == 0);
+        h->weights = weights;
+        h->device = device;
         return h.release();
     } catch (const std::exception& e) {
         put(err, err_len, e.what());
@@ -169,6 +175,37 @@ int s2_search(void* hp, const char* fen, int batch, int pipeline, double target,
         stats[6] = (long long)(1e6 * (pf.net + pf.submit + pf.collect));
         stats[7] = (long long)(1e6 * pf.encode);
         return n;
+    } catch (const std::exception& e) {
+        put(err, err_len, e.what());
+        return -1;
+    }
+}
+
+// policy: B x 4162 f32, val: B, qv: B x wide. Returns 0, or -1 with err.
+int s2_backend(void* hp, int B, int wide, const int64_t* ids, const float* cast, const int64_t* hm,
+               const int64_t* ep, const int64_t* I, const uint8_t* M, const int* widths, float* policy, float* val,
+               float* qv, char* err, int err_len)
+{
+    try {
+        Handle* h = static_cast<Handle*>(hp);
+        if (!h->backend) h->backend.reset(mayfly::make_cuda_backend(h->weights, h->device));
+        mayfly::NetBatch in;
+        const size_t b = (size_t)B, w = (size_t)wide;
+        in.B = B;
+        in.wide = wide;
+        in.ids.assign(ids, ids + b * 64);
+        in.cast.assign(cast, cast + b * 4);
+        in.hm.assign(hm, hm + b);
+        in.ep.assign(ep, ep + b);
+        in.I.assign(I, I + b * w);
+        in.M.assign(M, M + b * w);
+        in.widths.assign(widths, widths + b);
+        mayfly::NetResult out;
+        h->backend->evaluate(in, out);
+        std::memcpy(policy, out.policy.data(), 4 * out.policy.size());
+        std::memcpy(val, out.val.data(), 4 * out.val.size());
+        std::memcpy(qv, out.qv.data(), 4 * out.qv.size());
+        return 0;
     } catch (const std::exception& e) {
         put(err, err_len, e.what());
         return -1;

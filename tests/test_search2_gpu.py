@@ -1,6 +1,6 @@
 """The reference's own C++ search (mayfly/chess/cpp/search2.cpp, built from its sources into
 oracle/_ref/libsearch2_b200.so by oracle/Makefile) running on this evaluator through the product adapter
-mayfly_chess_b200/adapters/search2_net.h (mayfly2::Net over the C ABI, search2.h:55-88).
+mayfly_chess_b200/adapters/cudanet_backend_b200.h (mayfly2::Net over the C ABI, search2.h:55-88).
 
 What is checked:
   * the searches run to their visit targets and pick a legal root move;
@@ -44,6 +44,8 @@ def s2():
     L.s2_get.restype = i32
     L.s2_search.argtypes = [vp, cp, i32, i32, ctypes.c_double, vp, vp, i32, ctypes.POINTER(i32), vp, cp, i32]
     L.s2_search.restype = i32
+    L.s2_backend.argtypes = [vp, i32, i32] + [vp] * 10 + [cp, i32]
+    L.s2_backend.restype = i32
     return L
 
 
@@ -186,6 +188,40 @@ def test_search_throughput_146m(s2, tmp_path_factory, batch, pipeline):
           f"batches, {st[0] / step_s:.0f} evaluations/s over {step_s:.2f} s of steps; network {100 * net_s / step_s:.0f}%"
           f", encoding {100 * enc_s / step_s:.0f}% of it; {N.sum():.0f} root visits, {st[4]} tree nodes")
     assert 0 <= chosen < len(moves) and st[0] > 1000
+
+
+@pytest.mark.gpu
+def test_netbackend_full_rows(s2, small_net):
+    """mayfly::NetBackend (make_cuda_backend): the cut policy scattered into full 4,162-wide rows, 0 elsewhere,
+    val and qv as mayfly2::Net gives them."""
+    from mayfly_chess_b200.cudanet_py import CudaNet
+    from mayfly_chess_b200.inputs import PositionSet
+    from conftest import GOLDEN
+    path, _ = small_net
+    b = PositionSet(os.path.join(GOLDEN, "small_seed0_b256.npz")).batch(0, 40)
+    B, wide = b["I"].shape
+    widths = b["M"].sum(1).astype(np.int32)
+    policy = np.full((B, 4162), np.nan, np.float32)
+    val = np.zeros(B, np.float32)
+    qv = np.zeros((B, wide), np.float32)
+    M = b["M"].astype(np.uint8)
+    s = Search(s2, path, 0)
+    try:
+        err = ctypes.create_string_buffer(1024)
+        rc = s2.s2_backend(s.h, B, wide, *[np.ascontiguousarray(a).ctypes.data for a in
+                                           (b["ids"], b["cast"], b["hm"], b["ep"], b["I"], M, widths, policy, val,
+                                            qv)], err, 1024)
+        assert rc == 0, err.value
+    finally:
+        s.close()
+    with CudaNet(path) as net:
+        pol, v, q = net.evaluate(b["ids"], b["cast"], b["hm"], b["ep"], b["I"], b["M"])
+    np.testing.assert_array_equal(val, v)
+    np.testing.assert_array_equal(qv, q)
+    expect = np.zeros((B, 4162), np.float32)
+    for r in range(B):
+        expect[r, b["I"][r, :widths[r]]] = pol[r, :widths[r]]
+    np.testing.assert_array_equal(policy, expect)
 
 
 @pytest.mark.gpu
