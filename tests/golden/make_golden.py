@@ -32,9 +32,14 @@ Fixtures (all small .npz):
                               synthetic keys (random bitboards, kings on the corners, castling bits, black to
                               move, clocks past 100), with encode_keys' ids, cast, hm and ep for each; the real
                               positions are also checked against chess_core.cpp:582-612 encode
+  cnw_v1_seed1.json           what the reference's own exporter (mayfly/chess/cudanet/export_cudanet.py, run on a
+                              checkpoint of the seed-1 146M random-init state) writes: its header fields (the
+                              fingerprint mcts_cpp.fingerprint computes) and every tensor's name, dtype, shape,
+                              offset, size and SHA-256; the file itself (290 MB) is not kept
   meta.json                   fingerprints, state dict names and shapes, how each case was made
 
     python tests/golden/make_golden.py --only keys     regenerates keys_seed1.npz alone (seconds)
+    python tests/golden/make_golden.py --only cnw      regenerates cnw_v1_seed1.json alone (a minute)
 """
 import argparse
 import ast
@@ -206,6 +211,36 @@ def keys_case(ref, meta):
     print(f"keys_seed1: {keys.shape[0]} keys ({len(pos)} positions)")
 
 
+def cnw_case(ref):
+    """cnw_v1_seed1.json: the reference exporter's file for the seed-1 146M state, summarised."""
+    import hashlib
+    import tempfile
+    sys.path.insert(0, os.path.join(ref, "mayfly", "chess", "cudanet"))
+    import export_cudanet   # noqa: E402
+    st = W.random_state(W.FULL, 1)
+    with tempfile.TemporaryDirectory() as d:
+        ck = os.path.join(d, "seed1.pt")
+        torch.save({"model": {**st, "posidx": torch.arange(64)},
+                    "cfg": {"d": W.FULL.d, "layers": W.FULL.layers, "nhead": W.FULL.heads, "ff_mult": 2.0}}, ck)
+        out = os.path.join(d, "seed1.cnw")
+        argv = sys.argv
+        sys.argv = ["export_cudanet.py", ck, out]
+        try:
+            export_cudanet.main()
+        finally:
+            sys.argv = argv
+        hdr, arrays = export_cudanet.read_cnw(out)
+        size = os.path.getsize(out)
+    fix = {"generator": "tests/golden/make_golden.py --only cnw (mayfly/chess/cudanet/export_cudanet.py main)",
+           "file_bytes": size,
+           "header": {k: v for k, v in hdr.items() if k not in ("tensors", "source")},
+           "tensors": [dict(e, sha256=hashlib.sha256(np.ascontiguousarray(arrays[e["name"]]).tobytes()).hexdigest())
+                       for e in hdr["tensors"]]}
+    with open(os.path.join(HERE, "cnw_v1_seed1.json"), "w") as f:
+        json.dump(fix, f, indent=0)
+    print(f"cnw_v1_seed1: {len(fix['tensors'])} tensors, {size / 1e6:.1f} MB, fingerprint {hdr['fingerprint']}")
+
+
 def check_state_spec(chess_net, arch):
     m = chess_net.ChessNet(d=arch.d, nhead=arch.heads, layers=arch.layers, dim_ff=arch.ff, qhead=True)
     ref = [(k, tuple(v.shape)) for k, v in m.state_dict().items() if v.is_floating_point()]
@@ -232,12 +267,15 @@ def save_case(name, arch, seed, batch, outs, note, meta, full_rows=4, rounded=No
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=["keys"], help="regenerate one fixture alone")
+    ap.add_argument("--only", choices=["keys", "cnw"], help="regenerate one fixture alone")
     args = ap.parse_args()
     subprocess.run(["make", "-C", os.path.join(REPO, "oracle"), f"REF={args.ref}"], check=True)
     from oracle import positions as P
 
     chess_net, export_ts = import_reference(args.ref)
+    if args.only == "cnw":
+        cnw_case(args.ref)
+        return
     if args.only == "keys":
         with open(os.path.join(HERE, "meta.json")) as f:
             meta = json.load(f)
@@ -289,6 +327,7 @@ def main():
     save_case("full_seed1_fixed", W.FULL, 1, fixed_batch, o, "fixed edge cases", meta, rounded=rd)
     print(f"146M reference forward: {time.time() - t:.1f} s")
     keys_case(args.ref, meta)
+    cnw_case(args.ref)
     with open(os.path.join(HERE, "meta.json"), "w") as f:
         json.dump(meta, f, indent=1)
     print("done")

@@ -82,3 +82,27 @@ def test_e4m3_needs_calibration(tmp_path):
         W.act_scales(np.ones((W.SMALL.layers, 3)), W.SMALL)
     s = W.act_scales(np.zeros((W.SMALL.layers, 4)), W.SMALL)
     assert np.all(s == 1.0)       # a product input that is all zeros keeps scale 1
+
+
+def test_v1_writer_matches_the_reference_exporter(tmp_path):
+    """A version-1 (f16) file from this writer is byte-for-byte the reference exporter's
+    (mayfly/chess/cudanet/export_cudanet.py) for the same weights: the same header fields, fingerprint
+    (mcts_cpp.fingerprint) included, and every tensor's name, dtype, shape, offset, size and SHA-256, summarised
+    in tests/golden/cnw_v1_seed1.json by tests/golden/make_golden.py. So the evaluator's reader of its own f16
+    files is the reader of the reference's."""
+    import hashlib
+    import json
+    import os
+    from conftest import GOLDEN
+    from mayfly_chess_b200 import weights as W
+    with open(os.path.join(GOLDEN, "cnw_v1_seed1.json")) as f:
+        ref = json.load(f)
+    path = str(tmp_path / "seed1_f16.cnw")
+    W.write_cnw(path, W.random_state(W.FULL, 1), W.FULL, "f16")
+    hdr, arrays = W.read_cnw(path)
+    assert os.path.getsize(path) == ref["file_bytes"]
+    assert {k: v for k, v in hdr.items() if k not in ("tensors", "source")} == ref["header"]
+    assert len(hdr["tensors"]) == len(ref["tensors"])
+    for mine, theirs in zip(hdr["tensors"], ref["tensors"]):
+        sha = hashlib.sha256(np.ascontiguousarray(arrays[mine["name"]]).tobytes()).hexdigest()
+        assert dict(mine, sha256=sha) == theirs, mine["name"]
