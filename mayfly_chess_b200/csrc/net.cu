@@ -307,7 +307,10 @@ static void launch_gemm_pair_if(const CUtensorMap& ma, const CUtensorMap& mb, co
 // fit and the epilogue is light next to the MMAs (bias-only, f32 outputs, the f32 residual's TMA reduction, or
 // K >= 2048: measured on a B200, the pair kernel is faster for qkv, out and ff2 and slower for ff1, whose GELU
 // epilogue gates both CTAs of a pair, and for the bf16 residual's read-modify-write), else the widest single-CTA
-// tile that still gives every SM a tile (weights stream through fewer SMs otherwise).
+// tile that still gives two thirds of the SMs a tile. A launch costs ~10 us however small it is, so at small M
+// fewer, wider tiles win while most SMs are busy (measured, back-to-back launches: M = 4,160, the out product
+// 14.4 us with 132 tiles of 256 against 18.2 with 264 of 128; ff2 20.5 against 28.3); below that the weights
+// stream through too few SMs.
 constexpr int kPairTile = 2;
 
 // MAYFLY_CUDANET_TILE: "pair" or "single" forces the CTA-pair or the single-CTA kernels, anything else (the
@@ -330,7 +333,7 @@ static int pick_bn(int M, int N, int K, int epi, int num_sms)
     if (mode == 1 || (mode == 0 && light && ((M + 255) / 256) * ((N + 255) / 256) >= num_sms / 2)) return kPairTile;
     const int m_tiles = (M + 127) / 128;
     for (int bn : {256, 128})
-        if (m_tiles * ((N + bn - 1) / bn) >= num_sms) return bn;
+        if (3 * m_tiles * ((N + bn - 1) / bn) >= 2 * num_sms) return bn;
     return 64;
 }
 
