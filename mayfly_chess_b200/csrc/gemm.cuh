@@ -154,6 +154,7 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
         1024 + (size_t)STAGES * STAGE_BYTES + (size_t)EG * NBUF * CHUNK_BYTES + 256;
     static constexpr int THREADS = 64 + 128 * EG;
     static_assert(STAGES >= 3, "pipeline too shallow");
+    static_assert(!XLOAD || NBUF >= 2, "the residual loads refill a buffer NBUF - 1 chunks ahead: two at least");
     static_assert(SMEM <= 232448, "shared memory over the per-block limit");
     static_assert(BN % CHUNK_COLS == 0 && NC >= 1, "tile width must hold whole staging chunks");
     static_assert(!PAIR || BN == 256, "the pair kernel covers 256 columns");
