@@ -122,14 +122,16 @@ static CUtensorMap operand_map(const void* base, MapType type, uint64_t K, uint6
 
 // The output (and, for the residuals, the input) of a product: [M, N] with pitch ldc, 16-bit (`t16`) for
 // kEpiBias / kEpiBiasGelu, f32 for kEpiResidual / kEpiF32, e4m3 for kEpiGeluE4m3, bf16 for kEpiResidual16;
-// boxes of one staging chunk (128 rows x GemmCfg::ROW_BYTES: 64-byte rows for the GELU epilogues).
-static CUtensorMap output_map(void* base, int epi, MapType t16, int M, int N, int ldc)
+// boxes of one staging chunk (128 rows x GemmCfg::ROW_BYTES: 64-byte rows for the GELU epilogues and for the
+// bias epilogue of an FP8 product, `f8`).
+static CUtensorMap output_map(void* base, int epi, MapType t16, int M, int N, int ldc, bool f8 = false)
 {
     if (epi == kEpiResidual || epi == kEpiF32) return make_map(base, MapType::F32, N, M, ldc, 32, 128);
     if (epi == kEpiGeluE4m3) return make_map(base, MapType::U8, N, M, ldc, 64, 128, true);
     if (epi == kEpiBiasGelu) return make_map(base, t16, N, M, ldc, 32, 128, true);
     if (epi == kEpiResidual16) return make_map(base, MapType::BF16, N, M, ldc, 64, 128);
-    return make_map(base, t16, N, M, ldc, MF_BIAS_ROWB / 2, 128, MF_BIAS_ROWB == 64);
+    if (epi == kEpiBias && f8) return make_map(base, t16, N, M, ldc, 32, 128, true);
+    return make_map(base, t16, N, M, ldc, 64, 128);
 }
 
 // ------------------------------------------------------------------------------------------------ launchers
@@ -787,7 +789,7 @@ private:
     bool use_graph_ = true;
     CUtensorMap map_h_, map_att_, map_ff_, map_cls_, map_qkv_;
     std::map<std::pair<const void*, int>, CUtensorMap> wmaps_;
-    std::map<std::tuple<const void*, int, int, int, int>, CUtensorMap> omaps_;   // (out, epi, M, N, ldc)
+    std::map<std::tuple<const void*, int, int, int, int>, CUtensorMap> omaps_;   // (out, epi + 16 f8, M, N, ldc)
 
     struct Fly {
         int B, wide, slot;
@@ -985,9 +987,9 @@ void Net::gemm(int epi, const CUtensorMap& ma, const void* W, bool w_f8, int M, 
 {
     const int bn = pick_bn(M, N, K, epi, num_sms_);
     const CUtensorMap& mb = wmap(W, w_f8 ? MapType::U8 : type16(bf16()), N, K, static_cast<int>(w_box_rows(bn)));
-    const auto okey = std::make_tuple(static_cast<const void*>(out), epi, M, N, ldc);
+    const auto okey = std::make_tuple(static_cast<const void*>(out), epi + (w_f8 ? 16 : 0), M, N, ldc);
     auto it = omaps_.find(okey);
-    if (it == omaps_.end()) it = omaps_.emplace(okey, output_map(out, epi, type16(bf16()), M, N, ldc)).first;
+    if (it == omaps_.end()) it = omaps_.emplace(okey, output_map(out, epi, type16(bf16()), M, N, ldc, w_f8)).first;
     if (w_f8)
         launch_gemm<__nv_fp8_e4m3, __nv_bfloat16>(epi, bn, ma, mb, it->second, M, N, K, ep, err_word(), num_sms_, s);
     else if (bf16())
@@ -2009,7 +2011,7 @@ CUDANET_API int cudanet_k_gemm_f8(int epi, int bn, const void* A, const void* W,
         const CUtensorMap ma = mf::operand_map(A, mf::MapType::U8, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);
         const CUtensorMap mb = mf::operand_map(W, mf::MapType::U8, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
                                                mf::w_box_rows(bn));
-        const CUtensorMap mc = mf::output_map(C, epi, mf::MapType::BF16, M, N, ldc);
+        const CUtensorMap mc = mf::output_map(C, epi, mf::MapType::BF16, M, N, ldc, true);
         const mf::EpiArgs ep{bias, colscale, out_scale_inv};
         uint32_t* errw = nullptr;
         mf::RT(cudaMalloc(&errw, 4));
