@@ -160,10 +160,14 @@ CUDANET_API int cudanet_k_gemm_resln(int dtype, const void* A, const void* W, co
 CUDANET_API int cudanet_k_attention(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,
                                     char* err, int err_len);
 
-/* cudanet_k_attention on the tensor-memory kernel (tcgen05 products, head width 64 only), whichever kernel the
- * evaluator picks for this output type. */
+/* cudanet_k_attention on the two-group tensor-memory kernel (tcgen05 products, head width 64 only). */
 CUDANET_API int cudanet_k_attention_tc(int dtype, const void* qkv, void* att, int B, int d, int heads, void* stream,
                                        char* err, int err_len);
+/* One attention launch on a chosen kernel: kernel 0 the mma.sync kernel, 1 the two-group and 4 the four-group
+ * tensor-memory kernels (head width 64), -1 the evaluator's choice; e4m3_out writes e4m3 of att * mul (bf16
+ * qkv only), else att in the qkv type. For tests of every kernel on every output type. */
+CUDANET_API int cudanet_k_attention_kernel(int dtype, int e4m3_out, int kernel, const void* qkv, void* att, int B,
+                                           int d, int heads, float mul, void* stream, char* err, int err_len);
 
 /* att[b, :] = the attention output of board b's CLS query only (token 0 of each board), att dense [B, d]: what
  * the last layer needs, since the heads read the CLS row alone. No counterpart in the reference. */

@@ -317,4 +317,290 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ 
     if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
+// ------------------------------------------------------------------------------------------------ four groups
+// The same arithmetic with four softmax groups of 4 warps (576 threads), each group owning one tensor-memory
+// slot (columns 128 g .. 128 g + 79) and finishing its item before it takes the next: S(n) -> softmax -> P over
+// the Q tile -> (PV(n) on the tensor cores) -> O(n) normalised and stored -> slots handed back. Four items are
+// in flight instead of two and twice as many warps hide each other's latencies. Registers are tighter (112 a
+// thread), so a row's scores are read from tensor memory twice, 32 columns at a time: once for the row max, once
+// for the exponentials. The MMA thread issues whichever of the next S (its load landed, its group's slot free)
+// and the next PV (its P written) is ready first; it gives up after the wait limit with no progress.
+struct AttTc4Cfg {
+    static constexpr int DH = 64;
+    static constexpr int LS = 6;
+    static constexpr int G = 4;                              // softmax groups = tensor-memory slots
+    static constexpr int KEYS = 80;
+    static constexpr uint32_t Q_BYTES = 128 * 128;
+    static constexpr uint32_t KV_BYTES = KEYS * 128;
+    static constexpr uint32_t Q_OFF = 0, K_OFF = Q_BYTES, V_OFF = K_OFF + KV_BYTES;
+    static constexpr uint32_t LOAD_SLOT = V_OFF + KV_BYTES;
+    static constexpr uint32_t LOAD_BYTES = 3 * KEYS * 128;
+    static constexpr size_t SMEM = 1024 + LS * (size_t)LOAD_SLOT + 256;
+    static constexpr int THREADS = 64 + 128 * G;
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr uint32_t T_STRIDE = 128;
+    static_assert(LOAD_SLOT % 1024 == 0 && K_OFF % 1024 == 0 && V_OFF % 1024 == 0, "1024-byte aligned tiles");
+    static_assert(G * T_STRIDE <= TMEM_COLS && SMEM <= 232448, "resources");
+};
+
+template <typename T, typename TO>
+__global__ void __launch_bounds__(AttTc4Cfg::THREADS, 1)
+attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ att, int B, int heads, int d,
+                     float scale, float mul, uint32_t* err)
+{
+    using C = AttTc4Cfg;
+    constexpr int LS = C::LS, G = C::G;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + LS * C::LOAD_SLOT);   // [LS] Q, K, V landed
+    uint64_t* empty = full + LS;     // [LS] the load slot is finished with (its group's 4 warps)
+    uint64_t* sfull = empty + LS;    // [G] S in the group's tensor-memory slot
+    uint64_t* pready = sfull + G;    // [G] P in shared memory (4 warps)
+    uint64_t* ofull = pready + G;    // [G] O in the slot
+    uint64_t* tfree = ofull + G;     // [G] the slot is read (4 warps)
+    uint64_t* mma_done = tfree + G;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    volatile uint32_t* ok = tmem_slot + 1;   // [G x 2]: the leaders' broadcasts
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int items = B * heads;
+    const int my = (int)blockIdx.x < items ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+
+    for (int i = threadIdx.x; i < LS * 48 * 8; i += blockDim.x) {
+        const int sl = i / 384, rem = i % 384;
+        *reinterpret_cast<uint4*>(base + sl * C::LOAD_SLOT + C::Q_OFF + (80 + rem / 8) * 128 + (rem % 8) * 16) =
+            make_uint4(0, 0, 0, 0);
+    }
+    fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < LS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 4);
+        }
+        for (int i = 0; i < G; ++i) {
+            mbar_init(&sfull[i], 1);
+            mbar_init(&pready[i], 4);
+            mbar_init(&ofull[i], 1);
+            mbar_init(&tfree[i], 4);
+        }
+        mbar_init(mma_done, 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&tmQKV);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    griddep_wait();
+    if (threadIdx.x == 0) griddep_launch();
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            uint32_t issued = 0, issued_par = 0;
+            for (int n = 0; n < my; ++n) {
+                const int ls = n % LS, use = n / LS;
+                if (use > 0 && !mbar_wait(&empty[ls], (use - 1) & 1, err, kErrSmemEmpty)) break;
+                const int item = (int)blockIdx.x + n * (int)gridDim.x;
+                const int b = item / heads, h = item - b * heads;
+                uint8_t* sb = base + ls * C::LOAD_SLOT;
+                mbar_arrive_expect_tx(&full[ls], C::LOAD_BYTES);
+                tma_load_2d(sb + C::Q_OFF, &tmQKV, &full[ls], h * C::DH, b * kTokens);
+                tma_load_2d(sb + C::K_OFF, &tmQKV, &full[ls], d + h * C::DH, b * kTokens);
+                tma_load_2d(sb + C::V_OFF, &tmQKV, &full[ls], 2 * d + h * C::DH, b * kTokens);
+                issued |= 1u << ls;
+                issued_par = (issued_par & ~(1u << ls)) | ((uint32_t)(use & 1) << ls);
+            }
+            for (int sl = 0; sl < LS; ++sl)
+                if (issued & (1u << sl)) mbar_wait(&full[sl], (issued_par >> sl) & 1, err, kErrTmaFull);
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idS = Operand<T>::idesc(128, C::KEYS);
+            constexpr uint32_t idO = Operand<T>::idesc(128, C::DH) | (1u << 16);   // B (V) MN-major
+            int ns = 0, np = 0;                    // the next S and the next PV to issue
+            uint64_t t0 = globaltimer();
+            uint32_t idle = 0;
+            while (np < my) {
+                bool progressed = false;
+                if (ns < my && ns < np + G) {
+                    const int ls = ns % LS, g = ns % G;
+                    if (mbar_try_wait(&full[ls], (ns / LS) & 1) &&
+                        (ns < G || mbar_try_wait(&tfree[g], (ns / G - 1) & 1))) {
+                        tc_fence_after();
+                        const uint32_t sb = smem_u32(base + ls * C::LOAD_SLOT);
+#pragma unroll
+                        for (int k = 0; k < C::DH / 16; ++k)
+                            umma_f16(tmem + C::T_STRIDE * g, sdesc_sw128(sb + C::Q_OFF + 32u * k),
+                                     sdesc_sw128(sb + C::K_OFF + 32u * k), idS, k > 0 ? 1u : 0u);
+                        umma_commit(&sfull[g]);
+                        ++ns;
+                        progressed = true;
+                    }
+                }
+                if (np < ns) {
+                    const int ls = np % LS, g = np % G;
+                    if (mbar_try_wait(&pready[g], (np / G) & 1)) {
+                        tc_fence_after();
+                        const uint32_t sb = smem_u32(base + ls * C::LOAD_SLOT);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            umma_f16(tmem + C::T_STRIDE * g, sdesc_sw128(sb + C::Q_OFF + 32u * k),
+                                     sdesc_sw128(sb + C::V_OFF + 2048u * k), idO, k > 0 ? 1u : 0u);
+                        umma_commit(&ofull[g]);
+                        ++np;
+                        progressed = true;
+                    }
+                }
+                if (progressed) {
+                    idle = 0;
+                } else if ((++idle & 1023u) == 0) {
+                    const uint64_t now = globaltimer();
+                    if (idle == 1024u) t0 = now;          // the start of this stretch without progress
+                    else if (now - t0 > kWaitLimitNs) {
+                        set_error(err, kErrTmaFull);
+                        break;
+                    }
+                }
+            }
+            umma_commit(mma_done);
+            mbar_wait(mma_done, 0, err, kErrTmemFull);
+        }
+    } else {
+        // ---------------------------------------------------------------- softmax and output (four groups)
+        const int grp = (warp - 2) >> 2;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const bool live = quarter < 3;                   // rows 96..127 are padding
+        const bool leader = threadIdx.x == 64 + 128 * grp;
+        const uint32_t bar_id = 1 + grp;
+        const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + C::T_STRIDE * grp;
+        const float sl2 = scale * 1.4426950408889634f;
+        for (int n = grp; n < my; n += G) {
+            const int ls = n % LS;
+            const uint32_t par = (n / G) & 1;
+            if (leader) ok[2 * grp] = mbar_wait(&sfull[grp], par, err, kErrTmemFull) ? 1u : 0u;
+            named_barrier(bar_id, 128);
+            if (!ok[2 * grp]) break;
+            float p64 = 0.f, sum = 0.f;
+            if (live) {
+                tc_fence_after();
+                uint32_t r[32];
+                // pass 1: the row max over the 65 live keys (and key 64's score, kept)
+                float m = -INFINITY, s64;
+                {
+                    uint32_t r16[16];
+                    tmem_ld_32x32b_x16(t_row + 64, r16);
+                    tmem_ld_wait();
+                    s64 = __uint_as_float(r16[0]);
+                    m = s64;
+                }
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    tmem_ld_32x32b_x32(t_row + 32 * hh, r);
+                    tmem_ld_wait();
+                    float m4[4] = {m, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(r[j]));
+                    m = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+                }
+                const float mc = m * sl2;
+                // pass 2: exponentials, their sum, P (rounded to T) over the Q tile
+                uint8_t* pb = base + ls * C::LOAD_SLOT + C::Q_OFF;
+                float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    tmem_ld_32x32b_x32(t_row + 32 * hh, r);
+                    tmem_ld_wait();
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        const float p0 = ex2_approx(fmaf(__uint_as_float(r[j]), sl2, -mc));
+                        const float p1 = ex2_approx(fmaf(__uint_as_float(r[j + 1]), sl2, -mc));
+                        pk[j / 2] = pack2<T>(p0, p1);
+                        s4[(j / 2) & 3] += p0 + p1;
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        *reinterpret_cast<uint4*>(pb + swz<128>(row, 4 * hh + u)) =
+                            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+                }
+                p64 = ex2_approx(fmaf(s64, sl2, -mc));
+                sum = ((s4[0] + s4[1]) + (s4[2] + s4[3])) + p64;
+                fence_proxy_async_smem();   // the MMA (async proxy) reads what these generic stores wrote
+                tc_fence_before();          // and overwrites the S columns this thread has read
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pready[grp]);
+            if (leader) ok[2 * grp + 1] = mbar_wait(&ofull[grp], par, err, kErrTmemFull) ? 1u : 0u;
+            named_barrier(bar_id, 128);
+            if (!ok[2 * grp + 1]) break;
+            if (live) {
+                tc_fence_after();
+                const float inv = 1.f / sum;
+                const uint4* v64 = reinterpret_cast<const uint4*>(base + ls * C::LOAD_SLOT + C::V_OFF + 64 * 128);
+                const int item = (int)blockIdx.x + n * (int)gridDim.x;
+                const int b = item / heads, h = item - b * heads;
+                const size_t orow = (size_t)b * kTokens + row;
+#pragma unroll
+                for (int qq = 0; qq < 4; ++qq) {   // 16 output columns at a time
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(t_row + 16 * qq, r);
+                    tmem_ld_wait();
+                    float o[16];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const uint4 q = v64[2 * qq + u];
+                        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int c = 8 * u + 2 * i;
+                            o[c] = fmaf(p64, to_f32<T>(reinterpret_cast<const T*>(&w[i])[0]), __uint_as_float(r[c])) * inv;
+                            o[c + 1] = fmaf(p64, to_f32<T>(reinterpret_cast<const T*>(&w[i])[1]),
+                                            __uint_as_float(r[c + 1])) * inv;
+                        }
+                    }
+                    if (row < kTokens) {
+                        if constexpr (is_e4m3<TO>) {
+                            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(att) + orow * d +
+                                                                  (size_t)h * C::DH + 16 * qq);
+                            uint32_t w[4];
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+                                w[i] = pack_e4m3x4(o[4 * i] * mul, o[4 * i + 1] * mul, o[4 * i + 2] * mul,
+                                                   o[4 * i + 3] * mul);
+                            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                        } else {
+                            uint4* dst = reinterpret_cast<uint4*>(att + orow * d + (size_t)h * C::DH + 16 * qq);
+#pragma unroll
+                            for (int u = 0; u < 2; ++u)
+                                dst[u] = make_uint4(pack2<T>(o[8 * u], o[8 * u + 1]), pack2<T>(o[8 * u + 2], o[8 * u + 3]),
+                                                    pack2<T>(o[8 * u + 4], o[8 * u + 5]),
+                                                    pack2<T>(o[8 * u + 6], o[8 * u + 7]));
+                        }
+                    }
+                }
+                tc_fence_before();
+                fence_proxy_async_smem();   // the TMA refill of the load slot comes after these reads
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&tfree[grp]);
+                mbar_arrive(&empty[ls]);
+            }
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
 }  // namespace mf

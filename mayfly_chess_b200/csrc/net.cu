@@ -423,20 +423,43 @@ static void launch_attention_dh(const CUtensorMap& map, TO* att, int B, int d, i
              mul, err);
 }
 
-// Which attention kernel runs head width 64: measured on a B200, the tensor-memory kernel (attention_tc.cuh) is
-// faster where attention writes e4m3 (the FP8 pass: 8.5-8.9 vs 9.2-9.8 ms per 4,096-position pass) and the
-// mma.sync kernel where it writes 16-bit values (2.54 vs 2.79 ms per 1,024-position pass): the tensor-memory
-// kernel spends its time in the per-item handshakes between its softmax warps and the MMA thread, the mma.sync
-// kernel in keeping more items in flight. MAYFLY_CUDANET_ATT_TC=1 / 0 forces one of them.
+// Which attention kernel runs head width 64 (attention_tc.cuh has two tensor-memory kernels: two softmax groups
+// with a finished item pending per group, and four groups that finish each item before the next). Measured on a
+// B200: where attention writes 16-bit values the four-group kernel is fastest (2.41 ms per 1,024-position pass
+// against 2.59 for the mma.sync kernel and 2.90 for the two-group one); where it writes e4m3 (the FP8 pass) the
+// two-group kernel (9.44 against 9.57 ms per 4,096-position pass, and 9.2-9.8 for mma.sync). Forcing:
+// MAYFLY_CUDANET_ATT_TC=0 the mma.sync kernel, 1 the two-group kernel, 4 the four-group kernel.
 static int att_tc_mode()
 {
     static int mode = [] {
         const char* e = std::getenv("MAYFLY_CUDANET_ATT_TC");
         if (e && std::strcmp(e, "1") == 0) return 1;
+        if (e && std::strcmp(e, "4") == 0) return 4;
         if (e && std::strcmp(e, "0") == 0) return 0;
         return -1;
     }();
     return mode;
+}
+
+template <typename T, typename TO>
+static void launch_attention_tc4(const CUtensorMap& map, TO* att, int B, int d, int heads, float mul, uint32_t* err,
+                                 cudaStream_t s)
+{
+    using C = AttTc4Cfg;
+    static bool attr[64] = {};
+    static int sms[64] = {};
+    int dev = 0;
+    RT(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw std::runtime_error("cudanet_b200: device index out of range");
+    if (!attr[dev]) {
+        RT(cudaFuncSetAttribute(attention_tc4_kernel<T, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+        RT(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+        attr[dev] = true;
+    }
+    const int items = B * heads;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(C::DH));
+    launch_k(attention_tc4_kernel<T, TO>, dim3(std::min(items, sms[dev])), dim3(C::THREADS), C::SMEM, s, map, att, B,
+             heads, d, scale, mul, err);
 }
 
 // the tcgen05 attention (attention_tc.cuh): one CTA per SM, persistent over the (board, head) items
@@ -469,8 +492,9 @@ static void launch_attention(const CUtensorMap& map, TO* att, int B, int d, int 
     if (B < 1 || heads < 1 || d % heads) throw std::runtime_error("cudanet_b200: bad attention sizes");
     const int dh = d / heads;
     const int mode = att_tc_mode();
-    const bool tc = mode == 1 || (mode == -1 && is_e4m3<TO>);
-    if (dh == 64 && tc) launch_attention_tc<T, TO>(map, att, B, d, heads, mul, err, s);
+    const int pick = mode >= 0 ? mode : (is_e4m3<TO> ? 1 : 4);
+    if (dh == 64 && pick == 4) launch_attention_tc4<T, TO>(map, att, B, d, heads, mul, err, s);
+    else if (dh == 64 && pick == 1) launch_attention_tc<T, TO>(map, att, B, d, heads, mul, err, s);
     else if (dh == 64) launch_attention_dh<T, TO, 64>(map, att, B, d, heads, mul, err, s);
     else if (dh == 32) launch_attention_dh<T, TO, 32>(map, att, B, d, heads, mul, err, s);
     else throw std::runtime_error("cudanet_b200: head width must be 32 or 64");
@@ -1553,7 +1577,7 @@ static uint32_t* noalloc_scratch(int dev)
 // One attention launch of the unit-test entry points: its own error word, a map over exactly B * 65 rows.
 template <typename T, typename TO>
 static void attention_once(const void* qkv, void* att, int B, int d, int heads, float mul, cudaStream_t s,
-                           const char* who, bool force_tc = false)
+                           const char* who, int kernel = -1)
 {
     if (B < 1 || heads < 1 || d % heads) throw std::runtime_error(std::string(who) + ": bad sizes");
     if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(att)) & 15)
@@ -1563,12 +1587,12 @@ static void attention_once(const void* qkv, void* att, int B, int d, int heads, 
     RT(cudaMalloc(&errw, 4));
     RT(cudaMemset(errw, 0, 4));
     try {
-        if (force_tc) {
-            if (d / heads != 64) throw std::runtime_error(std::string(who) + ": head width must be 64");
-            launch_attention_tc<T, TO>(map, static_cast<TO*>(att), B, d, heads, mul, errw, s);
-        } else {
-            launch_attention<T, TO>(map, static_cast<TO*>(att), B, d, heads, mul, errw, s);
-        }
+        if (kernel >= 0 && d / heads != 64) throw std::runtime_error(std::string(who) + ": head width must be 64");
+        if (kernel == 1) launch_attention_tc<T, TO>(map, static_cast<TO*>(att), B, d, heads, mul, errw, s);
+        else if (kernel == 4) launch_attention_tc4<T, TO>(map, static_cast<TO*>(att), B, d, heads, mul, errw, s);
+        else if (kernel == 0) launch_attention_dh<T, TO, 64>(map, static_cast<TO*>(att), B, d, heads, mul, errw, s);
+        else if (kernel == -1) launch_attention<T, TO>(map, static_cast<TO*>(att), B, d, heads, mul, errw, s);
+        else throw std::runtime_error(std::string(who) + ": kernel must be -1, 0, 1 or 4");
         RT(cudaStreamSynchronize(s));
     } catch (...) {
         cudaFree(errw);
@@ -1939,11 +1963,31 @@ CUDANET_API int cudanet_k_attention_tc(int dtype, const void* qkv, void* att, in
         const cudaStream_t s = static_cast<cudaStream_t>(stream);
         if (dtype == 1)
             mf::attention_once<__nv_bfloat16, __nv_bfloat16>(qkv, att, B, d, heads, 1.f, s, "cudanet_k_attention_tc",
-                                                             true);
+                                                             1);
         else if (dtype == 0)
-            mf::attention_once<__half, __half>(qkv, att, B, d, heads, 1.f, s, "cudanet_k_attention_tc", true);
+            mf::attention_once<__half, __half>(qkv, att, B, d, heads, 1.f, s, "cudanet_k_attention_tc", 1);
         else
             throw std::runtime_error("cudanet_k_attention_tc: dtype must be 0 (f16) or 1 (bf16)");
+        return 0;
+    });
+}
+
+CUDANET_API int cudanet_k_attention_kernel(int dtype, int e4m3_out, int kernel, const void* qkv, void* att, int B,
+                                           int d, int heads, float mul, void* stream, char* err, int err_len)
+{
+    return mf::guarded(err, err_len, "cudanet_k_attention_kernel: unknown exception", [&] {
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        const char* who = "cudanet_k_attention_kernel";
+        if (e4m3_out && dtype == 1)
+            mf::attention_once<__nv_bfloat16, __nv_fp8_e4m3>(qkv, att, B, d, heads, mul, s, who, kernel);
+        else if (e4m3_out)
+            throw std::runtime_error("cudanet_k_attention_kernel: e4m3 outputs take bf16 qkv (dtype 1)");
+        else if (dtype == 1)
+            mf::attention_once<__nv_bfloat16, __nv_bfloat16>(qkv, att, B, d, heads, 1.f, s, who, kernel);
+        else if (dtype == 0)
+            mf::attention_once<__half, __half>(qkv, att, B, d, heads, 1.f, s, who, kernel);
+        else
+            throw std::runtime_error("cudanet_k_attention_kernel: dtype must be 0 (f16) or 1 (bf16)");
         return 0;
     });
 }

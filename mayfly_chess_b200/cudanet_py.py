@@ -84,6 +84,8 @@ def load(dll=None):
         lib.cudanet_k_attention.restype = i32
         lib.cudanet_k_attention_tc.argtypes = [i32, vp, vp, i32, i32, i32, vp, cp, i32]
         lib.cudanet_k_attention_tc.restype = i32
+        lib.cudanet_k_attention_kernel.argtypes = [i32, i32, i32, vp, vp, i32, i32, i32, ctypes.c_float, vp, cp, i32]
+        lib.cudanet_k_attention_kernel.restype = i32
         lib.cudanet_k_attention_cls.argtypes = [i32, vp, vp, i32, i32, i32, vp, cp, i32]
         lib.cudanet_k_attention_cls.restype = i32
         lib.cudanet_k_layernorm.argtypes = [i32, vp, vp, vp, vp, i32, i32, i32, vp, cp, i32]
@@ -470,6 +472,20 @@ def k_attention(qkv, att, B, d, heads, dll=None):
                                  ERR_LEN)
     if rc != 0:
         raise RuntimeError(f"cudanet_k_attention: {_msg(err)}")
+    return att
+
+
+def k_attention_kernel(qkv, att, B, d, heads, kernel, mul=1.0, dll=None):
+    """One attention launch on a chosen kernel (0 mma.sync, 1 two-group, 4 four-group tensor-memory, -1 the
+    evaluator's choice); att uint8 gets e4m3 of att * mul (bf16 qkv), else att in qkv's type."""
+    import torch
+    lib = load(dll)
+    err = ctypes.create_string_buffer(ERR_LEN)
+    rc = lib.cudanet_k_attention_kernel(_dtype_code(qkv), 1 if att.dtype == torch.uint8 else 0, int(kernel),
+                                        qkv.data_ptr(), att.data_ptr(), B, d, heads, float(mul), _stream(), err,
+                                        ERR_LEN)
+    if rc != 0:
+        raise RuntimeError(f"cudanet_k_attention_kernel: {_msg(err)}")
     return att
 
 

@@ -150,14 +150,20 @@ def test_layernorm_f8(k, xdtype, d, stride):
     assert_e4m3_close(h, y, slack=1e-4 * mul)
 
 
+@pytest.mark.parametrize("kernel", ["default", "mma", "tc", "tc4"])
 @pytest.mark.parametrize("d,heads", [(1024, 16), (256, 8)])
 @pytest.mark.parametrize("B", [1, 3, 64])
-def test_attention_f8(k, d, heads, B):
+def test_attention_f8(k, kernel, d, heads, B):
+    if kernel != "default" and d // heads != 64:
+        pytest.skip("the kernels chosen by name are the head-width-64 ones")
     rows = B * 65
     qkv = torch.randn(rows, 3 * d, device="cuda").to(torch.bfloat16)
     att = torch.full((rows, d), 0x7F, device="cuda", dtype=torch.uint8)
     mul = 100.0
-    k.k_attention_f8(qkv, att, B, d, heads, mul)
+    if kernel == "default":
+        k.k_attention_f8(qkv, att, B, d, heads, mul)
+    else:
+        k.k_attention_kernel(qkv, att, B, d, heads, {"mma": 0, "tc": 1, "tc4": 4}[kernel], mul)
     torch.cuda.synchronize()
     dh = d // heads
     q, kk, v = qkv.float().view(B, 65, 3, heads, dh).permute(2, 0, 3, 1, 4).unbind(0)

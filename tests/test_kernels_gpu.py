@@ -91,18 +91,22 @@ def test_gemm_repeatable(k, dtype):
     assert torch.equal(C1, C2)
 
 
-@pytest.mark.parametrize("kernel", ["default", "tc"])
+@pytest.mark.parametrize("kernel", ["default", "tc", "mma", "tc4"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("d,heads", [(1024, 16), (256, 8)])
 @pytest.mark.parametrize("B", [1, 3, 64, 300])
 def test_attention(k, kernel, dtype, d, heads, B):
-    """The evaluator's attention kernel, and the tensor-memory one (head width 64) on its own."""
-    if kernel == "tc" and d // heads != 64:
-        pytest.skip("the tensor-memory kernel takes head width 64")
+    """The evaluator's attention kernel, and each kernel for head width 64 on its own: the mma.sync kernel and
+    the two- and four-group tensor-memory kernels."""
+    if kernel != "default" and d // heads != 64:
+        pytest.skip("the kernels chosen by name are the head-width-64 ones")
     rows = B * 65
     qkv = torch.randn(rows, 3 * d, device="cuda").to(dtype)
     att = torch.full((rows, d), float("nan"), device="cuda", dtype=dtype)
-    (k.k_attention_tc if kernel == "tc" else k.k_attention)(qkv, att, B, d, heads)
+    if kernel in ("mma", "tc4"):
+        k.k_attention_kernel(qkv, att, B, d, heads, 0 if kernel == "mma" else 4)
+    else:
+        (k.k_attention_tc if kernel == "tc" else k.k_attention)(qkv, att, B, d, heads)
     torch.cuda.synchronize()
     dh = d // heads
     q, kk, v = qkv.float().view(B, 65, 3, heads, dh).permute(2, 0, 3, 1, 4).unbind(0)
