@@ -324,7 +324,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ 
 // in flight instead of two and twice as many warps hide each other's latencies. Registers are tighter (112 a
 // thread), so a row's scores are read from tensor memory twice, 32 columns at a time: once for the row max, once
 // for the exponentials. The MMA thread issues whichever of the next S (its load landed, its group's slot free)
-// and the next PV (its P written) is ready first; it gives up after the wait limit with no progress.
+// and the next PV (its P written) is ready first, polling with mbarrier.test_wait (which never suspends the
+// thread on one barrier while the other is ready); it gives up after the wait limit with no progress.
 struct AttTc4Cfg {
     static constexpr int DH = 64;
     static constexpr int LS = 6;
@@ -430,8 +431,8 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
                 bool progressed = false;
                 if (ns < my && ns < np + G) {
                     const int ls = ns % LS, g = ns % G;
-                    if (mbar_try_wait(&full[ls], (ns / LS) & 1) &&
-                        (ns < G || mbar_try_wait(&tfree[g], (ns / G - 1) & 1))) {
+                    if (mbar_test_wait(&full[ls], (ns / LS) & 1) &&
+                        (ns < G || mbar_test_wait(&tfree[g], (ns / G - 1) & 1))) {
                         tc_fence_after();
                         const uint32_t sb = smem_u32(base + ls * C::LOAD_SLOT);
 #pragma unroll
@@ -445,7 +446,7 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
                 }
                 if (np < ns) {
                     const int ls = np % LS, g = np % G;
-                    if (mbar_try_wait(&pready[g], (np / G) & 1)) {
+                    if (mbar_test_wait(&pready[g], (np / G) & 1)) {
                         tc_fence_after();
                         const uint32_t sb = smem_u32(base + ls * C::LOAD_SLOT);
 #pragma unroll
