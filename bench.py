@@ -14,7 +14,7 @@ independent evaluator per GPU, no collective on the data path (weak scaling: 1,0
              The working set (285 MB of weights, ~1.2 GB of activations) is far larger than L2.
   e2e        the same metric through the reference-facing API, CudaNet.evaluate on host numpy arrays: each step
              copies the inputs into pinned staging and up, and the outputs down and out (wall clock).
-  roofline   the dominant product, qkv (the CTA-pair tcgen05 GEMM, one launch per layer, 28.7% of device time in
+  roofline   the dominant product, qkv (the CTA-pair tcgen05 GEMM, one launch per layer, 29.0% of device time in
              the ncu launch list, profiles/launches_bf16_b1024.md): its algorithmic FLOPs per launch / its mean launch
              time, from CUDA events around each step of an eager pass on the evaluator's stream
              (cudanet_profile), against the measured sustained bf16 peak. `traffic` is its DRAM bytes per launch
