@@ -121,9 +121,9 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
     static constexpr bool HEAVY = EPI == kEpiBiasGelu || EPI == kEpiGeluE4m3;   // GELU's erf per element
     static constexpr int OUT_BYTES = (EPI == kEpiResidual || EPI == kEpiF32) ? 4 : (EPI == kEpiGeluE4m3 ? 1 : 2);
     // one staging chunk: 128 rows x ROW_BYTES (64-byte rows for the GELU epilogues, whose four groups each take
-    // a narrow chunk at a time; 128-byte rows otherwise)
-    // the FP8 bias epilogue (qkv): half the mainloop time of a 16-bit tile to hide in, so four groups on
-    // narrower chunks (measured 2.5% faster on the FP8 qkv product, no faster on the 16-bit one)
+    // a narrow chunk at a time, and for the FP8 bias epilogue (qkv), which has half the mainloop time of a
+    // 16-bit tile to hide in: four groups on narrower chunks measured 2.7% faster there, no faster on the 16-bit
+    // product; 128-byte rows otherwise)
     static constexpr bool NARROW = EPI == kEpiBias && F8;
     static constexpr int ROW_BYTES = (HEAVY || NARROW) ? 64 : 128;
     static constexpr int CHUNK_COLS = ROW_BYTES / OUT_BYTES;
@@ -131,10 +131,10 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
     static constexpr uint32_t CHUNK_BYTES = 128 * ROW_BYTES;
     // Epilogue groups: 4 warps each, one per TMEM lane quarter, splitting a tile's chunks round-robin. Four
     // groups where the per-element work is heavy (GELU's erf: more warps to hide its latency and share its
-    // issue slots), two where the chunks are many; the residuals' bulk traffic wants deep prefetch (four
-    // staging buffers per CTA in flight)
-    // (the bf16 residual, 4 chunks a tile, measured faster with two groups of two buffers; the f32 residual,
-    // 8 chunks a tile, with one group of four)
+    // issue slots) and for the narrow FP8 bias chunks, two where the chunks are many. The bf16 residual's loads
+    // of X want deep prefetch: two groups of two staging buffers (four chunks of X in flight per CTA; with one
+    // buffer a group the refill would land in the buffer being stored). The f32 residual stages only acc + bias
+    // for its TMA reductions: two groups of one buffer (measured best of 1 x 2, 2 x 1, 2 x 2 and 4 x 1).
     static constexpr int EG = XLOAD ? (NC % 2 == 0 ? 2 : 1)
                               : REDUCE ? ((NC % MF_REDUCE_EG == 0) ? MF_REDUCE_EG : 1)
                                        : ((HEAVY || NARROW) && NC % 4 == 0) ? 4 : (NC % 2 == 0 ? 2 : 1);
@@ -473,11 +473,12 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
             constexpr int RB = C::ROW_BYTES;
             if constexpr (EPI == kEpiResidual16) {
                 // X (bf16) + v in f32, rounded once to bf16
-                uint4 xs[8];
+                constexpr int UNITS = RB / 16;
+                uint4 xs[UNITS];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) xs[j] = *reinterpret_cast<const uint4*>(buf + swz<RB>(row, j));
+                for (int j = 0; j < UNITS; ++j) xs[j] = *reinterpret_cast<const uint4*>(buf + swz<RB>(row, j));
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < UNITS; ++j) {
                     const float* w = v + 8 * j;
                     xs[j].x = pack2<__nv_bfloat16>(bf16_lo(xs[j].x) + w[0], bf16_hi(xs[j].x) + w[1]);
                     xs[j].y = pack2<__nv_bfloat16>(bf16_lo(xs[j].y) + w[2], bf16_hi(xs[j].y) + w[3]);
@@ -485,7 +486,7 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                     xs[j].w = pack2<__nv_bfloat16>(bf16_lo(xs[j].w) + w[6], bf16_hi(xs[j].w) + w[7]);
                 }
 #pragma unroll
-                for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(buf + swz<RB>(row, j)) = xs[j];
+                for (int j = 0; j < UNITS; ++j) *reinterpret_cast<uint4*>(buf + swz<RB>(row, j)) = xs[j];
             } else if constexpr (C::OUT_BYTES == 4) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
