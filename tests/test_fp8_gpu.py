@@ -157,6 +157,7 @@ def test_attention_f8(k, kernel, d, heads, B):
     if kernel != "default" and d // heads != 64:
         pytest.skip("the kernels chosen by name are the head-width-64 ones")
     rows = B * 65
+    torch.manual_seed(1000 * B + d)
     qkv = torch.randn(rows, 3 * d, device="cuda").to(torch.bfloat16)
     att = torch.full((rows, d), 0x7F, device="cuda", dtype=torch.uint8)
     mul = 100.0
@@ -167,10 +168,12 @@ def test_attention_f8(k, kernel, d, heads, B):
     torch.cuda.synchronize()
     dh = d // heads
     q, kk, v = qkv.float().view(B, 65, 3, heads, dh).permute(2, 0, 3, 1, 4).unbind(0)
-    o = torch.softmax(q @ kk.transpose(-1, -2) / math.sqrt(dh), -1) @ v
-    ref = o.transpose(1, 2).reshape(rows, d)
-    # P is rounded to bf16 before the second product (as in the 16-bit kernel), then one e4m3 rounding
-    assert_e4m3_close(att, ref * mul, slack=mul * (2e-3 + 2.0 ** -7 * ref.abs()))
+    p = torch.softmax(q @ kk.transpose(-1, -2) / math.sqrt(dh), -1)
+    ref = (p @ v).transpose(1, 2).reshape(rows, d)
+    pv_abs = (p @ v.abs()).transpose(1, 2).reshape(rows, d)
+    # P is rounded to bf16 before the second product (at most 2^-8 sum_j p_j |v_j| on an output), then one e4m3
+    # rounding
+    assert_e4m3_close(att, ref * mul, slack=mul * (2.0 ** -8 * pv_abs + 1e-4))
 
 
 # ------------------------------------------------------------------------------------------------ calibration
