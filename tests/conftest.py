@@ -45,3 +45,17 @@ def chesscore():
         pytest.skip("oracle/_ref/libchesscore.so not built and no reference checkout to build it from")
     from oracle import positions
     return positions
+
+
+@pytest.fixture(autouse=True)
+def _seeded(request):
+    """Every test draws its random inputs from a seed fixed by its own name, so a run is repeatable."""
+    import zlib
+    seed = zlib.crc32(request.node.nodeid.encode()) & 0x7FFFFFFF
+    np.random.seed(seed)
+    try:
+        import torch
+        torch.manual_seed(seed)
+    except ImportError:
+        pass
+    yield
