@@ -1,7 +1,7 @@
 """Generates the committed golden fixtures from the REFERENCE itself, in a container that has the reference
 checkout (it is not needed, and not present, where the tests and the bench run).
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref <reference checkout>]
 
 What it does:
   1. Builds the reference's own C++ chess core (make -C oracle) and uses it, through oracle/positions.py, for
