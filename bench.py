@@ -1,7 +1,7 @@
 """Throughput of MayFly's batched network evaluation on B200s: positions evaluated per second.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch 1024] [--precision bf16|f16|e4m3]
-                    [--impl reference]
+                    [--impl reference] [--no-fp8] [--no-strong] [--no-sweep] [--no-cpu]
 
 Workload (the metric's configuration): the 146M trunk (d 1024, 16 layers, 16 heads, FFN
 2048, 65 tokens, policy + qvalue heads and the search's reduction) with seed-1 random-init weights in bf16,
@@ -14,26 +14,32 @@ independent evaluator per GPU, no collective on the data path (weak scaling: 1,0
              The working set (285 MB of weights, ~1.2 GB of activations) is far larger than L2.
   e2e        the same metric through the reference-facing API, CudaNet.evaluate on host numpy arrays: each step
              copies the inputs into pinned staging and up, and the outputs down and out (wall clock).
-  roofline   the dominant product, qkv (the CTA-pair tcgen05 GEMM, one launch per layer, 29.0% of device time in
-             the ncu launch list, profiles/launches_bf16_b1024.md): its algorithmic FLOPs per launch / its mean launch
-             time, from CUDA events around each step of an eager pass on the evaluator's stream
-             (cudanet_profile), against the measured sustained bf16 peak. `traffic` is its DRAM bytes per launch
-             from the ncu capture (profiles/gemm_qkv_pair_*), scaled by B / 1,024. The whole trunk-GEMM family is
-             reported beside it (`gemm_family`).
-  cpu_baseline  the CPU fp32 restatement of the reference forward (oracle/, test infrastructure) on a bounded
-             sample on this host's cores.
+  parity     rank 0's e2e outputs at B = 1,024 (positions 0..1023) against the reference ChessNet's float32
+             outputs for the same positions (tests/golden/full_seed1_b1024.npz).
+  roofline   the dominant product, qkv (the CTA-pair tcgen05 GEMM, one launch per layer): its algorithmic FLOPs per
+             launch / its mean launch time, from CUDA events around each step of an eager pass on the evaluator's
+             stream (cudanet_profile), against the measured BURST bf16 peak (each launch is timed alone, for well
+             under a second). `traffic` is its DRAM bytes per launch from the ncu capture
+             (profiles/gemm_qkv_pair_*), scaled by B / 1,024. The whole trunk-GEMM family and the whole pass are
+             reported beside it against the same peak.
+  fp8        BASELINE config 4 (N = 1 only): the e4m3 evaluator and the bf16 evaluator on the same 4,096 positions
+             on this GPU, positions/s of each and their ratio, the e4m3 pass's parity against the float32
+             reference (and the reference model with e4m3-rounded weights, the control), and its dominant
+             product's roofline against twice the measured burst bf16 peak (no FP8 peak is measured).
+  strong     BASELINE config 5: 8,192 positions a step split evenly over the N ranks (device time, max over
+             ranks); at N > 1 rank 0 also times all 8,192 alone, and efficiency = value / (N x that).
+  latency_sweep  BASELINE config 3: p50 / p99 per call through CudaNet.evaluate at B = 1, 16, 64, 128, 256 and
+             the weight stream's GB/s (bytes of the weights / p50).
+  cpu_baseline  the CPU fp32 restatement of the reference forward (oracle/, test infrastructure) on this host's
+             cores: the median of 5 calls on 64 positions after 2 warm-up calls.
 
---total 8192 is BASELINE config 5 as strong scaling: 8,192 positions per step split over the ranks (each rank's
-share from position rank * 8192 / N). The default keeps 1,024 positions per GPU (weak scaling), the metric's
-configuration.
+--total 8192 runs the whole line as strong scaling (8,192 positions per step split over the ranks). The
+default keeps 1,024 positions per GPU (weak scaling), the metric's configuration.
 
---precision e4m3 --batch 4096 is BASELINE config 4: the same net with e4m3 weight matrices (per-output-channel
-scales) and e4m3 product inputs at static per-layer scales calibrated on 256 seed-1 positions outside every
-rank's batch (mayfly_chess_b200.quant, one bf16 pass on the GPU before the file is written); its roofline
-peak is twice the measured bf16 figure (no FP8 peak is measured).
+--precision e4m3 --batch 4096 runs the whole line on the e4m3 evaluator (config 4 alone).
 
 --impl reference times the reference's CPU path (the same fp32 restatement, all host threads) on the same
-metric, rank 0 only.
+metric and configuration (1,024 positions a step), rank 0 only.
 """
 import argparse
 import json
@@ -156,25 +162,62 @@ def load_peaks():
         return FALLBACK_PEAKS, "fallback"
 
 
-def cpu_sample(n_pos, threads):
-    """Positions/s of the CPU fp32 oracle (test infrastructure) on n_pos positions of the workload."""
+def cpu_model():
+    """The host CPU's model name (lscpu, else /proc/cpuinfo)."""
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for ln in out.splitlines():
+            if ln.startswith("Model name:"):
+                return ln.split(":", 1)[1].strip()
+    except (OSError, subprocess.SubprocessError):
+        pass
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_sample(n_pos, threads, calls=5, warmup=2):
+    """Positions/s of the CPU fp32 oracle (test infrastructure): the median of `calls` timed calls on n_pos
+    positions of the workload each (different positions per call), after `warmup` untimed calls."""
     import torch
     from mayfly_chess_b200 import weights as W
     from mayfly_chess_b200.inputs import PositionSet
     from oracle import chessnet_oracle as O
     torch.set_num_threads(threads)
     st = W.random_state(W.FULL, 1)
-    b = PositionSet(POSITIONS).batch(0, n_pos)
-    O.evaluate(st, W.FULL, PositionSet(POSITIONS).batch(n_pos, 2))      # warm-up
-    t0 = time.perf_counter()
-    O.evaluate(st, W.FULL, b)
-    return n_pos / (time.perf_counter() - t0)
+    ps = PositionSet(POSITIONS)
+    ts = []
+    for i in range(warmup + calls):
+        b = ps.batch(i * n_pos, n_pos)
+        t0 = time.perf_counter()
+        O.evaluate(st, W.FULL, b)
+        if i >= warmup:
+            ts.append(time.perf_counter() - t0)
+    return n_pos / statistics.median(ts), ts
+
+
+def workload_config(args, B, world, wide, precision):
+    """The `config` object of both arms' lines (the same workload, so the two lines compare)."""
+    return {"workload": ("config 4 (e4m3 layer products, calibrated static input scales)"
+                         if precision == "e4m3" else "config 2") +
+                        ": 146M trunk (d1024 L16 H16 FF2048, 65 tokens), seed-1 random-init "
+                        f"weights, {B} seed-1 random-playout positions per GPU per step",
+            "batch_per_gpu": B, "global_batch": B * world, "wide": wide, "precision": precision,
+            "parallelism": f"replicas x{world} (no collective)",
+            "l2": "working set larger than L2 (285 MB weights + ~1.2 GB activations per pass)"}
 
 
 def bench_reference(args):
     """--impl reference: the reference's CPU implementation of the path (its fp32 forward and _collect
     arithmetic, restated in oracle/chessnet_oracle.py; the reference's own code cannot travel here) timed with
-    every host thread; each step is a bounded sample of the workload's positions."""
+    every host thread on the same configuration as the product's line: each timed step evaluates the same
+    1,024 seed-1 positions (rank 0's batch) in one call. The warm-up steps run 32 positions each (they only
+    bring the thread pool and the allocator up to speed)."""
     from mayfly_chess_b200 import replicas
     rank, world, _ = replicas.rank_env()
     if rank != 0:
@@ -187,27 +230,80 @@ def bench_reference(args):
     torch.set_num_threads(cores)
     st = W.random_state(W.FULL, 1)
     ps = PositionSet(POSITIONS)
-    n = args.ref_sample
+    start, B = replicas.shard(0, world, len(ps), total=args.total or None, per_rank=None if args.total else args.batch)
+    b = ps.batch(start, B)
     for i in range(args.warmup):
-        O.evaluate(st, W.FULL, ps.batch(i * n, n))
+        O.evaluate(st, W.FULL, ps.batch(start + 32 * i, 32))
     times = []
     for i in range(args.steps):
-        b = ps.batch((args.warmup + i) * n, n)
         t0 = time.perf_counter()
         O.evaluate(st, W.FULL, b)
         times.append(time.perf_counter() - t0)
     total = sum(times)
-    v = n * args.steps / total
+    v = B * args.steps / total
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "positions/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "146M trunk fp32 on the host CPU (reference forward + _collect), seed-1 weights, "
-                               f"{n} seed-1 positions per step", "batch": n, "parallelism": "host threads"},
-        "cpu_baseline": {"value": v, "unit": "positions/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} steps of {n} positions (fp32 torch restatement of ChessNet + post)"},
+        "higher_is_better": True, "scaling": "strong" if args.total else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args, B, world, b["I"].shape[1], args.precision),
+        "cpu_baseline": {"value": v, "unit": "positions/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
+                         "sample": f"{args.steps} steps of the same {B} positions in one call each (fp32 torch "
+                                   "restatement of ChessNet + post, all host threads); warm-up steps of 32"},
         "e2e": {"value": v, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def b1024_reference():
+    """(batch of positions 0..1023, {pol, val, qv, pol_e4m3w, ...}) from tests/golden/full_seed1_b1024.npz: the
+    reference ChessNet's float32 outputs at the legal moves, re-padded to the batch."""
+    from mayfly_chess_b200.inputs import PositionSet
+    z = np.load(os.path.join(REPO, "tests", "golden", "full_seed1_b1024.npz"))
+    widths = z["widths"].astype(np.int64)
+    b = PositionSet(POSITIONS).batch(int(z["first_row"]), len(widths))
+    if not np.array_equal(b["widths"], widths):
+        raise SystemExit("full_seed1_b1024.npz does not match positions_seed1.npz")
+    ref = {}
+    for k in z.files:
+        if k.startswith(("pol", "qv")):
+            ref[k] = np.zeros(b["I"].shape, np.float32)
+            ref[k][b["M"]] = z[k]
+        elif k.startswith("val"):
+            ref[k] = z[k]
+    return b, ref
+
+
+def parity_summary(ref, got, widths):
+    """The parity metrics of tests/parity.py (the reference's metric set), the headline figures only."""
+    sys.path.insert(0, os.path.join(REPO, "tests"))
+    from parity import metrics
+    m = metrics(ref, got, widths)
+    keys = ("pol_max", "pol_mean", "prior_max", "prior_mean", "q_max", "val_max", "top1", "top1_clear", "top3",
+            "rows", "nonfinite", "pad_nonzero")
+    return {k: m[k] for k in keys}
+
+
+def device_pass_ms(net, b, steps, warmup):
+    """Mean device milliseconds of a pass over batch b through cudanet_evaluate_device (inputs in HBM), CUDA
+    events on the launching stream."""
+    import torch
+    B, wide = b["I"].shape
+    dev = {k: torch.from_numpy(np.ascontiguousarray(b[k])).cuda() for k in ("ids", "cast", "hm", "ep", "I")}
+    Md = torch.from_numpy(b["M"].astype(np.uint8)).cuda()
+    pol, val, qv = torch.empty(B, wide, device="cuda"), torch.empty(B, device="cuda"), torch.empty(B, wide,
+                                                                                                   device="cuda")
+    for _ in range(warmup):
+        net.evaluate_device(dev["ids"], dev["cast"], dev["hm"], dev["ep"], dev["I"], Md, pol, val, qv)
+    s = torch.cuda.current_stream()
+    net.check(s)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        net.evaluate_device(dev["ids"], dev["cast"], dev["hm"], dev["ep"], dev["I"], Md, pol, val, qv)
+    e1.record(s)
+    torch.cuda.synchronize()
+    net.check(s)
+    return e0.elapsed_time(e1) / steps
 
 
 def main():
@@ -220,10 +316,11 @@ def main():
                     help="strong scaling (config 5): this many positions per step over all ranks (overrides --batch)")
     ap.add_argument("--precision", default="bf16", choices=["bf16", "f16", "e4m3"])
     ap.add_argument("--impl", default="own", choices=["own", "reference"])
-    ap.add_argument("--ref-sample", type=int, default=16, help="positions per step of the reference arm")
-    ap.add_argument("--cpu-sample", type=int, default=32, help="positions of the cpu_baseline sample")
+    ap.add_argument("--cpu-sample", type=int, default=64, help="positions per call of the cpu_baseline sample")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-fp8", action="store_true", help="leave out the fp8 object (config 4)")
+    ap.add_argument("--no-strong", action="store_true", help="leave out the strong object (config 5)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -258,11 +355,21 @@ def main():
                                   per_rank=None if args.total else args.batch)
     except ValueError as e:
         raise SystemExit(str(e))
+    STRONG_TOTAL = 8192
+    do_strong = not args.no_strong and not args.total and args.precision != "e4m3" and STRONG_TOTAL % world == 0
+    do_fp8 = not args.no_fp8 and world == 1 and args.precision == "bf16"
+    FP8_B = 4096
+    # one evaluator serves every batch size this rank runs (a CUDA graph per size)
+    need = [B]
+    if do_strong:
+        need.append(STRONG_TOTAL if rank == 0 else STRONG_TOTAL // world)
+    if do_fp8:
+        need.append(FP8_B)
+    os.environ.setdefault("MAYFLY_CUDANET_MAX_BATCH", str(max(need + [1024])))
     arch = W.FULL
     st = W.random_state(arch, 1)
     tmp = tempfile.mkdtemp(prefix="mayfly_b200_")
     path = os.path.join(tmp, f"net_{args.precision}_{rank}.cnw")
-    os.environ.setdefault("MAYFLY_CUDANET_MAX_BATCH", str(max(B, 1024)))
     if args.precision == "e4m3":
         from mayfly_chess_b200 import quant
         amax = quant.calibrate(st, arch, ps.batch(CALIB_ROWS[0], CALIB_ROWS[1] - CALIB_ROWS[0]), device=local)
@@ -288,7 +395,8 @@ def main():
         step_dev()
     net.check(torch.cuda.current_stream())
     vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
-    clocks = Clocks(vis[local] if local < len(vis) else local)   # nvidia-smi counts physical devices
+    gpu_index = vis[local] if local < len(vis) else local   # nvidia-smi counts physical devices
+    clocks = Clocks(gpu_index)
     clocks.start()
     time.sleep(0.3)
     barrier()
@@ -318,6 +426,15 @@ def main():
     e2e = world * B * args.steps / e2e_s
     h2d = B * (64 * 8 + 8 + 8 + 16) + B * wide * 9
     d2h = 256 + 4 * B * (2 * wide + 1)
+    parity = None
+    if start == 0 and B == 1024:
+        rb, ref = b1024_reference()
+        tag = "_e4m3w" if args.precision == "e4m3" else ""
+        parity = {"against": "reference ChessNet float32 outputs, positions 0..1023 (tests/golden/full_seed1_b1024.npz)",
+                  **parity_summary((ref["pol"], ref["val"], ref["qv"]), (p_h, v_h, q_h), rb["widths"])}
+        if tag:
+            parity["vs_e4m3_weight_model"] = parity_summary((ref["pol" + tag], ref["val" + tag], ref["qv" + tag]),
+                                                            (p_h, v_h, q_h), rb["widths"])
 
     # ---------------------------------------------------------------- the key-fed path (encode on the GPU)
     keys, ep_sq, clock = keys_of_inputs(b)
@@ -364,21 +481,91 @@ def main():
                             "h2d_bytes_per_step": B * 96 + B * wide * 9, "d2h_bytes_per_step": d2h}}
 
     # ---------------------------------------------------------------- roofline of the dominant kernel
+    peaks, peak_kind = load_peaks()
+    burst = float(peaks.get("bf16_tflops"))
+    sustained = float(peaks.get("bf16_tflops_sustained", burst))
+
+    def roofline_of(prof, Bp, precision):
+        qkv_flop = 2.0 * Bp * arch.tokens * 3 * arch.d * arch.d
+        achieved = qkv_flop / (prof["qkv"] / arch.layers / 1000.0) / 1e12
+        traffic = QKV_TRAFFIC_PER_POS.get(precision)
+        peak = burst * (2.0 if precision == "e4m3" else 1.0)
+        eb = 1 if precision == "e4m3" else 2
+        return {"bound": "tensor", "kernel": "gemm_tc_pair_kernel, the qkv product (one per layer)",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": (f"2 x {peak_kind} bf16 burst (no measured FP8 peak)" if precision == "e4m3"
+                                else f"{peak_kind} bf16 burst (each launch timed alone)"),
+                "frac_of_sustained": achieved / (sustained * peak / burst),
+                "traffic": traffic * Bp if traffic is not None else None, "flop_per_launch": qkv_flop,
+                "algorithmic_bytes_per_launch": Bp * arch.tokens * arch.d * eb + 3 * arch.d * arch.d * eb
+                                                + Bp * arch.tokens * 3 * arch.d * 2,
+                "timing": "CUDA events around each step of an eager pass (cudanet_profile), mean of 3"}
+
     prof = net.profile(B, reps=3)
     fl_alg, fl_pos, gemm_fl_pos = flops_per_position()
-    qkv_flop = 2.0 * B * arch.tokens * 3 * arch.d * arch.d
-    achieved = qkv_flop / (prof["qkv"] / arch.layers / 1000.0) / 1e12
-    traffic = QKV_TRAFFIC_PER_POS.get(args.precision)
-    traffic = traffic * B if traffic is not None else None
+    roofline = roofline_of(prof, B, args.precision)
     trunk_gemm_ms = prof["qkv"] + prof["out"] + prof["ff1"] + prof["ff2"]
     launches = 4 * arch.layers
     family = gemm_fl_pos * B / (trunk_gemm_ms / 1000.0) / 1e12
-    peaks, peak_kind = load_peaks()
-    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
-    peak_source = f"{peak_kind} bf16 sustained"
-    if args.precision == "e4m3":
-        peak *= 2.0
-        peak_source = f"2 x {peak_kind} bf16 sustained (no measured FP8 peak)"
+    peak = roofline["peak"]
+
+    # ---------------------------------------------------------------- config 5: strong scaling over 8,192
+    strong = None
+    if do_strong:
+        sb = ps.batch(rank * (STRONG_TOTAL // world), STRONG_TOTAL // world)
+        barrier()
+        ms = max_over_ranks(device_pass_ms(net, sb, args.steps, 3))
+        strong = {"total_positions": STRONG_TOTAL, "per_rank": STRONG_TOTAL // world, "ms_per_step": ms,
+                  "value": STRONG_TOTAL / (ms / 1000.0), "unit": "positions/s",
+                  "timing": "device time of K passes over each rank's share, max over ranks"}
+        if world > 1:
+            one = None
+            if rank == 0:
+                one = device_pass_ms(net, ps.batch(0, STRONG_TOTAL), args.steps, 3)
+            barrier()
+            if rank == 0:
+                strong["single_gpu_ms_per_step"] = one
+                strong["single_gpu_value"] = STRONG_TOTAL / (one / 1000.0)
+                strong["efficiency"] = strong["value"] / (world * strong["single_gpu_value"])
+        else:
+            strong["efficiency"] = 1.0
+
+    # ---------------------------------------------------------------- config 4: e4m3 against bf16 at 4,096
+    fp8 = None
+    if do_fp8:
+        from mayfly_chess_b200 import quant
+        fb = ps.batch(0, FP8_B)
+        amax = quant.calibrate(st, arch, ps.batch(CALIB_ROWS[0], CALIB_ROWS[1] - CALIB_ROWS[0]), device=local)
+        p8 = os.path.join(tmp, "net_e4m3.cnw")
+        quant.write_e4m3(p8, st, arch, amax)
+        net8 = CudaNet(p8, device=local)
+        os.remove(p8)
+        device_pass_ms(net8, fb, 3, 3)
+        device_pass_ms(net, fb, 3, 3)
+        ck = Clocks(gpu_index)
+        ck.start()
+        time.sleep(0.3)
+        ms8 = device_pass_ms(net8, fb, args.steps, 3)
+        ms16 = device_pass_ms(net, fb, args.steps, 3)
+        ck_out = ck.stop()
+        rb, ref = b1024_reference()
+        got8 = net8.evaluate(rb["ids"], rb["cast"], rb["hm"], rb["ep"], rb["I"], rb["M"])
+        prof8 = net8.profile(FP8_B, reps=3)
+        net8.close()
+        fp8 = {"config": "config 4: e4m3 layer matrices (per-output-channel scales), e4m3 product inputs at static "
+                         "per-layer scales calibrated on 256 seed-1 positions outside the batch, bf16 residual "
+                         "stream, bf16 heads; the same 4,096 seed-1 positions through both evaluators",
+               "batch": FP8_B,
+               "e4m3": {"value": FP8_B / (ms8 / 1000.0), "ms_per_step": ms8},
+               "bf16": {"value": FP8_B / (ms16 / 1000.0), "ms_per_step": ms16},
+               "ratio": ms16 / ms8, "unit": "positions/s", "clocks": ck_out,
+               "parity_vs_fp32": parity_summary((ref["pol"], ref["val"], ref["qv"]), got8, rb["widths"]),
+               "parity_vs_e4m3_weight_model": parity_summary((ref["pol_e4m3w"], ref["val_e4m3w"], ref["qv_e4m3w"]),
+                                                             got8, rb["widths"]),
+               "e4m3_weight_model_vs_fp32": parity_summary((ref["pol"], ref["val"], ref["qv"]),
+                                                           (ref["pol_e4m3w"], ref["val_e4m3w"], ref["qv_e4m3w"]),
+                                                           rb["widths"]),
+               "roofline": roofline_of(prof8, FP8_B, "e4m3"), "profile_ms": prof8}
 
     # ---------------------------------------------------------------- latency (config 3) and CPU baseline
     sweep = {}
@@ -397,14 +584,17 @@ def main():
             # matrices (bf16, or e4m3 layer matrices + bf16 heads) + f32 vectors and scales, read once per call
             wbytes = (151265280 + 1302528) if args.precision == "e4m3" else (285483008 + 811008)
             sweep[str(Bs)] = {"p50_ms": 1000 * p50, "p99_ms": 1000 * p99, "positions_per_s": Bs / p50,
-                              "weight_stream_gbs": wbytes / p50 / 1e9}
+                              "weight_stream_gbs": wbytes / p50 / 1e9,
+                              "hbm_frac": wbytes / p50 / 1e9 / float(peaks.get("hbm_gbs", 6650.0))}
     cpu = None
     if rank == 0 and not args.no_cpu:
         cores = os.cpu_count() or 1
-        v = cpu_sample(args.cpu_sample, cores)
-        cpu = {"value": v, "unit": "positions/s", "cores": cores, "kind": "port",
-               "sample": f"{args.cpu_sample} seed-1 positions of the 146M net, fp32 torch restatement of the "
-                         "reference forward + post (oracle/), one call"}
+        v, ts = cpu_sample(args.cpu_sample, cores)
+        cpu = {"value": v, "unit": "positions/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
+               "sample": f"median of 5 calls on {args.cpu_sample} seed-1 positions each (after 2 warm-up calls) "
+                         "of the 146M net, fp32 torch restatement of the reference forward + post (oracle/), "
+                         "all host threads",
+               "call_seconds": ts}
 
     net.close()
     if world > 1:
@@ -416,22 +606,10 @@ def main():
         "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
         "scaling": "strong" if args.total else "weak",
         "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
-        "config": {"workload": ("config 4 (e4m3 layer products, calibrated static input scales)"
-                                if args.precision == "e4m3" else "config 2") +
-                               ": 146M trunk (d1024 L16 H16 FF2048, 65 tokens), seed-1 random-init "
-                               f"weights, {B} seed-1 random-playout positions per GPU per step",
-                   "batch_per_gpu": B, "global_batch": B * world, "wide": wide, "precision": args.precision,
-                   "parallelism": f"replicas x{world} (no collective)",
-                   "l2": "working set larger than L2 (285 MB weights + ~1.2 GB activations per pass)"},
+        "config": workload_config(args, B, world, wide, args.precision),
         "e2e": {"value": e2e, "unit": "positions/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": (1 + 7 * arch.layers - 1 + 2 + 1) * args.steps,
-        "roofline": {"bound": "tensor", "kernel": "gemm_tc_pair_kernel, the qkv product (one per layer)",
-                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                     "peak_source": peak_source, "traffic": traffic, "flop_per_launch": qkv_flop,
-                     "algorithmic_bytes_per_launch": B * arch.tokens * arch.d * (1 if args.precision == "e4m3" else 2)
-                                                     + 3 * arch.d * arch.d * (1 if args.precision == "e4m3" else 2)
-                                                     + B * arch.tokens * 3 * arch.d * 2,
-                     "timing": "CUDA events around each step of an eager pass (cudanet_profile), mean of 3"},
+        "roofline": roofline,
         "gemm_family": {"kernels": "qkv, out, ff1, ff2 of every layer (64 launches)", "achieved": family,
                         "unit": "TFLOP/s", "frac": family / peak, "flop_per_launch": gemm_fl_pos * B / launches},
         "pass": {"flop_per_position": fl_pos, "flop_per_position_algorithmic": fl_alg,
@@ -439,6 +617,9 @@ def main():
                  "frac_whole_pass": fl_pos * value / world / 1e12 / peak, "profile_ms": prof},
         "p50_latency_ms_bs64": sweep.get("64", {}).get("p50_ms"),
         "clocks": clk,
+        "parity": parity,
+        "fp8": fp8,
+        "strong": strong,
         "latency_sweep": sweep,
         "encoder": encoder,
         "cpu_baseline": cpu,

@@ -143,9 +143,12 @@ CUDANET_API int cudanet_k_gemm(int dtype, int epi, int bn, const void* A, const 
  * costs while other batches are in flight). No counterpart in the reference. It allocates nothing: its only
  * scratch, the kernel's 4-byte error word, lives in a static 256-byte device array that every GPU loading the
  * library holds until exit. The first call on a device looks up that array's address (cudaGetSymbolAddress);
- * make that first call before any stream capture. Calls share the array and it keeps the last call's word
- * (each call clears it first), so calls that overlap on the GPU race on it. Any M, N, K that cudanet_k_gemm
- * takes fits: the scratch need does not grow with the product. */
+ * make that first call before any stream capture. The address is kept for the life of the process, so do not
+ * call this on a device after resetting it (cudaDeviceReset). Like the other single-kernel entry points the
+ * call is synchronous: it reads the error word back and returns once the product has completed. Calls share
+ * the array and it keeps the last call's word (each call clears it first, in stream order), so calls that
+ * overlap on the GPU race on it. It takes and rejects exactly what cudanet_k_gemm does (ldc < N included).
+ * Any M, N, K that cudanet_k_gemm takes fits: the scratch need does not grow with the product. */
 CUDANET_API int cudanet_k_gemm_noalloc(int dtype, int epi, int bn, const void* A, const void* W, const float* bias,
                                        void* C, int M, int N, int K, int ldc, void* stream, char* err, int err_len);
 

@@ -1556,7 +1556,9 @@ constexpr size_t kNoAllocBytesPerCall = sizeof(uint32_t);
 static __device__ __align__(256) uint32_t g_noalloc_scratch[kNoAllocScratchBytes / sizeof(uint32_t)];
 
 // The array's device address on the current device, looked up once per device (host code must not hand the
-// symbol itself to a kernel: on the host it is only a stand-in for the device copy).
+// symbol itself to a kernel: on the host it is only a stand-in for the device copy). The address belongs to the
+// device's context as it was at the lookup: a process that resets a device (cudaDeviceReset) must not call the
+// entry point on that device afterwards.
 static uint32_t* noalloc_scratch(int dev)
 {
     static std::mutex mu;
@@ -1885,6 +1887,7 @@ CUDANET_API int cudanet_k_gemm_noalloc(int dtype, int epi, int bn, const void* A
         const long long ob = (epi == 2 || epi == 3) ? 4 : 2;
         if ((ldc * ob) % 16 || (N * ob) % 16)
             throw std::runtime_error("cudanet_k_gemm_noalloc: C's rows and row pitch must be multiples of 16 bytes");
+        if (ldc < N) throw std::runtime_error("cudanet_k_gemm_noalloc: ldc < N");
         const bool b16 = dtype == 1;
         const mf::MapType t = mf::type16(b16);
         const CUtensorMap ma = mf::operand_map(A, t, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128);

@@ -35,7 +35,12 @@ _load_lock = threading.Lock()
 
 
 def dll_path(dll=None):
-    return dll or os.environ.get("MAYFLY_CUDANET_DLL") or os.path.join(HERE, "libcudanet_b200.so")
+    """Which library file a handle binds: the explicit argument, then $MAYFLY_CUDANET_DLL, then the build in this
+    package's folder."""
+    for choice in (dll, os.environ.get("MAYFLY_CUDANET_DLL")):
+        if choice:
+            return choice
+    return os.path.join(HERE, "libcudanet_b200.so")
 
 
 def load(dll=None):
@@ -109,15 +114,27 @@ def load(dll=None):
         return lib
 
 
-def _arr(a, dtype, shape, name):
-    """A C-contiguous array of exactly this dtype and shape (copied only when it has to be)."""
-    a = np.asarray(a)
-    if dtype is np.uint8 and a.dtype == np.bool_:
-        a = a.view(np.uint8)
-    a = np.ascontiguousarray(a, dtype=dtype)
-    if a.shape != shape:
-        raise ValueError(f"{name}: shape {a.shape}, expected {shape}")
-    return a
+def _as_c(value, dtype, shape, name):
+    """`value` as a C-ordered array of `dtype` that the library can read in place; numpy makes a new array only
+    when the dtype or the memory order has to change (a bool mask is reinterpreted as bytes, never copied).
+    ValueError names the argument when its shape is not `shape`."""
+    arr = np.asarray(value)
+    if arr.dtype == np.bool_ and dtype is np.uint8:
+        arr = arr.view(np.uint8)
+    arr = np.require(np.atleast_1d(arr), dtype=dtype, requirements="C")
+    if arr.shape == shape:
+        return arr
+    raise ValueError(f"{name}: shape {arr.shape}, expected {shape}")
+
+
+# The six position inputs MCTS._prepare hands the evaluator: name, element type and shape for (B, wide).
+_POSITION_INPUTS = (("ids", np.int64, lambda B, w: (B, 64)), ("cast", np.float32, lambda B, w: (B, 4)),
+                    ("hm", np.int64, lambda B, w: (B,)), ("ep", np.int64, lambda B, w: (B,)),
+                    ("I", np.int64, lambda B, w: (B, w)), ("M", np.uint8, lambda B, w: (B, w)))
+# The key-fed form: transposition keys instead of the encoded board.
+_KEY_INPUTS = (("keys", np.uint64, lambda B, w: (B, 10)), ("ep_sq", np.int64, lambda B, w: (B,)),
+               ("clock", np.int64, lambda B, w: (B,)), ("I", np.int64, lambda B, w: (B, w)),
+               ("M", np.uint8, lambda B, w: (B, w)))
 
 
 def _p(a):
@@ -132,33 +149,36 @@ class CudaNet:
     """One evaluator handle: the weights on one B200, a CUDA graph per batch size. One call at a time."""
 
     def __init__(self, weights_path, device=0, dll=None):
-        self.path = os.path.abspath(weights_path)
-        self.device = int(device)
-        self.dll = dll_path(dll)
-        self._lib = load(self.dll)
-        self._lock = threading.Lock()
-        self._h = None
-        err = ctypes.create_string_buffer(ERR_LEN)
-        h = self._lib.cudanet_create(self.path.encode("utf-8"), self.device, err, ERR_LEN)
-        if not h:
-            raise RuntimeError(f"cudanet_create({self.path}): {_msg(err)}")
-        self._h = ctypes.c_void_p(h)
-        self.max_batch = int(self._lib.cudanet_max_batch(self._h))
+        self.path, self.device, self.dll = os.path.abspath(weights_path), int(device), dll_path(dll)
+        self._lib, self._lock, self._h = load(self.dll), threading.Lock(), None
+        reason = ctypes.create_string_buffer(ERR_LEN)
+        handle = self._lib.cudanet_create(self.path.encode("utf-8"), self.device, reason, ERR_LEN)
+        if handle:
+            self._h = ctypes.c_void_p(handle)
+            self.max_batch = int(self._lib.cudanet_max_batch(self._h))
+            return
+        raise RuntimeError(f"cudanet_create({self.path}): {_msg(reason)}")
 
-    def _inputs(self, ids, cast, hm, ep, I, M):
+    def _batch_dims(self, I):
+        """(B, wide) of a call, from the move-index matrix I, after the checks every entry point makes."""
         if self._h is None:
             raise RuntimeError("CudaNet is closed")
-        I = np.asarray(I)
-        if I.ndim != 2:
-            raise ValueError(f"I: shape {I.shape}, expected (B, wide)")
-        B, wide = I.shape
-        if not 1 <= B <= self.max_batch:
+        shape = np.shape(I)
+        if len(shape) != 2:
+            raise ValueError(f"I: shape {shape}, expected (B, wide)")
+        B, wide = shape
+        if B < 1 or B > self.max_batch:
             raise ValueError(f"batch {B}: cudanet takes 1 to {self.max_batch} (env MAYFLY_CUDANET_MAX_BATCH)")
         if wide < 1:
             raise ValueError("wide must be at least 1")
-        return (B, wide, _arr(ids, np.int64, (B, 64), "ids"), _arr(cast, np.float32, (B, 4), "cast"),
-                _arr(hm, np.int64, (B,), "hm"), _arr(ep, np.int64, (B,), "ep"), _arr(I, np.int64, (B, wide), "I"),
-                _arr(M, np.uint8, (B, wide), "M"))
+        return B, wide
+
+    def _convert(self, spec, values):
+        B, wide = self._batch_dims(values[-2])
+        return (B, wide) + tuple(_as_c(v, dt, shape(B, wide), name) for (name, dt, shape), v in zip(spec, values))
+
+    def _inputs(self, ids, cast, hm, ep, I, M):
+        return self._convert(_POSITION_INPUTS, (ids, cast, hm, ep, I, M))
 
     def evaluate(self, ids, cast, hm, ep, I, M):
         """One batch. Returns (pol (B, wide), val (B,), qv (B, wide)) float32."""
@@ -175,19 +195,7 @@ class CudaNet:
         return pol, val, qv
 
     def _key_inputs(self, keys, ep_sq, clock, I, M):
-        if self._h is None:
-            raise RuntimeError("CudaNet is closed")
-        I = np.asarray(I)
-        if I.ndim != 2:
-            raise ValueError(f"I: shape {I.shape}, expected (B, wide)")
-        B, wide = I.shape
-        if not 1 <= B <= self.max_batch:
-            raise ValueError(f"batch {B}: cudanet takes 1 to {self.max_batch} (env MAYFLY_CUDANET_MAX_BATCH)")
-        if wide < 1:
-            raise ValueError("wide must be at least 1")
-        return (B, wide, _arr(keys, np.uint64, (B, 10), "keys"), _arr(ep_sq, np.int64, (B,), "ep_sq"),
-                _arr(clock, np.int64, (B,), "clock"), _arr(I, np.int64, (B, wide), "I"),
-                _arr(M, np.uint8, (B, wide), "M"))
+        return self._convert(_KEY_INPUTS, (keys, ep_sq, clock, I, M))
 
     def evaluate_keys(self, keys, ep_sq, clock, I, M):
         """evaluate from transposition keys: keys (B, 10) uint64 = Board._transposition_key()[0:10] (turn and
@@ -305,14 +313,9 @@ class CudaNet:
         inputs (qkv, out, ff1, ff2) as float32 (layers, 4)."""
         if self._h is None:
             raise RuntimeError("CudaNet is closed")
-        ids = np.asarray(ids)
-        B = ids.shape[0]
-        if not 1 <= B <= self.max_batch:
-            raise ValueError(f"batch {B}: cudanet takes 1 to {self.max_batch} (env MAYFLY_CUDANET_MAX_BATCH)")
-        ids = _arr(ids, np.int64, (B, 64), "ids")
-        cast = _arr(cast, np.float32, (B, 4), "cast")
-        hm = _arr(hm, np.int64, (B,), "hm")
-        ep = _arr(ep, np.int64, (B,), "ep")
+        B, _ = self._batch_dims(np.empty((np.shape(ids)[0], 1)))
+        ids, cast, hm, ep = (_as_c(v, dt, shape(B, 1), name)
+                             for (name, dt, shape), v in zip(_POSITION_INPUTS[:4], (ids, cast, hm, ep)))
         out = np.zeros(4 * 256, np.float32)
         err = ctypes.create_string_buffer(ERR_LEN)
         with self._lock:

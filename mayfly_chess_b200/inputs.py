@@ -9,7 +9,7 @@ and legal_moves (:550-563) produce them:
     widths uint16 [N]      number of legal moves
     moves  uint16 [sum(widths)]  every position's legal moves' policy indices, python-chess order, concatenated
 make_batch turns a slice of it into what MCTS._prepare builds (mayfly/chess/mcts.py:1004-1058,
-cpp/export_ts.py:279-294 make_batches): ids int64 (B, 64), cast float32 (B, 4), hm int64 (B,), ep int64 (B,),
+cpp/export_ts.py:101-117 make_batches): ids int64 (B, 64), cast float32 (B, 4), hm int64 (B,), ep int64 (B,),
 I int64 (B, wide) and M bool (B, wide), padded to the batch's widest row.
 """
 import os

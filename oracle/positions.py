@@ -5,8 +5,8 @@ Only the fixture generator (tests/golden/make_golden.py) and the tests use this 
 imports it; the bench reads the committed position fixtures as data.
 
 What it restates:
-  * the inputs MCTS._prepare builds for a batch (mayfly/chess/mcts.py:1004-1058, cpp/export_ts.py:251-264
-    encode, cpp/export_ts.py:279-294 make_batches): ids (B, 64) int64, cast (B, 4) float32, hm (B,) int64,
+  * the inputs MCTS._prepare builds for a batch (mayfly/chess/mcts.py:1004-1058, cpp/export_ts.py:73-86
+    encode, cpp/export_ts.py:101-117 make_batches): ids (B, 64) int64, cast (B, 4) float32, hm (B,) int64,
     ep (B,) int64, and I (B, wide) int64 / M (B, wide) bool, the legal moves' policy indices padded to the
     batch's widest row, in python-chess's legal-move order (chess_core.cpp:550-563 legal_moves);
   * the encoder itself is chess_core.cpp:582-612 encode (mayfly_movegen.encode), which

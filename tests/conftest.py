@@ -40,7 +40,8 @@ def chesscore():
     missing (where there is no checkout the build fails and the tests that need it are skipped)."""
     lib = os.path.join(REPO, "oracle", "_ref", "libchesscore.so")
     if not os.path.exists(lib):
-        subprocess.run(["make", "-C", os.path.join(REPO, "oracle")], capture_output=True)
+        ref = os.environ.get("MAYFLY_REFERENCE") or os.path.join(os.path.dirname(REPO), "reference")
+        subprocess.run(["make", "-C", os.path.join(REPO, "oracle"), f"REF={ref}"], capture_output=True)
     if not os.path.exists(lib):
         pytest.skip("oracle/_ref/libchesscore.so not built and no reference checkout to build it from")
     from oracle import positions
@@ -59,3 +60,22 @@ def _seeded(request):
     except ImportError:
         pass
     yield
+
+
+def golden_b1024():
+    """(batch dict, reference outputs dict) of full_seed1_b1024.npz: positions_seed1.npz rows 0..1023 as one
+    padded batch, and the fixture's flattened legal-move outputs re-padded to it (0 on padding)."""
+    from mayfly_chess_b200.inputs import PositionSet
+    z = np.load(os.path.join(GOLDEN, "full_seed1_b1024.npz"))
+    ps = PositionSet(os.path.join(GOLDEN, "positions_seed1.npz"))
+    widths = z["widths"].astype(np.int64)
+    b = ps.batch(int(z["first_row"]), len(widths))
+    assert np.array_equal(b["widths"], widths), "the fixture's rows are not the position set's"
+    ref = {}
+    for k in z.files:
+        if k.startswith(("pol", "qv")):
+            ref[k] = np.zeros(b["I"].shape, np.float32)
+            ref[k][b["M"]] = z[k]
+        elif k.startswith("val"):
+            ref[k] = z[k]
+    return b, ref

@@ -1,7 +1,7 @@
 """Generates the committed golden fixtures from the REFERENCE itself, in a container that has the reference
 checkout (it is not needed, and not present, where the tests and the bench run).
 
-    python tests/golden/make_golden.py [--ref <reference checkout>]
+    python tests/golden/make_golden.py --ref <reference checkout>     (or MAYFLY_REFERENCE=<checkout> in the env)
 
 What it does:
   1. Builds the reference's own C++ chess core (make -C oracle) and uses it, through oracle/positions.py, for
@@ -38,8 +38,13 @@ Fixtures (all small .npz):
                               offset, size and SHA-256; the file itself (290 MB) is not kept
   meta.json                   fingerprints, state dict names and shapes, how each case was made
 
+  full_seed1_b1024.npz        the 146M net on the first 1,024 seed-1 positions (positions_seed1.npz rows
+                              0..1023, the bench's own batch): the reference outputs at the legal moves only,
+                              flattened row after row (pol, qv; val per row), with the bf16w and e4m3w controls
+
     python tests/golden/make_golden.py --only keys     regenerates keys_seed1.npz alone (seconds)
     python tests/golden/make_golden.py --only cnw      regenerates cnw_v1_seed1.json alone (a minute)
+    python tests/golden/make_golden.py --only b1024    regenerates full_seed1_b1024.npz alone (a few minutes)
 """
 import argparse
 import ast
@@ -264,17 +269,60 @@ def save_case(name, arch, seed, batch, outs, note, meta, full_rows=4, rounded=No
                            "B": int(batch["ids"].shape[0]), "wide": int(batch["I"].shape[1]), "note": note}
 
 
+def b1024_case(chess_net, export_ts, meta):
+    """full_seed1_b1024.npz: config 2 at its own batch. The reference forward runs in chunks of 256 rows (each
+    row's arithmetic does not depend on the others in the batch); the outputs are kept at the legal moves only,
+    concatenated row after row in positions_seed1.npz order, which the test re-pads from the position set."""
+    from mayfly_chess_b200.inputs import PositionSet
+    ps = PositionSet(os.path.join(HERE, "positions_seed1.npz"))
+    B, chunk = 1024, 256
+    st = W.random_state(W.FULL, 1)
+    states = {"": st, "_bf16w": W.dequantised_state(st, W.FULL, "bf16"),
+              "_e4m3w": W.dequantised_state(st, W.FULL, "e4m3")}
+    out = {}
+    t = time.time()
+    for tag, s in states.items():
+        pols, qvs, vals = [], [], []
+        for c in range(0, B, chunk):
+            b = ps.batch(c, chunk)
+            P_, V_, Q_, _, _ = reference_outputs(chess_net, export_ts, W.FULL, s, b)
+            for i, k in enumerate(b["widths"]):
+                pols.append(P_[i, :k])
+                qvs.append(Q_[i, :k])
+            vals.append(V_)
+        out["pol" + tag] = np.concatenate(pols).astype(np.float32)
+        out["qv" + tag] = np.concatenate(qvs).astype(np.float32)
+        out["val" + tag] = np.concatenate(vals).astype(np.float32)
+        print(f"full_seed1_b1024{tag}: {time.time() - t:.1f} s", flush=True)
+    widths = ps.widths[:B].astype(np.uint16)
+    np.savez_compressed(os.path.join(HERE, "full_seed1_b1024.npz"), widths=widths, first_row=np.int64(0), **out)
+    meta["cases"]["full_seed1_b1024"] = {
+        "arch": [W.FULL.d, W.FULL.layers, W.FULL.heads, W.FULL.ff], "seed": 1, "B": B,
+        "note": "positions_seed1.npz rows 0..1023 (the bench's batch); outputs at the legal moves only, "
+                "flattened; reference forward in chunks of 256 rows; bf16w / e4m3w controls"}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=["keys", "cnw"], help="regenerate one fixture alone")
+    ap.add_argument("--ref", default=os.environ.get("MAYFLY_REFERENCE"),
+                    help="the reference checkout (default: $MAYFLY_REFERENCE)")
+    ap.add_argument("--only", choices=["keys", "cnw", "b1024"], help="regenerate one fixture alone")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the reference checkout with --ref or MAYFLY_REFERENCE")
     subprocess.run(["make", "-C", os.path.join(REPO, "oracle"), f"REF={args.ref}"], check=True)
     from oracle import positions as P
 
     chess_net, export_ts = import_reference(args.ref)
     if args.only == "cnw":
         cnw_case(args.ref)
+        return
+    if args.only == "b1024":
+        with open(os.path.join(HERE, "meta.json")) as f:
+            meta = json.load(f)
+        b1024_case(chess_net, export_ts, meta)
+        with open(os.path.join(HERE, "meta.json"), "w") as f:
+            json.dump(meta, f, indent=1)
         return
     if args.only == "keys":
         with open(os.path.join(HERE, "meta.json")) as f:
@@ -326,6 +374,7 @@ def main():
     o, rd = run(W.FULL, st, fixed_batch)
     save_case("full_seed1_fixed", W.FULL, 1, fixed_batch, o, "fixed edge cases", meta, rounded=rd)
     print(f"146M reference forward: {time.time() - t:.1f} s")
+    b1024_case(chess_net, export_ts, meta)
     keys_case(args.ref, meta)
     cnw_case(args.ref)
     with open(os.path.join(HERE, "meta.json"), "w") as f:

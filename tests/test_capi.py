@@ -75,3 +75,31 @@ def test_python_wrapper_fails_loudly_without_library(tmp_path):
     from mayfly_chess_b200 import cudanet_py
     with pytest.raises(FileNotFoundError):
         cudanet_py.CudaNet(str(tmp_path / "x.cnw"), dll=str(tmp_path / "nolib.so"))
+
+
+def test_python_wrapper_checks_inputs_as_the_reference_does():
+    """CudaNet's argument checks (mayfly/chess/cudanet/cudanet_py.py:105-133): the same exceptions and messages,
+    run on a handle object that never reaches the library."""
+    import numpy as np
+    from mayfly_chess_b200 import cudanet_py
+    net = object.__new__(cudanet_py.CudaNet)
+    net._h, net.max_batch = None, 4
+    ok = dict(ids=np.zeros((2, 64), np.int64), cast=np.zeros((2, 4), np.float32), hm=np.zeros(2, np.int64),
+              ep=np.zeros(2, np.int64), I=np.zeros((2, 3), np.int64), M=np.ones((2, 3), bool))
+    with pytest.raises(RuntimeError, match="CudaNet is closed"):
+        net._inputs(**ok)
+    net._h = ctypes.c_void_p(1)
+    B, wide, ids, cast, hm, ep, I, M = net._inputs(**ok)
+    assert (B, wide) == (2, 3) and M.dtype == np.uint8 and ids.flags.c_contiguous
+    assert M.base is not None or M.ctypes.data == ok["M"].ctypes.data     # a bool mask is viewed, not copied
+    with pytest.raises(ValueError, match=r"I: shape \(6,\), expected \(B, wide\)"):
+        net._inputs(**{**ok, "I": np.zeros(6, np.int64)})
+    with pytest.raises(ValueError, match=r"batch 5: cudanet takes 1 to 4 \(env MAYFLY_CUDANET_MAX_BATCH\)"):
+        net._inputs(**{**ok, "I": np.zeros((5, 3), np.int64)})
+    with pytest.raises(ValueError, match="wide must be at least 1"):
+        net._inputs(**{**ok, "I": np.zeros((2, 0), np.int64)})
+    with pytest.raises(ValueError, match=r"cast: shape \(2, 3\), expected \(2, 4\)"):
+        net._inputs(**{**ok, "cast": np.zeros((2, 3), np.float32)})
+    # Fortran-ordered or other-typed inputs are converted, not refused
+    _, _, ids2, *_ = net._inputs(**{**ok, "ids": np.asfortranarray(np.ones((2, 64), np.int32))})
+    assert ids2.dtype == np.int64 and ids2.flags.c_contiguous and (ids2 == 1).all()

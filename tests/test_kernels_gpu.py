@@ -79,6 +79,27 @@ def test_gelu_epilogue_is_exact_erf_gelu(k):
     assert ((C.float() - ref).abs() <= ulp + 1e-7).all()
 
 
+def test_gelu_epilogue_bf16_every_value(k):
+    """The bf16 GELU epilogue (the one the bf16 passes run) on every bf16 value x with 2^-60 <= |x| < 10, and 0:
+    an identity W makes acc = x exactly; the bf16 output must be within one bf16 unit in the last place of the
+    exact-erf GELU (F.gelu in float64). Below 2^-60 GELU is x / 2 to far better than a bf16 ulp."""
+    K = 1024
+    bits = torch.arange(0, 1 << 16, dtype=torch.int32).to(torch.int16).view(torch.bfloat16).float()
+    keep = torch.isfinite(bits) & (bits.abs() < 10) & ((bits.abs() >= 2.0 ** -60) | (bits == 0))
+    vals = bits[keep]
+    n = (vals.numel() + K - 1) // K * K
+    x = torch.zeros(n).index_copy_(0, torch.arange(vals.numel()), vals).view(-1, K).cuda().to(torch.bfloat16)
+    W = torch.eye(K, device="cuda", dtype=torch.bfloat16)
+    b = torch.zeros(K, device="cuda")
+    C = torch.empty(x.shape[0], K, device="cuda", dtype=torch.bfloat16)
+    k.k_gemm(x, W, b, C, 1)
+    torch.cuda.synchronize()
+    ref = F.gelu(x.float().double()).float()
+    ulp = torch.clamp(ref.abs(), min=2.0 ** -126) * 2.0 ** -7
+    err = (C.float() - ref).abs()
+    assert (err <= ulp).all(), (err / ulp).max().item()
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_gemm_repeatable(k, dtype):
     A = torch.randn(4160, 1024, device="cuda").to(dtype)

@@ -28,6 +28,28 @@ def test_oracle_matches_reference(case, arch, seed):
         assert (pol[i, w:] == 0).all() and (qv[i, w:] == 0).all()
 
 
+def test_b1024_fixture_agrees_with_b64():
+    """The config-2 fixture (1,024 rows, reference forward in chunks of 256) gives its first 64 rows what the
+    64-row fixture gives them (the reference's float32 CPU arithmetic, batched differently), and the oracle gives
+    a slice of it within the oracle's bars."""
+    from conftest import golden_b1024
+    b, ref = golden_b1024()
+    b64, r64 = golden_case("full_seed1_b64")
+    w = b64["I"].shape[1]
+    for k in ("pol", "qv", "pol_bf16w", "qv_bf16w", "pol_e4m3w", "qv_e4m3w"):
+        assert np.abs(ref[k][:64, :w] - r64[k]).max() < TOL_LOGIT, k
+    for k in ("val", "val_bf16w", "val_e4m3w"):
+        assert np.abs(ref[k][:64] - r64[k]).max() < TOL_PROB, k
+    st = W.random_state(W.FULL, 1)
+    sl = {k: v[960:976] for k, v in b.items()}
+    sl["I"], sl["M"] = sl["I"][:, :int(sl["widths"].max())], sl["M"][:, :int(sl["widths"].max())]
+    pol, val, qv, _, _ = O.evaluate(st, W.FULL, sl)
+    w = sl["I"].shape[1]
+    assert np.abs(pol - ref["pol"][960:976, :w]).max() < TOL_LOGIT
+    assert np.abs(val - ref["val"][960:976]).max() < TOL_PROB
+    assert np.abs(qv - ref["qv"][960:976, :w]).max() < TOL_PROB
+
+
 def test_post_no_legal_move_gives_minus_one():
     pol = np.zeros((1, 4162), np.float32)
     import torch

@@ -72,3 +72,44 @@ def test_two_rank_gloo_reduction():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert got == [(0, 2, 0, 15.5, 0, 4096), (1, 2, 1, 15.5, 4096, 4096)]
+
+
+def _timed_step(rank, world):
+    """What a bench rank does around its timed region: a barrier, its own work, the max over ranks."""
+    import torch.distributed as dist
+    replicas.barrier(dist)
+    return replicas.max_over_ranks(1.0 + rank, dist)
+
+
+def test_supervised_run_healthy():
+    rep = replicas.run(_timed_step, 2, timeout_s=60, pg_timeout_s=20)
+    assert rep.ok, rep.describe()
+    assert rep.results == {0: 2.0, 1: 2.0}
+
+
+@pytest.mark.parametrize("kind,why", [("raise", "raised RuntimeError: injected fault on rank 1"),
+                                      ("exit", "exited with code 3"),
+                                      ("hang", "no result within 20 s (killed)")])
+def test_supervised_run_names_the_failed_rank(monkeypatch, kind, why):
+    """A rank that raises, exits or stops answering (injected on the host) is named in the report, and the call
+    returns within its deadline; the surviving rank's collective ends with an error (its process group times out
+    or sees the peer gone) instead of waiting for ever."""
+    import time
+    monkeypatch.setenv(replicas.FAULT_ENV, f"1:{kind}")
+    t0 = time.monotonic()
+    rep = replicas.run(_timed_step, 2, timeout_s=20, pg_timeout_s=5)
+    took = time.monotonic() - t0
+    assert not rep.ok
+    assert why in rep.failures.get(1, ""), rep.describe()
+    assert 0 in rep.failures or 0 in rep.results
+    assert took < 20 + 15, took
+    assert f"rank 1: {why}" in rep.describe()
+
+
+def test_inject_fault_spec():
+    replicas.inject_fault(0, {})                                   # nothing set
+    replicas.inject_fault(0, {replicas.FAULT_ENV: "1:raise"})      # another rank's fault
+    with pytest.raises(RuntimeError, match="injected fault on rank 2"):
+        replicas.inject_fault(2, {replicas.FAULT_ENV: "2:raise"})
+    with pytest.raises(ValueError, match="unknown fault kind"):
+        replicas.inject_fault(0, {replicas.FAULT_ENV: "0:melt"})

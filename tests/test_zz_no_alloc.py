@@ -1,10 +1,17 @@
-"""The allocation-free product (cudanet_k_gemm_noalloc) against the ordinary one (cudanet_k_gemm), through the
-C ABI on a B200. It exists for callers that cannot call cudaMalloc: a process whose GPU memory is reserved up
-front, or a search thread that must not stall in-flight batches on an allocation. Its scratch (the kernel's error
-word) is a static device array, so this checks that two calls in a row each give the ordinary entry point's
-result, with the word from the first call not leaking into the second. This file is named to run last."""
+"""The allocation-free product (cudanet_k_gemm_noalloc) through the C ABI on a B200.
+
+Who needs it: a caller that cannot call cudaMalloc, such as a process whose GPU memory is reserved in full up
+front, or a search thread that must not take the device-wide synchronisation an allocation costs while other
+batches are in flight. Its only scratch (the kernel's error word) is a static device array shared by every call,
+which each call clears in stream order before its launch. So two calls in a row must each give what the ordinary
+entry point (cudanet_k_gemm) gives, bit for bit, and what a float32 torch product gives within the GEMM tests'
+tolerance. This file is named to run last."""
+import ctypes
+import math
+
 import pytest
 import torch
+import torch.nn.functional as F
 
 pytestmark = pytest.mark.gpu
 
@@ -16,6 +23,16 @@ def k():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return cudanet_py
+
+
+def _ref(A, W, bias, epi, C0):
+    """The product in float32: acc + bias, then GELU (epi 1) or the residual add (epi 2)."""
+    y = A.float() @ W.float().t() + bias
+    if epi == 1:
+        y = F.gelu(y)
+    if epi == 2:
+        y = C0.float() + y
+    return y
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -36,6 +53,12 @@ def test_noalloc_matches_ordinary_two_calls(k, dtype, epi):
         # the same kernel on the same inputs: the results agree exactly (within 0, the tightest tolerance)
         assert torch.equal(got, want), f"call {call}: max diff {(got.float() - want.float()).abs().max().item()}"
         assert torch.isfinite(got.float()).all()
+        # and the float32 product within the GEMM tests' bar (test_kernels_gpu.test_gemm): 1e-3 absolute for the
+        # f32 accumulation order, plus one rounding of a 16-bit output
+        rel = 0.0 if epi in (2, 3) else (2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11)
+        ref = _ref(A, W, bias, epi, C0)
+        excess = ((got.float() - ref).abs() - (1e-3 + rel * ref.abs())).max().item()
+        assert math.isfinite(excess) and excess <= 0, f"call {call}: {excess}"
 
 
 def test_noalloc_rejects_what_the_ordinary_rejects(k):
@@ -45,9 +68,20 @@ def test_noalloc_rejects_what_the_ordinary_rejects(k):
     C = torch.empty(128, 256, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="noalloc"):
         k.k_gemm_noalloc(A, W, b, C, 0)
-    # and still works afterwards
+    # a row pitch shorter than a row (ldc < N), through the C function itself: both entry points refuse it on
+    # the host, before anything is queued
+    lib = k.load()
     A = torch.randn(128, 128, device="cuda").to(torch.bfloat16)
     W = torch.randn(256, 128, device="cuda").to(torch.bfloat16)
+    C = torch.zeros(128, 256, device="cuda", dtype=torch.bfloat16)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for fn in (lib.cudanet_k_gemm, lib.cudanet_k_gemm_noalloc):
+        err = ctypes.create_string_buffer(256)
+        rc = fn(1, 0, 0, A.data_ptr(), W.data_ptr(), b.data_ptr(), C.data_ptr(), 128, 256, 128, 128, stream, err, 256)
+        assert rc == -1 and b"ldc < N" in err.value
+    torch.cuda.synchronize()
+    assert (C == 0).all()
+    # and still works afterwards
     want, got = torch.empty_like(C), torch.empty_like(C)
     k.k_gemm(A, W, b, want, 0)
     k.k_gemm_noalloc(A, W, b, got, 0)
