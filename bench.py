@@ -101,7 +101,9 @@ def flops_per_position(d=1024, layers=16, heads=16, ff=2048, tokens=65, moves=41
 
 
 class Clocks:
-    """nvidia-smi samples of one GPU every 200 ms while running."""
+    """nvidia-smi samples of one GPU every 100 ms while running; stop(t0, t1) summarises the samples taken inside
+    the timed window [t0, t1] (time.monotonic), the nearest later samples when the window is shorter than the
+    sampling period."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -115,7 +117,7 @@ class Clocks:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                          "-lms", "100", "-i", str(self.index)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -124,9 +126,9 @@ class Clocks:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
 
-    def stop(self):
+    def stop(self, t0=None, t1=None):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -135,9 +137,15 @@ class Clocks:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.t.join(timeout=2)
+        lines = self.lines
+        if t0 is not None:
+            inside = [ln for t, ln in lines if t0 <= t <= t1]
+            lines = inside or [ln for t, ln in lines if t >= t0][:2]
+        else:
+            lines = [ln for _, ln in lines]
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in lines:
             p = [x.strip() for x in ln.split(",")]
             if len(p) < 8:
                 continue
@@ -150,7 +158,8 @@ class Clocks:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "window": "samples inside the timed region" if t0 is not None else "all samples"}
 
 
 def load_peaks():
@@ -306,6 +315,44 @@ def device_pass_ms(net, b, steps, warmup):
     return e0.elapsed_time(e1) / steps
 
 
+def bench_latency(args):
+    """--latency B: p50 / p99 of K calls of CudaNet.evaluate on B host positions after W warm-up calls, with
+    the weight stream's GB/s, on cuda:0 (the command the small-batch ncu captures run)."""
+    from mayfly_chess_b200 import weights as W
+    from mayfly_chess_b200.cudanet_py import CudaNet
+    from mayfly_chess_b200.inputs import PositionSet
+    B = args.latency
+    os.environ.setdefault("MAYFLY_CUDANET_MAX_BATCH", str(max(B, 1024)))
+    st = W.random_state(W.FULL, 1)
+    tmp = tempfile.mkdtemp(prefix="mayfly_b200_")
+    path = os.path.join(tmp, f"net_{args.precision}.cnw")
+    if args.precision == "e4m3":
+        from mayfly_chess_b200 import quant
+        amax = quant.calibrate(st, W.FULL, PositionSet(POSITIONS).batch(CALIB_ROWS[0], CALIB_ROWS[1] - CALIB_ROWS[0]))
+        quant.write_e4m3(path, st, W.FULL, amax)
+    else:
+        W.write_cnw(path, st, W.FULL, args.precision)
+    net = CudaNet(path)
+    os.remove(path)
+    b = PositionSet(POSITIONS).batch(0, B)
+    for _ in range(args.warmup):
+        net.evaluate(b["ids"], b["cast"], b["hm"], b["ep"], b["I"], b["M"])
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        net.evaluate(b["ids"], b["cast"], b["hm"], b["ep"], b["I"], b["M"])
+        ts.append(time.perf_counter() - t0)
+    prof = net.profile(B, reps=3)
+    net.close()
+    ts.sort()
+    p50, p99 = ts[len(ts) // 2], ts[min(len(ts) - 1, int(len(ts) * 0.99))]
+    wbytes = (151265280 + 1302528) if args.precision == "e4m3" else (285483008 + 811008)
+    print(json.dumps({"metric": f"p50 latency per call at batch {B} (config 3)", "value": 1000 * p50, "unit": "ms",
+                      "p99_ms": 1000 * p99, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+                      "dtype": args.precision, "batch": B, "weight_stream_gbs": wbytes / p50 / 1e9,
+                      "graph_pass_ms": prof["graph_pass"], "profile_ms": prof}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -321,11 +368,15 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-fp8", action="store_true", help="leave out the fp8 object (config 4)")
     ap.add_argument("--no-strong", action="store_true", help="leave out the strong object (config 5)")
+    ap.add_argument("--latency", type=int, default=0, metavar="B",
+                    help="config 3 at one batch size alone: K timed CudaNet.evaluate calls at batch B (one GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":
         return bench_reference(args)
+    if args.latency:
+        return bench_latency(args)
 
     import torch
     import torch.distributed as dist
@@ -402,12 +453,13 @@ def main():
     barrier()
     s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.monotonic()
     e0.record(s)
     for _ in range(args.steps):
         step_dev()
     e1.record(s)
     barrier()
-    clk = clocks.stop()
+    clk = clocks.stop(w0, time.monotonic())
     net.check(s)
     dev_ms = e0.elapsed_time(e1)
     dev_ms = max_over_ranks(dev_ms)
@@ -545,9 +597,10 @@ def main():
         ck = Clocks(gpu_index)
         ck.start()
         time.sleep(0.3)
+        w0 = time.monotonic()
         ms8 = device_pass_ms(net8, fb, args.steps, 3)
         ms16 = device_pass_ms(net, fb, args.steps, 3)
-        ck_out = ck.stop()
+        ck_out = ck.stop(w0, time.monotonic())
         rb, ref = b1024_reference()
         got8 = net8.evaluate(rb["ids"], rb["cast"], rb["hm"], rb["ep"], rb["I"], rb["M"])
         prof8 = net8.profile(FP8_B, reps=3)
