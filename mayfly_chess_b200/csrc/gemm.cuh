@@ -197,48 +197,53 @@ __device__ __forceinline__ float ex2_approx_f(float x)
 }
 
 // s * gelu(x) for the exact-erf GELU (F.gelu(approximate="none") = x * Phi(x), Phi the standard normal CDF).
-// With q = erfc(|x| / sqrt(2)) / 2, x * Phi(x) = relu(x) - |x| q for either sign of x, and q comes from
-// Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26 (|error of erfc| <= 1.5e-7):
-//   erfc(z) = (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),  t = 1 / (1 + p z),  z >= 0.
-// The reciprocal and 2^x run on the special-function unit (rcp.approx, ex2.approx: relative errors near
-// 2^-23), everything else two lanes at a time. No cancellation anywhere (the negative tail is -|x| q
-// directly), so the result is good to a few f32 ulps where |gelu| is not tiny, far below the 16-bit or e4m3
-// rounding that follows.
+// With a = |x| and q(a) = Phi(-a) = erfc(a / sqrt(2)) / 2, x * Phi(x) = relu(x) - a q(a) for either sign of x
+// (no cancellation: the negative side is -a q directly). log2 q(a) is smooth on [0, 10], so
+// q(a) = 2^P(u), u = a / 5 - 1, with P the degree-8 polynomial csrc/gelu_poly.py fits to log2 Phi(-a) (least
+// squares on Chebyshev nodes, relative error of q below 2.5e-5 over [0, 10] in f32 arithmetic); a is clamped to
+// 10, where q = 7.6e-24 (GELU is then x, or below 1e-21 in magnitude). One 2^x on the special-function unit per
+// value and no division; the polynomial runs two lanes per instruction (f32x2). The output scale s (e4m3
+// outputs) rides in the constant term: s q = 2^(P + log2 s), and s relu(x) = relu(s x) for s > 0.
 struct GeluK {
-    uint64_t c, p, one, a5, a4, a3, a2, a1, nl2e, s;
+    uint64_t c0, c1, c2, c3, c4, c5, c6, c7, c8, mu, m1, s;
     __device__ __forceinline__ explicit GeluK(float scale)
     {
-        const float h = -0.5f * scale;   // the polynomial carries -s / 2: h t P(t) e = -s q
-        c = pk2(0.70710678118654752440f, 0.70710678118654752440f);
-        p = pk2(0.3275911f, 0.3275911f);
-        one = pk2(1.0f, 1.0f);
-        a5 = pk2(1.061405429f * h, 1.061405429f * h);
-        a4 = pk2(-1.453152027f * h, -1.453152027f * h);
-        a3 = pk2(1.421413741f * h, 1.421413741f * h);
-        a2 = pk2(-0.284496736f * h, -0.284496736f * h);
-        a1 = pk2(0.254829592f * h, 0.254829592f * h);
-        nl2e = pk2(-1.4426950408889634f, -1.4426950408889634f);
+        const float l2s = scale == 1.0f ? 0.0f : log2f(scale);
+        c0 = pk2(-2.173420143e+01f + l2s, -2.173420143e+01f + l2s);
+        c1 = pk2(-3.741247559e+01f, -3.741247559e+01f);
+        c2 = pk2(-1.744393730e+01f, -1.744393730e+01f);
+        c3 = pk2(-3.288443387e-01f, -3.288443387e-01f);
+        c4 = pk2(1.906916946e-01f, 1.906916946e-01f);
+        c5 = pk2(-9.975451976e-02f, -9.975451976e-02f);
+        c6 = pk2(6.548856944e-02f, 6.548856944e-02f);
+        c7 = pk2(-5.716544390e-02f, -5.716544390e-02f);
+        c8 = pk2(2.371014841e-02f, 2.371014841e-02f);
+        mu = pk2(-0.2f, -0.2f);      // u = (-a) * (-1/5) - 1
+        m1 = pk2(-1.0f, -1.0f);
         s = pk2(scale, scale);
     }
 };
 
-// s * gelu of both lanes of x2
+// s * gelu of both lanes of x2 (SCALED: s != 1)
+template <bool SCALED = false>
 __device__ __forceinline__ float2 gelu_pair(uint64_t x2, const GeluK& K)
 {
     const float2 x = upk2(x2);
-    const uint64_t ax = pk2(fabsf(x.x), fabsf(x.y));
-    const uint64_t az = mul2(ax, K.c);                                   // |x| / sqrt(2)
-    const float2 den = upk2(fma2(K.p, az, K.one));
-    const uint64_t t = pk2(rcp_approx(den.x), rcp_approx(den.y));
-    uint64_t h = fma2(t, K.a5, K.a4);
-    h = fma2(t, h, K.a3);
-    h = fma2(t, h, K.a2);
-    h = fma2(t, h, K.a1);
-    h = mul2(t, h);                                                      // -s/2 t P(t)
-    const float2 arg = upk2(mul2(az, mul2(az, K.nl2e)));                 // -z^2 log2(e)
-    const uint64_t nq = mul2(h, pk2(ex2_approx_f(arg.x), ex2_approx_f(arg.y)));   // -s q
-    const float2 xs = upk2(mul2(x2, K.s));
-    return upk2(fma2(ax, nq, pk2(fmaxf(xs.x, 0.f), fmaxf(xs.y, 0.f))));  // s relu(x) - s |x| q
+    const uint64_t na = pk2(fmaxf(-fabsf(x.x), -10.0f), fmaxf(-fabsf(x.y), -10.0f));   // -a, a clamped to 10
+    const uint64_t u = fma2(na, K.mu, K.m1);
+    uint64_t p = fma2(u, K.c8, K.c7);
+    p = fma2(u, p, K.c6);
+    p = fma2(u, p, K.c5);
+    p = fma2(u, p, K.c4);
+    p = fma2(u, p, K.c3);
+    p = fma2(u, p, K.c2);
+    p = fma2(u, p, K.c1);
+    p = fma2(u, p, K.c0);                                                 // log2(s q)
+    const float2 lp = upk2(p);
+    const uint64_t sq = pk2(ex2_approx_f(lp.x), ex2_approx_f(lp.y));      // s q
+    float2 xs = x;
+    if constexpr (SCALED) xs = upk2(mul2(x2, K.s));
+    return upk2(fma2(na, sq, pk2(fmaxf(xs.x, 0.f), fmaxf(xs.y, 0.f))));  // s relu(x) - s a q
 }
 
 template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -450,8 +455,8 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                     const GeluK K(ep.out_scale_inv);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const float2 g0 = gelu_pair(pk2(v[4 * i], v[4 * i + 1]), K);
-                        const float2 g1 = gelu_pair(pk2(v[4 * i + 2], v[4 * i + 3]), K);
+                        const float2 g0 = gelu_pair<true>(pk2(v[4 * i], v[4 * i + 1]), K);
+                        const float2 g1 = gelu_pair<true>(pk2(v[4 * i + 2], v[4 * i + 3]), K);
                         q[8 * p + i] = pack_e4m3x4(g0.x, g0.y, g1.x, g1.y);
                     }
                 } else if constexpr (EPI == kEpiBias) {

@@ -88,10 +88,9 @@ def exact_gelu(x):
 
 def test_gelu_epilogue_bf16_every_value(k):
     """The bf16 GELU epilogue (the one the bf16 passes run) on every bf16 value x with 2^-60 <= |x| < 10, and 0:
-    an identity W makes acc = x exactly. For x >= -6 the bf16 output must be within one bf16 unit in the last
-    place of the exact-erf GELU (exact_gelu, float64); below -6, where |GELU| < 6e-9, Abramowitz & Stegun 7.1.26's
-    error in erfc is a few percent of a value that small (its published bound is absolute, 1.5e-7 on erfc), so
-    there the absolute error must stay within 1e-10. Below 2^-60 GELU is x / 2 to far better than a bf16 ulp."""
+    an identity W makes acc = x exactly, and the bf16 output must be within one bf16 unit in the last place of the
+    exact-erf GELU (exact_gelu, float64) everywhere, the far negative tail included (|GELU| ~ 1e-22 at -10).
+    Below 2^-60 GELU is x / 2 to far better than a bf16 ulp."""
     K = 1024
     bits = torch.arange(0, 1 << 16, dtype=torch.int32).to(torch.int16).view(torch.bfloat16).float()
     keep = torch.isfinite(bits) & (bits.abs() < 10) & ((bits.abs() >= 2.0 ** -60) | (bits == 0))
@@ -106,9 +105,7 @@ def test_gelu_epilogue_bf16_every_value(k):
     ref = exact_gelu(x).float()
     ulp = torch.clamp(ref.abs(), min=2.0 ** -126) * 2.0 ** -7
     err = (C.float() - ref).abs()
-    body = x.float() >= -6
-    assert (err[body] <= ulp[body]).all(), (err / ulp)[body].max().item()
-    assert (err[~body] <= 1e-10).all(), err[~body].max().item()
+    assert (err <= ulp).all(), (err / ulp).max().item()
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
