@@ -183,8 +183,8 @@ CUDANET_API int cudanet_k_layernorm(int dtype, const float* x, const float* g, c
 
 /* The FP8 pieces (no counterpart in the reference). A[M, K] and W[N, K] are e4m3 bytes, K a multiple of 128;
  * v = acc * colscale[n] + bias[n] with epi 0: C bf16 = v; 2: C f32 += v; 3: C f32 = v; 4: C e4m3 =
- * gelu(v) * out_scale_inv (round to nearest even, saturating at +-448); 5: C bf16 = bf16(C + v). bn as for
- * cudanet_k_gemm. */
+ * gelu(v) * out_scale_inv (round to nearest even, saturating at +-448); 5: C bf16 = bf16(C + bf16(v)) (v rounded
+ * to bf16, then added into C by a bf16 reduction in memory). bn as for cudanet_k_gemm. */
 CUDANET_API int cudanet_k_gemm_f8(int epi, int bn, const void* A, const void* W, const float* colscale,
                                   const float* bias, float out_scale_inv, void* C, int M, int N, int K, int ldc,
                                   void* stream, char* err, int err_len);

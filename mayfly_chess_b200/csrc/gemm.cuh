@@ -12,7 +12,7 @@
 //   kEpiF32       C (f32)   = acc + bias                             heads
 // and for the FP8 path (no reference counterpart; acc scaled per column first):
 //   kEpiGeluE4m3  C (e4m3)  = e4m3(gelu(acc + bias) / scale)         ff1, writing ff2's input
-//   kEpiResidual16 X (bf16) = X + (acc + bias), in place             out and ff2 on a bf16 residual stream
+//   kEpiResidual16 X (bf16) = bf16(X + bf16(acc + bias)), in place   out and ff2 on a bf16 residual stream
 //
 // Two kernels, both persistent over output tiles with one CTA per SM:
 //   gemm_tc_kernel       one CTA per 128 x BN tile (BN 64, 128 or 256): tcgen05.mma.cta_group::1, M=128.
@@ -28,12 +28,11 @@
 //               tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31; the groups split a tile's
 //               column chunks), bias / GELU / residual, then the row goes into a 128-row staging chunk in shared
 //               memory (128-byte rows with the 128-byte swizzle, or 64-byte rows with the 64-byte swizzle for the
-//               4-group GELU epilogues) and one thread stores the chunk with a TMA tensor store (coalesced,
-//               asynchronous). The f32 residual stages acc + bias alone and adds it into X with a TMA
-//               reduction (cp.reduce.async.bulk.tensor .add, done at L2): X is never read into the SM, and the
-//               shared-memory traffic per tile halves against a read-modify-write through the staging chunk.
-//               The bf16 residual (X + v rounded once) TMA-loads the chunk of X into the staging buffer, several
-//               chunks ahead (also across tiles), and adds in registers.
+//               4-group epilogues) and one thread stores the chunk with a TMA tensor store (coalesced,
+//               asynchronous). The residuals stage v = acc + bias alone (f32, or rounded to bf16 for the bf16
+//               stream) and add it into X with a TMA reduction (cp.reduce.async.bulk.tensor .add, done at L2, in
+//               X's type: f32, or bf16 rounded to nearest): X is never read into the SM, and the shared-memory
+//               traffic per tile halves against a read-modify-write through the staging chunk.
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1. Tiles run M-block-major (all
 // N blocks of an M block back to back), so an A block is read from HBM once and the weights stay in L2.
 // Out-of-range rows and columns (M and N tails) are zero-filled by TMA loads and clipped by TMA stores.
@@ -50,10 +49,6 @@
 
 #include "ptx.cuh"
 
-// Staging buffers per CTA for the bf16 residual epilogue (each 16 KB; what they take from the operand ring).
-#ifndef MF_RESID_BUFFERS
-#define MF_RESID_BUFFERS 4
-#endif
 // Epilogue groups and staging buffers per group of the f32 residual (added into X by TMA reductions).
 #ifndef MF_REDUCE_EG
 #define MF_REDUCE_EG 2
@@ -112,34 +107,29 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
     static constexpr int BK = F8 ? 128 : 64;            // elements of K per stage: one 128-byte swizzle row
     static constexpr int KSTEPS = 4;                    // MMA instructions per stage (K = 16 or 32 each, 32 bytes)
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;   // rows of W per CTA per stage
-    static constexpr bool RESID = EPI == kEpiResidual || EPI == kEpiResidual16;
-    // the bf16 residual reads X back into the staging chunk (X + v is rounded once); the f32 residual is added
-    // into X by a TMA reduction at L2 (the same f32 add), so it neither reads X nor stages it
-    static constexpr bool XLOAD = EPI == kEpiResidual16;
-    static constexpr bool REDUCE = EPI == kEpiResidual;
+    // the residuals are added into X by a TMA reduction at L2 (f32 adds for the f32 stream, bf16 adds of the
+    // bf16-rounded v for the bf16 stream), so X is neither read into the SM nor staged
+    static constexpr bool REDUCE = EPI == kEpiResidual || EPI == kEpiResidual16;
     static constexpr bool IS_F8 = F8;
     static constexpr bool HEAVY = EPI == kEpiBiasGelu || EPI == kEpiGeluE4m3;   // GELU's erf per element
     static constexpr int OUT_BYTES = (EPI == kEpiResidual || EPI == kEpiF32) ? 4 : (EPI == kEpiGeluE4m3 ? 1 : 2);
     // one staging chunk: 128 rows x ROW_BYTES (64-byte rows for the GELU epilogues, whose four groups each take
-    // a narrow chunk at a time, and for the FP8 bias epilogue (qkv), which has half the mainloop time of a
-    // 16-bit tile to hide in: four groups on narrower chunks measured 2.7% faster there, no faster on the 16-bit
-    // product; 128-byte rows otherwise)
-    static constexpr bool NARROW = EPI == kEpiBias && F8;
+    // a narrow chunk at a time, and for the FP8 bias and bf16-residual epilogues, which have half the mainloop
+    // time of a 16-bit tile to hide in: four groups on narrower chunks measured 2.7% faster on the FP8 qkv
+    // product, no faster on the 16-bit one; 128-byte rows otherwise)
+    static constexpr bool NARROW = (EPI == kEpiBias && F8) || EPI == kEpiResidual16;
     static constexpr int ROW_BYTES = (HEAVY || NARROW) ? 64 : 128;
     static constexpr int CHUNK_COLS = ROW_BYTES / OUT_BYTES;
     static constexpr int NC = BN / CHUNK_COLS;           // staging chunks per tile
     static constexpr uint32_t CHUNK_BYTES = 128 * ROW_BYTES;
     // Epilogue groups: 4 warps each, one per TMEM lane quarter, splitting a tile's chunks round-robin. Four
     // groups where the per-element work is heavy (GELU's erf: more warps to hide its latency and share its
-    // issue slots) and for the narrow FP8 bias chunks, two where the chunks are many. The bf16 residual's loads
-    // of X want deep prefetch: two groups of two staging buffers (four chunks of X in flight per CTA; with one
-    // buffer a group the refill would land in the buffer being stored). The f32 residual stages only acc + bias
-    // for its TMA reductions: two groups of one buffer (measured best of 1 x 2, 2 x 1, 2 x 2 and 4 x 1).
-    static constexpr int EG = XLOAD ? (NC % 2 == 0 ? 2 : 1)
-                              : REDUCE ? ((NC % MF_REDUCE_EG == 0) ? MF_REDUCE_EG : 1)
-                                       : ((HEAVY || NARROW) && NC % 4 == 0) ? 4 : (NC % 2 == 0 ? 2 : 1);
-    static constexpr int NBUF = XLOAD ? MF_RESID_BUFFERS / EG
-                                      : REDUCE ? MF_REDUCE_NBUF : (EG >= 2 ? 1 : 2);   // staging buffers per group
+    // issue slots) and for the narrow chunks, two where the chunks are many. The f32 residual stages only
+    // acc + bias for its TMA reductions: two groups of one buffer (measured best of 1 x 2, 2 x 1, 2 x 2 and
+    // 4 x 1).
+    static constexpr int EG = EPI == kEpiResidual ? ((NC % MF_REDUCE_EG == 0) ? MF_REDUCE_EG : 1)
+                              : ((HEAVY || NARROW) && NC % 4 == 0) ? 4 : (NC % 2 == 0 ? 2 : 1);
+    static constexpr int NBUF = EPI == kEpiResidual ? MF_REDUCE_NBUF : (EG >= 2 ? 1 : 2);   // staging buffers a group
     static constexpr uint32_t A_BYTES = BM * 128;
     static constexpr uint32_t B_BYTES = B_ROWS * 128;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -150,7 +140,6 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
         1024 + (size_t)STAGES * STAGE_BYTES + (size_t)EG * NBUF * CHUNK_BYTES + 256;
     static constexpr int THREADS = 64 + 128 * EG;
     static_assert(STAGES >= 3, "pipeline too shallow");
-    static_assert(!XLOAD || NBUF >= 2, "the residual loads refill a buffer NBUF - 1 chunks ahead: two at least");
     static_assert(SMEM <= 232448, "shared memory over the per-block limit");
     static_assert(BN % CHUNK_COLS == 0 && NC >= 1, "tile width must hold whole staging chunks");
     static_assert(!PAIR || BN == 256, "the pair kernel covers 256 columns");
@@ -327,7 +316,7 @@ __device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u 
 // The shared-memory carve-up common to both kernels.
 template <typename C> struct SmemLayout {
     uint8_t *sA, *sB, *sC;
-    uint64_t *full, *empty, *tfull, *tempty, *mma_done, *xfull;
+    uint64_t *full, *empty, *tfull, *tempty, *mma_done;
     uint32_t* tmem_slot;
     volatile uint32_t* epi_ok;   // per epilogue group: the leader's broadcast flag
 
@@ -342,8 +331,7 @@ template <typename C> struct SmemLayout {
         tfull = empty + C::STAGES;
         tempty = tfull + 2;
         mma_done = tempty + 2;
-        xfull = mma_done + 1;                                              // EG x NBUF (residual loads)
-        tmem_slot = reinterpret_cast<uint32_t*>(xfull + C::EG * C::NBUF);
+        tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
         epi_ok = tmem_slot + 1;
     }
 };
@@ -369,25 +357,7 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
     const uint32_t bar_id = 1 + grp;
     constexpr int CPG = C::NC / C::EG;                    // chunks per tile for one group
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-    const int total_chunks = my_tiles * CPG;              // this group's chunks over all its tiles
     uint8_t* gbuf = L.sC + grp * C::NBUF * C::CHUNK_BYTES;
-    uint64_t* xfull = L.xfull + grp * C::NBUF;            // this group's residual-load barriers
-
-    // this group's chunk h: tile h / CPG of this CTA, chunk grp + (h % CPG) * EG of it
-    auto chunk_xy = [&](int h, int& x, int& y) {
-        x = origin_col(h / CPG) + (grp + (h % CPG) * C::EG) * C::CHUNK_COLS;
-        y = origin_row(h / CPG);
-    };
-    int loads = 0;    // residual chunks whose load the leader issued
-    if constexpr (C::XLOAD) {
-        if (leader)
-            for (; loads < C::NBUF && loads < total_chunks; ++loads) {
-                int x, y;
-                chunk_xy(loads, x, y);
-                mbar_arrive_expect_tx(&xfull[loads], C::CHUNK_BYTES);
-                tma_load_2d(gbuf + loads * C::CHUNK_BYTES, tmC, &xfull[loads], x, y);
-            }
-    }
 
     // the bias slice of the next tile is pulled into L1 a tile ahead (8 x 128-byte lines for 256 columns), so
     // the epilogue's bias reads do not wait on L2 (and the column scales, for FP8 products)
@@ -405,9 +375,8 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
 
     int acc = 0;
     uint32_t acc_phase = 0;
-    bool ok = true;
     int g = 0;        // this group's chunks done
-    for (int it = 0; it < my_tiles && ok; ++it) {
+    for (int it = 0; it < my_tiles; ++it) {
         const int row0 = origin_row(it), colb = origin_col(it);
         prefetch_bias(it + 1);
         if (leader) L.epi_ok[grp] = mbar_wait(&L.tfull[acc], acc_phase, err, kErrTmemFull) ? 1u : 0u;
@@ -420,12 +389,11 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
             const int b = g % C::NBUF;
             uint8_t* buf = gbuf + b * C::CHUNK_BYTES;
             const int col0 = colb + c * C::CHUNK_COLS;
-            // this chunk's row in registers, 32 accumulator columns at a time: f32 values (f32 outputs and the
-            // residuals, which add them to X once its chunk has landed) or the row's output bytes already
-            // packed (16-bit and e4m3 outputs)
+            // this chunk's row in registers, 32 accumulator columns at a time: f32 values (f32 outputs, 32 columns
+            // a chunk) or the row's output bytes already packed (16-bit and e4m3 outputs)
             constexpr int LOADS = C::CHUNK_COLS / 32;
             constexpr int QW = C::ROW_BYTES / 4;
-            float v[C::RESID ? C::CHUNK_COLS : 32];
+            float v[32];
             uint32_t q[QW];
 #pragma unroll
             for (int p = 0; p < LOADS; ++p) {
@@ -438,8 +406,7 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                     __syncwarp();
                     if (lane == 0) release(acc);
                 }
-                constexpr int off0 = 0;
-                const int off = C::RESID ? 32 * p : off0;
+                constexpr int off = 0;
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[off + i] = __uint_as_float(r[i]);
                 if constexpr (C::IS_F8) scale_bias32(v, off, colscale, bias, col0 + 32 * p, N);
@@ -462,37 +429,16 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                 } else if constexpr (EPI == kEpiBias) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) q[16 * p + i] = pack2<T>(v[2 * i], v[2 * i + 1]);
+                } else if constexpr (EPI == kEpiResidual16) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) q[16 * p + i] = pack2<__nv_bfloat16>(v[2 * i], v[2 * i + 1]);
                 }
             }
-            // the staging buffer must be ready: loaded (bf16 residual) or no longer read by its last store
-            if constexpr (C::XLOAD) {
-                if (leader) L.epi_ok[grp] = mbar_wait(&xfull[b], (g / C::NBUF) & 1u, err, kErrTmaFull) ? 1u : 0u;
-            } else {
-                if (leader) bulk_wait_read<C::NBUF - 1>();
-            }
+            // the staging buffer must no longer be read by its last store
+            if (leader) bulk_wait_read<C::NBUF - 1>();
             named_barrier(bar_id, 128);
-            if (!L.epi_ok[grp]) {
-                ok = false;
-                break;
-            }
             constexpr int RB = C::ROW_BYTES;
-            if constexpr (EPI == kEpiResidual16) {
-                // X (bf16) + v in f32, rounded once to bf16
-                constexpr int UNITS = RB / 16;
-                uint4 xs[UNITS];
-#pragma unroll
-                for (int j = 0; j < UNITS; ++j) xs[j] = *reinterpret_cast<const uint4*>(buf + swz<RB>(row, j));
-#pragma unroll
-                for (int j = 0; j < UNITS; ++j) {
-                    const float* w = v + 8 * j;
-                    xs[j].x = pack2<__nv_bfloat16>(bf16_lo(xs[j].x) + w[0], bf16_hi(xs[j].x) + w[1]);
-                    xs[j].y = pack2<__nv_bfloat16>(bf16_lo(xs[j].y) + w[2], bf16_hi(xs[j].y) + w[3]);
-                    xs[j].z = pack2<__nv_bfloat16>(bf16_lo(xs[j].z) + w[4], bf16_hi(xs[j].z) + w[5]);
-                    xs[j].w = pack2<__nv_bfloat16>(bf16_lo(xs[j].w) + w[6], bf16_hi(xs[j].w) + w[7]);
-                }
-#pragma unroll
-                for (int j = 0; j < UNITS; ++j) *reinterpret_cast<uint4*>(buf + swz<RB>(row, j)) = xs[j];
-            } else if constexpr (C::OUT_BYTES == 4) {
+            if constexpr (C::OUT_BYTES == 4) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
                     *reinterpret_cast<float4*>(buf + swz<RB>(row, j)) =
@@ -506,33 +452,15 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
             fence_proxy_async_smem();
             named_barrier(bar_id, 128);
             if (leader) {
-                if constexpr (C::REDUCE) tma_reduce_add_2d(tmC, buf, col0, row0);   // X += acc + bias
+                if constexpr (C::REDUCE) tma_reduce_add_2d(tmC, buf, col0, row0);   // X += v
                 else tma_store_2d(tmC, buf, col0, row0);
                 bulk_commit();
-                if constexpr (C::XLOAD) {
-                    // refill the previous chunk's buffer (its store has been read) NBUF chunks ahead
-                    const int next = g - 1 + C::NBUF;
-                    if (g >= 1 && next < total_chunks && next >= loads) {
-                        bulk_wait_read<1>();
-                        const int nb = next % C::NBUF;
-                        int x, y;
-                        chunk_xy(next, x, y);
-                        mbar_arrive_expect_tx(&xfull[nb], C::CHUNK_BYTES);
-                        tma_load_2d(gbuf + nb * C::CHUNK_BYTES, tmC, &xfull[nb], x, y);
-                        loads = next + 1;
-                    }
-                }
             }
         }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
     }
-    if (leader) {
-        bulk_wait_all();
-        // residual loads issued but never consumed (only after a failure) land before the CTA leaves
-        if constexpr (C::XLOAD)
-            for (int h = g; h < loads; ++h) mbar_wait(&xfull[h % C::NBUF], (h / C::NBUF) & 1u, err, kErrTmaFull);
-    }
+    if (leader) bulk_wait_all();
 }
 
 // ------------------------------------------------------------------------------------------------ one CTA
@@ -562,7 +490,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_init(&L.tempty[b], 4 * C::EG);
         }
         mbar_init(L.mma_done, 1);
-        for (int b = 0; b < C::EG * C::NBUF; ++b) mbar_init(&L.xfull[b], 1);
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
@@ -708,7 +635,6 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             mbar_init(&L.tempty[b], 2 * 4 * C::EG);   // the epilogue warps of both CTAs
         }
         mbar_init(L.mma_done, 1);
-        for (int b = 0; b < C::EG * C::NBUF; ++b) mbar_init(&L.xfull[b], 1);
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);

@@ -122,14 +122,14 @@ static CUtensorMap operand_map(const void* base, MapType type, uint64_t K, uint6
 
 // The output (and, for the residuals, the input) of a product: [M, N] with pitch ldc, 16-bit (`t16`) for
 // kEpiBias / kEpiBiasGelu, f32 for kEpiResidual / kEpiF32, e4m3 for kEpiGeluE4m3, bf16 for kEpiResidual16;
-// boxes of one staging chunk (128 rows x GemmCfg::ROW_BYTES: 64-byte rows for the GELU epilogues and for the
-// bias epilogue of an FP8 product, `f8`).
+// boxes of one staging chunk (128 rows x GemmCfg::ROW_BYTES: 64-byte rows for the GELU epilogues, the bf16
+// residual and the bias epilogue of an FP8 product, `f8`). The residuals' maps take TMA reduce-adds into X.
 static CUtensorMap output_map(void* base, int epi, MapType t16, int M, int N, int ldc, bool f8 = false)
 {
     if (epi == kEpiResidual || epi == kEpiF32) return make_map(base, MapType::F32, N, M, ldc, 32, 128);
     if (epi == kEpiGeluE4m3) return make_map(base, MapType::U8, N, M, ldc, 64, 128, true);
     if (epi == kEpiBiasGelu) return make_map(base, t16, N, M, ldc, 32, 128, true);
-    if (epi == kEpiResidual16) return make_map(base, MapType::BF16, N, M, ldc, 64, 128);
+    if (epi == kEpiResidual16) return make_map(base, MapType::BF16, N, M, ldc, 32, 128, true);
     if (epi == kEpiBias && f8) return make_map(base, t16, N, M, ldc, 32, 128, true);
     return make_map(base, t16, N, M, ldc, 64, 128);
 }
@@ -306,9 +306,9 @@ static void launch_gemm_pair_if(const CUtensorMap& ma, const CUtensorMap& mb, co
 }
 
 // Tile choice: kPairTile (a CTA pair per 256 x 256 tile) when there are at least as many pair tiles as pairs
-// fit and the epilogue is light next to the MMAs (bias-only, f32 outputs, the f32 residual's TMA reduction, or
+// fit and the epilogue is light next to the MMAs (bias-only, f32 outputs, the residuals' TMA reductions, or
 // K >= 2048: measured on a B200, the pair kernel is faster for qkv, out and ff2 and slower for ff1, whose GELU
-// epilogue gates both CTAs of a pair, and for the bf16 residual's read-modify-write), else the widest single-CTA
+// epilogue gates both CTAs of a pair), else the widest single-CTA
 // tile that still gives two thirds of the SMs a tile. A launch costs ~10 us however small it is, so at small M
 // fewer, wider tiles win while most SMs are busy (measured, back-to-back launches: M = 4,160, the out product
 // 14.4 us with 132 tiles of 256 against 18.2 with 264 of 128; ff2 20.5 against 28.3); below that the weights
@@ -331,7 +331,7 @@ static int tile_mode()
 static int pick_bn(int M, int N, int K, int epi, int num_sms)
 {
     const int mode = tile_mode();
-    const bool light = epi == kEpiBias || epi == kEpiF32 || epi == kEpiResidual || K >= 2048;
+    const bool light = epi == kEpiBias || epi == kEpiF32 || epi == kEpiResidual || epi == kEpiResidual16 || K >= 2048;
     if (mode == 1 || (mode == 0 && light && ((M + 255) / 256) * ((N + 255) / 256) >= num_sms / 2)) return kPairTile;
     const int m_tiles = (M + 127) / 128;
     for (int bn : {256, 128})

@@ -18,9 +18,10 @@ The FP8 evaluator has no counterpart in the reference (its FP8 study was a simul
 mayfly/docs/cuda_backend.md:150-152). For it, forward takes two options: `act` [layers, 4] rounds the input
 of each layer's four products (qkv, out, ff1, ff2) to e4m3 at that static scale, as the evaluator's producers
 do (with the weight matrices already e4m3-rounded by weights.dequantised_state, this is the FP8 pass in fp32
-arithmetic); `resid_bf16` rounds the residual stream to bf16 after the embedding and after every residual add,
-as the FP8 evaluator stores it; `record` [layers, 4] receives max |.| of those inputs (what the evaluator's
-calibration measures).
+arithmetic); `resid_bf16` keeps the residual stream in bf16 as the FP8 evaluator stores it: the embedding is
+rounded to bf16, and each residual add rounds the product's output v to bf16 and then the sum (the evaluator adds
+bf16(v) into the stream with a bf16 reduction in memory); `record` [layers, 4] receives max |.| of those inputs
+(what the evaluator's calibration measures).
 
 The reference's Python search plays a bf16 autocast pass of the same module on the GPU (mayfly/chess/mcts.py:
 1296-1318, torch.autocast("cuda", torch.bfloat16) around ChessNet.forward), which its own parity check uses as the
@@ -85,11 +86,11 @@ def layer(state, arch, i, x, act=None, record=None, resid=_same, sdpa=False):
     else:
         s = torch.matmul(q, k.transpose(-1, -2)) * (1.0 / math.sqrt(dh))
         o = torch.matmul(torch.softmax(s, dim=-1), v).transpose(1, 2).reshape(B, L, d)
-    x = resid(x + F.linear(product_input(o, 1), state[p + "self_attn.out_proj.weight"],
-                           state[p + "self_attn.out_proj.bias"]))
+    x = resid(x + resid(F.linear(product_input(o, 1), state[p + "self_attn.out_proj.weight"],
+                                 state[p + "self_attn.out_proj.bias"])))
     h = F.layer_norm(x, (d,), state[p + "norm2.weight"], state[p + "norm2.bias"], LN_EPS)
     f = F.gelu(F.linear(product_input(h, 2), state[p + "linear1.weight"], state[p + "linear1.bias"]))
-    return resid(x + F.linear(product_input(f, 3), state[p + "linear2.weight"], state[p + "linear2.bias"]))
+    return resid(x + resid(F.linear(product_input(f, 3), state[p + "linear2.weight"], state[p + "linear2.bias"])))
 
 
 @torch.no_grad()
