@@ -56,6 +56,14 @@
 #ifndef MF_REDUCE_NBUF
 #define MF_REDUCE_NBUF 1
 #endif
+// The FP8 bias epilogue (qkv): 64-byte staging rows in four groups (1) or 128-byte rows (0), and its staging
+// buffers per group.
+#ifndef MF_F8_BIAS_NARROW
+#define MF_F8_BIAS_NARROW 1
+#endif
+#ifndef MF_F8_BIAS_NBUF
+#define MF_F8_BIAS_NBUF 1
+#endif
 
 namespace mf {
 
@@ -117,7 +125,8 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
     // a narrow chunk at a time, and for the FP8 bias and bf16-residual epilogues, which have half the mainloop
     // time of a 16-bit tile to hide in: four groups on narrower chunks measured 2.7% faster on the FP8 qkv
     // product, no faster on the 16-bit one; 128-byte rows otherwise)
-    static constexpr bool NARROW = (EPI == kEpiBias && F8) || EPI == kEpiResidual16;
+    static constexpr bool F8_BIAS = EPI == kEpiBias && F8;
+    static constexpr bool NARROW = (F8_BIAS && MF_F8_BIAS_NARROW) || EPI == kEpiResidual16;
     static constexpr int ROW_BYTES = (HEAVY || NARROW) ? 64 : 128;
     static constexpr int CHUNK_COLS = ROW_BYTES / OUT_BYTES;
     static constexpr int NC = BN / CHUNK_COLS;           // staging chunks per tile
@@ -129,7 +138,8 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
     // 4 x 1).
     static constexpr int EG = EPI == kEpiResidual ? ((NC % MF_REDUCE_EG == 0) ? MF_REDUCE_EG : 1)
                               : ((HEAVY || NARROW) && NC % 4 == 0) ? 4 : (NC % 2 == 0 ? 2 : 1);
-    static constexpr int NBUF = EPI == kEpiResidual ? MF_REDUCE_NBUF : (EG >= 2 ? 1 : 2);   // staging buffers a group
+    static constexpr int NBUF = EPI == kEpiResidual ? MF_REDUCE_NBUF
+                                : F8_BIAS ? MF_F8_BIAS_NBUF : (EG >= 2 ? 1 : 2);   // staging buffers a group
     static constexpr uint32_t A_BYTES = BM * 128;
     static constexpr uint32_t B_BYTES = B_ROWS * 128;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;

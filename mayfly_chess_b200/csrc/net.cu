@@ -21,6 +21,7 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <set>
 #include <stdexcept>
 #include <string>
 #include <tuple>
@@ -130,7 +131,7 @@ static CUtensorMap output_map(void* base, int epi, MapType t16, int M, int N, in
     if (epi == kEpiGeluE4m3) return make_map(base, MapType::U8, N, M, ldc, 64, 128, true);
     if (epi == kEpiBiasGelu) return make_map(base, t16, N, M, ldc, 32, 128, true);
     if (epi == kEpiResidual16) return make_map(base, MapType::BF16, N, M, ldc, 32, 128, true);
-    if (epi == kEpiBias && f8) return make_map(base, t16, N, M, ldc, 32, 128, true);
+    if (epi == kEpiBias && f8 && MF_F8_BIAS_NARROW) return make_map(base, t16, N, M, ldc, 32, 128, true);
     return make_map(base, t16, N, M, ldc, 64, 128);
 }
 
@@ -429,15 +430,18 @@ static void launch_attention_dh(const CUtensorMap& map, TO* att, int B, int d, i
 // against 2.59 for the mma.sync kernel and 2.90 for the two-group one); where it writes e4m3 (the FP8 pass) the
 // two-group kernel (9.44 against 9.57 ms per 4,096-position pass, and 9.2-9.8 for mma.sync). Forcing:
 // MAYFLY_CUDANET_ATT_TC=0 the mma.sync kernel, 1 the two-group kernel, 4 the four-group kernel.
+static int att_tc_env()
+{
+    const char* e = std::getenv("MAYFLY_CUDANET_ATT_TC");
+    if (e && std::strcmp(e, "1") == 0) return 1;
+    if (e && std::strcmp(e, "4") == 0) return 4;
+    if (e && std::strcmp(e, "0") == 0) return 0;
+    return -1;
+}
+
 static int att_tc_mode()
 {
-    static int mode = [] {
-        const char* e = std::getenv("MAYFLY_CUDANET_ATT_TC");
-        if (e && std::strcmp(e, "1") == 0) return 1;
-        if (e && std::strcmp(e, "4") == 0) return 4;
-        if (e && std::strcmp(e, "0") == 0) return 0;
-        return -1;
-    }();
+    static int mode = att_tc_env();
     return mode;
 }
 
@@ -487,11 +491,11 @@ static void launch_attention_tc(const CUtensorMap& map, TO* att, int B, int d, i
 // att = attention(qkv) in TO (T, or e4m3 of att * mul); map from qkv_map over at least B * 65 rows
 template <typename T, typename TO>
 static void launch_attention(const CUtensorMap& map, TO* att, int B, int d, int heads, float mul, uint32_t* err,
-                             cudaStream_t s)
+                             cudaStream_t s, int mode_override = -2)
 {
     if (B < 1 || heads < 1 || d % heads) throw std::runtime_error("cudanet_b200: bad attention sizes");
     const int dh = d / heads;
-    const int mode = att_tc_mode();
+    const int mode = mode_override != -2 ? mode_override : att_tc_mode();
     const int pick = mode >= 0 ? mode : (is_e4m3<TO> ? 1 : 4);
     if (dh == 64 && pick == 4) launch_attention_tc4<T, TO>(map, att, B, d, heads, mul, err, s);
     else if (dh == 64 && pick == 1) launch_attention_tc<T, TO>(map, att, B, d, heads, mul, err, s);
@@ -828,6 +832,9 @@ private:
     // calibration: while set, the 16-bit pass records max |.| of the four products' inputs per layer here
     unsigned int* amax_ = nullptr;
 
+    int att_mode_ = -1;   // MAYFLY_CUDANET_ATT_TC when the handle was made (-1: the evaluator's choice)
+    std::set<int> no_graph_;   // batch sizes whose capture failed: run eagerly
+
     // profiling marks
     bool prof_on_ = false;
     std::vector<cudaEvent_t> prof_ev_;
@@ -962,6 +969,7 @@ void Net::init(const std::string& path, int device)
         map_qkv_ = qkv_map(qkv_, bf16(), static_cast<int>(rows_pad_), a.d, a.heads);
         const char* g = std::getenv("MAYFLY_CUDANET_GRAPH");
         use_graph_ = !(g && std::strcmp(g, "0") == 0);
+        att_mode_ = att_tc_env();
         RT(cudaStreamSynchronize(stream_));
     } catch (...) {
         release();
@@ -1151,7 +1159,7 @@ template <typename T> void Net::forward_t(int B, cudaStream_t s)
             gemm(kEpiResidual, map_ff_, l.ff2_w, false, B, d, ff, EpiArgs{l.ff2_b, nullptr, 1.f}, x_, xp, s);
             continue;
         }
-        launch_attention<T, T>(map_qkv_, static_cast<T*>(att_), B, d, a.heads, 1.f, err_word(), s);
+        launch_attention<T, T>(map_qkv_, static_cast<T*>(att_), B, d, a.heads, 1.f, err_word(), s, att_mode_);
         amax(4 * i + 1, att_, nd, s);
         mark(kPOut, s);
         if (fuse) {
@@ -1219,7 +1227,7 @@ void Net::forward_f8(int B, cudaStream_t s)
             gemm(kEpiResidual16, map_ff_, l.ff2_w, true, B, d, ff, EpiArgs{l.ff2_b, l.ff2_cs, 1.f}, x, xp, s);
             continue;
         }
-        launch_attention<T, F8>(map_qkv_, static_cast<F8*>(att_), B, d, a.heads, l.inv_out, err_word(), s);
+        launch_attention<T, F8>(map_qkv_, static_cast<F8*>(att_), B, d, a.heads, l.inv_out, err_word(), s, att_mode_);
         mark(kPOut, s);
         gemm(kEpiResidual16, map_att_, l.out_w, true, rows, d, d, EpiArgs{l.out_b, l.out_cs, 1.f}, x, d, s);
         mark(kPLn2, s);
@@ -1275,14 +1283,14 @@ void Net::forward(int B, cudaStream_t s)
         return;
     }
     forward_kernels(B, s);
-    if (!use_graph_) return;
+    if (!use_graph_ || no_graph_.count(B)) return;
     RT(cudaStreamSynchronize(s));
     try {
         capture(B);
     } catch (const std::exception& ex) {
-        std::fprintf(stderr, "cudanet_b200: CUDA graph capture failed at B=%d, eager from now on: %.300s\n", B,
-                     ex.what());
-        use_graph_ = false;
+        std::fprintf(stderr, "cudanet_b200: CUDA graph capture failed at B=%d, eager for this batch size: %.300s\n",
+                     B, ex.what());
+        no_graph_.insert(B);
         cudaGetLastError();
     }
 }

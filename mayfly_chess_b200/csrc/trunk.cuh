@@ -110,19 +110,16 @@ template <typename XT> __device__ __forceinline__ float4 store_x4(XT* p, float4 
 // One warp per row, rows = B * 65. ids and hm are clamped to their tables (a bad input cannot read out of
 // bounds), as the reference kernel does. d = 128 * V. h is 16-bit, or e4m3 of h * mul (the FP8 path); x is
 // f32, or bf16 (the FP8 path), and h is the norm of x as stored.
+// One row (a whole warp): the body of embed_ln_kernel.
 template <typename T, int V, typename XT = float>
-__global__ void __launch_bounds__(256) embed_ln_kernel(
-    const int64_t* __restrict__ ids, const float* __restrict__ cast, const int64_t* __restrict__ hm,
+__device__ __forceinline__ void embed_ln_row(
+    int row, const int64_t* __restrict__ ids, const float* __restrict__ cast, const int64_t* __restrict__ hm,
     const int64_t* __restrict__ ep, const float* __restrict__ piece, const float* __restrict__ pos,
     const float* __restrict__ cls, const float* __restrict__ cast_w, const float* __restrict__ cast_b,
     const float* __restrict__ hm_emb, const float* __restrict__ ep_mark, const float* __restrict__ g,
-    const float* __restrict__ beta, XT* __restrict__ x, T* __restrict__ h, int rows, float eps, float mul)
+    const float* __restrict__ beta, XT* __restrict__ x, T* __restrict__ h, float eps, float mul)
 {
     constexpr int d = 128 * V;
-    griddep_wait();
-    griddep_launch();
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (row >= rows) return;   // whole warp
     const int lane = threadIdx.x & 31;
     const int b = row / kTokens, t = row % kTokens;
     float4 v[V];
@@ -173,26 +170,51 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(
     ln_row_store<T, V>(v, d, g, beta, h + (size_t)row * d, eps, mul);
 }
 
+template <typename T, int V, typename XT = float>
+__global__ void __launch_bounds__(256) embed_ln_kernel(
+    const int64_t* __restrict__ ids, const float* __restrict__ cast, const int64_t* __restrict__ hm,
+    const int64_t* __restrict__ ep, const float* __restrict__ piece, const float* __restrict__ pos,
+    const float* __restrict__ cls, const float* __restrict__ cast_w, const float* __restrict__ cast_b,
+    const float* __restrict__ hm_emb, const float* __restrict__ ep_mark, const float* __restrict__ g,
+    const float* __restrict__ beta, XT* __restrict__ x, T* __restrict__ h, int rows, float eps, float mul)
+{
+    griddep_wait();
+    griddep_launch();
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;   // whole warp
+    embed_ln_row<T, V, XT>(row, ids, cast, hm, ep, piece, pos, cls, cast_w, cast_b, hm_emb, ep_mark, g, beta, x, h,
+                           eps, mul);
+}
+
 // ------------------------------------------------------------------------------------------------ LayerNorm
 // h[r] = LN(x[r]) for rows r = row0 + i * row_stride, i < n (row_stride 65 picks the CLS rows for the final
 // norm, chess_net.py:194 / cudanet/kernels_heads.cu:64-86). Output rows are dense: h row i. One warp per row.
 // h is 16-bit, or e4m3 of h * mul (the FP8 path); x is f32, or bf16 (the FP8 path).
+// Output row i (a whole warp): the body of layernorm_kernel.
 template <typename T, int V, typename XT = float>
-__global__ void __launch_bounds__(256) layernorm_kernel(const XT* __restrict__ x, const float* __restrict__ g,
-                                                        const float* __restrict__ b, T* __restrict__ h, int n,
-                                                        int row_stride, float eps, float mul)
+__device__ __forceinline__ void ln_row(int i, const XT* __restrict__ x, const float* __restrict__ g,
+                                       const float* __restrict__ b, T* __restrict__ h, int row_stride, float eps,
+                                       float mul)
 {
     constexpr int d = 128 * V;
-    griddep_wait();
-    griddep_launch();
-    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (i >= n) return;
     const int lane = threadIdx.x & 31;
     const XT* xr = x + (size_t)i * row_stride * d;
     float4 v[V];
 #pragma unroll
     for (int k = 0; k < V; ++k) v[k] = load_x4<XT>(xr + 4 * (lane + 32 * k));
     ln_row_store<T, V>(v, d, g, b, h + (size_t)i * d, eps, mul);
+}
+
+template <typename T, int V, typename XT = float>
+__global__ void __launch_bounds__(256) layernorm_kernel(const XT* __restrict__ x, const float* __restrict__ g,
+                                                        const float* __restrict__ b, T* __restrict__ h, int n,
+                                                        int row_stride, float eps, float mul)
+{
+    griddep_wait();
+    griddep_launch();
+    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (i >= n) return;
+    ln_row<T, V, XT>(i, x, g, b, h, row_stride, eps, mul);
 }
 
 // ------------------------------------------------------------------------------------------------ attention
@@ -277,33 +299,25 @@ template <int DH> __device__ __forceinline__ uint32_t att_off(int r, int c)
     else return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 }
 
-template <typename T, typename TO, int DH>
-__global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const __grid_constant__ CUtensorMap tmQKV,
-                                                                   TO* __restrict__ att, int B, int heads, int d,
-                                                                   float scale, float mul, uint32_t* err)
+// The item loop of the mma.sync attention over items first, first + stride, ... < B * heads, run by every thread
+// of the CTA (warps from kAttWarps on only take part in the barriers). Shared memory at `base` holds NB Q/K/V
+// tile sets and `full` their NB barriers; thread 0 issues the loads. n counts the items this CTA computed before
+// the call (the barriers' phases continue from it) and the count after the call is returned; issued counts the
+// items whose loads thread 0 started.
+template <typename T, typename TO, int DH, int NB>
+__device__ __forceinline__ int attention_mma_items(uint8_t* base, uint64_t* full, volatile uint32_t* ok_flag,
+                                                   const CUtensorMap* tmQKVp, TO* __restrict__ att, int B,
+                                                   int heads, int d, float scale, float mul, uint32_t* err,
+                                                   int first, int stride, int n, int& issued)
 {
     using C = AttCfg<DH>;
     static_assert(kTokens == 65 && kAttRows == 80, "the softmax below hard-codes which key tiles are live");
     constexpr int NT = kAttRows / 8;          // 10 key tiles of 8
     constexpr int DT = DH / 8;                // output column tiles of 8
     constexpr int CH = DH * 2 / 16;           // 16-byte chunks per 16-bit row
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    constexpr int NB = kAttBuffers;
-    uint64_t* full = reinterpret_cast<uint64_t*>(base + NB * C::SET);
-    volatile uint32_t* ok_flag = reinterpret_cast<volatile uint32_t*>(full + 2);
-
+    const CUtensorMap& tmQKV = *tmQKVp;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int items = B * heads;
-    if (tid == 0) {
-        for (int i = 0; i < NB; ++i) mbar_init(&full[i], 1);
-        fence_barrier_init();
-        tma_prefetch_desc(&tmQKV);
-    }
-    __syncthreads();
-    griddep_wait();   // qkv and att belong to the earlier kernels until they complete
-    if (tid == 0) griddep_launch();
-
     auto issue = [&](int item, int buf) {
         const int b = item / heads, h = item - b * heads;
         uint8_t* s = base + buf * C::SET;
@@ -312,170 +326,196 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const __grid_
         for (int which = 0; which < 3; ++which)
             tma_load_2d(s + which * C::TILE, &tmQKV, &full[buf], which * d + h * DH, b * kTokens);
     };
-    int issued = 0;   // items whose loads thread 0 started (thread 0's count)
-    if (tid == 0 && (int)blockIdx.x < items) {
-        issue(blockIdx.x, 0);
-        issued = 1;
+    if (tid == 0 && first < items) {
+        issue(first, n % NB);
+        ++issued;
     }
 
     const int g = lane >> 2, t = lane & 3;
     const int q0 = warp * 16;
     const float sl2 = scale * 1.4426950408889634f;
-    int n = 0;   // items this CTA has computed
-    for (int item = blockIdx.x; item < items; item += gridDim.x, ++n) {
+    for (int item = first; item < items; item += stride, ++n) {
         const int buf = n % NB;
         if (tid == 0) {
-            if (NB == 2 && item + (int)gridDim.x < items) {
-                issue(item + gridDim.x, buf ^ 1);   // that buffer's last reader finished before the last barrier
+            if (NB == 2 && item + stride < items) {
+                issue(item + stride, buf ^ 1);   // that buffer's last reader finished before the last barrier
                 ++issued;
             }
             *ok_flag = mbar_wait(&full[buf], (n / NB) & 1, err, kErrTmaFull) ? 1u : 0u;
         }
         __syncthreads();
         if (!*ok_flag) break;
-        const uint8_t* sQ = base + buf * C::SET;
-        const uint8_t* sK = sQ + C::TILE;
-        const uint8_t* sV = sK + C::TILE;
-        const int b = item / heads, h = item - b * heads;
+        if (warp < kAttWarps) {
+            const uint8_t* sQ = base + buf * C::SET;
+            const uint8_t* sK = sQ + C::TILE;
+            const uint8_t* sV = sK + C::TILE;
+            const int b = item / heads, h = item - b * heads;
 
-        // S = Q K^T for this warp's 16 rows and keys 0..71 (key tile 9, keys 72..79, is all padding: P = 0)
-        constexpr int NT_LIVE = (kTokens + 7) / 8;   // 9 key tiles hold the 65 live keys
-        float s[NT][4];
+            // S = Q K^T for this warp's 16 rows and keys 0..71 (key tile 9, keys 72..79, is all padding: P = 0)
+            constexpr int NT_LIVE = (kTokens + 7) / 8;   // 9 key tiles hold the 65 live keys
+            float s[NT][4];
 #pragma unroll
-        for (int nn = 0; nn < NT; ++nn) s[nn][0] = s[nn][1] = s[nn][2] = s[nn][3] = 0.f;
+            for (int nn = 0; nn < NT; ++nn) s[nn][0] = s[nn][1] = s[nn][2] = s[nn][3] = 0.f;
 #pragma unroll
-        for (int k0 = 0; k0 < DH; k0 += 16) {
-            uint32_t a[4];
-            ldsm_x4(smem_u32(sQ + att_off<DH>(q0 + (lane & 15), (k0 >> 3) + (lane >> 4))), a[0], a[1], a[2], a[3]);
+            for (int k0 = 0; k0 < DH; k0 += 16) {
+                uint32_t a[4];
+                ldsm_x4(smem_u32(sQ + att_off<DH>(q0 + (lane & 15), (k0 >> 3) + (lane >> 4))), a[0], a[1], a[2], a[3]);
 #pragma unroll
-            for (int nn = 0; nn < NT_LIVE; nn += 2) {
-                // keys nn*8 .. nn*8+15: matrices (keys 0-7, k0), (keys 0-7, k0+8), (keys 8-15, k0), (keys 8-15, k0+8)
-                const int key = nn * 8 + (lane & 7) + ((lane >> 4) << 3);
-                const int kc = (k0 >> 3) + ((lane >> 3) & 1);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4(smem_u32(sK + att_off<DH>(key, kc)), b0, b1, b2, b3);
-                MmaName<T>::mma(s[nn], a, b0, b1);
-                if (nn + 1 < NT_LIVE) MmaName<T>::mma(s[nn + 1], a, b2, b3);
+                for (int nn = 0; nn < NT_LIVE; nn += 2) {
+                    // keys nn*8 .. nn*8+15: matrices (keys 0-7, k0), (keys 0-7, k0+8), (keys 8-15, k0), (keys 8-15, k0+8)
+                    const int key = nn * 8 + (lane & 7) + ((lane >> 4) << 3);
+                    const int kc = (k0 >> 3) + ((lane >> 3) & 1);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(smem_u32(sK + att_off<DH>(key, kc)), b0, b1, b2, b3);
+                    MmaName<T>::mma(s[nn], a, b0, b1);
+                    if (nn + 1 < NT_LIVE) MmaName<T>::mma(s[nn + 1], a, b2, b3);
+                }
             }
-        }
 
-        // softmax over keys 0..64 of rows g and g+8 (each row spread over the quad's 4 lanes), in base 2:
-        // exp(x * scale - m) = 2^(x * c - m * c), c = scale * log2(e), one FMA per score before the hardware 2^x
-        // (ex2.approx, relative error near 2^-22, far below the 16-bit rounding P gets next). Key tiles 0..7 are
-        // all live, tile 8 holds key 64 (lane t = 0, j = 0) and padding, tile 9 is padding: P = 0 there.
-        float mx0 = -INFINITY, mx1 = -INFINITY;
+            // softmax over keys 0..64 of rows g and g+8 (each row spread over the quad's 4 lanes), in base 2:
+            // exp(x * scale - m) = 2^(x * c - m * c), c = scale * log2(e), one FMA per score before the hardware 2^x
+            // (ex2.approx, relative error near 2^-22, far below the 16-bit rounding P gets next). Key tiles 0..7 are
+            // all live, tile 8 holds key 64 (lane t = 0, j = 0) and padding, tile 9 is padding: P = 0 there.
+            float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-        for (int nn = 0; nn < 8; ++nn) {
-            mx0 = fmaxf(mx0, fmaxf(s[nn][0], s[nn][1]));
-            mx1 = fmaxf(mx1, fmaxf(s[nn][2], s[nn][3]));
-        }
-        if (t == 0) {
-            mx0 = fmaxf(mx0, s[8][0]);
-            mx1 = fmaxf(mx1, s[8][2]);
-        }
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        const float mc0 = mx0 * sl2, mc1 = mx1 * sl2;
-        float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-        for (int nn = 0; nn < 8; ++nn) {
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                s[nn][j] = ex2_approx(fmaf(s[nn][j], sl2, -mc0));
-                s[nn][2 + j] = ex2_approx(fmaf(s[nn][2 + j], sl2, -mc1));
-                sum0 += s[nn][j];
-                sum1 += s[nn][2 + j];
+            for (int nn = 0; nn < 8; ++nn) {
+                mx0 = fmaxf(mx0, fmaxf(s[nn][0], s[nn][1]));
+                mx1 = fmaxf(mx1, fmaxf(s[nn][2], s[nn][3]));
             }
-        }
-        s[8][0] = t == 0 ? ex2_approx(fmaf(s[8][0], sl2, -mc0)) : 0.f;
-        s[8][2] = t == 0 ? ex2_approx(fmaf(s[8][2], sl2, -mc1)) : 0.f;
-        s[8][1] = s[8][3] = 0.f;
-        sum0 += s[8][0];
-        sum1 += s[8][2];
+            if (t == 0) {
+                mx0 = fmaxf(mx0, s[8][0]);
+                mx1 = fmaxf(mx1, s[8][2]);
+            }
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+            const float mc0 = mx0 * sl2, mc1 = mx1 * sl2;
+            float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) s[9][j] = 0.f;
-        sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
-        sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
-        sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
-        sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+            for (int nn = 0; nn < 8; ++nn) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    s[nn][j] = ex2_approx(fmaf(s[nn][j], sl2, -mc0));
+                    s[nn][2 + j] = ex2_approx(fmaf(s[nn][2 + j], sl2, -mc1));
+                    sum0 += s[nn][j];
+                    sum1 += s[nn][2 + j];
+                }
+            }
+            s[8][0] = t == 0 ? ex2_approx(fmaf(s[8][0], sl2, -mc0)) : 0.f;
+            s[8][2] = t == 0 ? ex2_approx(fmaf(s[8][2], sl2, -mc1)) : 0.f;
+            s[8][1] = s[8][3] = 0.f;
+            sum0 += s[8][0];
+            sum1 += s[8][2];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[9][j] = 0.f;
+            sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+            sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+            sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+            sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
 
-        // O = P V: P's fragments are S's accumulators (keys 16kk..16kk+15 = key tiles 2kk, 2kk+1)
-        float o[DT][4];
+            // O = P V: P's fragments are S's accumulators (keys 16kk..16kk+15 = key tiles 2kk, 2kk+1)
+            float o[DT][4];
 #pragma unroll
-        for (int nn = 0; nn < DT; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
+            for (int nn = 0; nn < DT; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
 #pragma unroll
-        for (int kk = 0; kk < kAttRows / 16; ++kk) {
-            uint32_t a[4];
-            a[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
-            a[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
-            a[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-            a[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+            for (int kk = 0; kk < kAttRows / 16; ++kk) {
+                uint32_t a[4];
+                a[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
+                a[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
+                a[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+                a[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
-            for (int nn = 0; nn < DT; nn += 2) {
-                // V rows (keys) 16kk.., transposed: matrices (keys 0-7, cols nn*8), (keys 8-15, cols nn*8),
-                // (keys 0-7, cols nn*8+8), (keys 8-15, cols nn*8+8)
-                const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-                const int vc = nn + (lane >> 4);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(smem_u32(sV + att_off<DH>(key, vc)), b0, b1, b2, b3);
-                MmaName<T>::mma(o[nn], a, b0, b1);
-                MmaName<T>::mma(o[nn + 1], a, b2, b3);
+                for (int nn = 0; nn < DT; nn += 2) {
+                    // V rows (keys) 16kk.., transposed: matrices (keys 0-7, cols nn*8), (keys 8-15, cols nn*8),
+                    // (keys 0-7, cols nn*8+8), (keys 8-15, cols nn*8+8)
+                    const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                    const int vc = nn + (lane >> 4);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(smem_u32(sV + att_off<DH>(key, vc)), b0, b1, b2, b3);
+                    MmaName<T>::mma(o[nn], a, b0, b1);
+                    MmaName<T>::mma(o[nn + 1], a, b2, b3);
+                }
             }
-        }
 
-        // normalise, stage this warp's rows in its own rows of the Q tile (no other warp reads them; the
-        // tile is not refilled before the barrier that ends this item), store
-        const float inv0 = 1.f / sum0, inv1 = 1.f / sum1;
-        uint8_t* st = base + buf * C::SET;
-        const size_t row0 = (size_t)b * kTokens;
-        __syncwarp();
-        if constexpr (is_e4m3<TO>) {
-            // e4m3 rows of DH bytes at a pitch of DH + 16 bytes, inside the warp's own 16 rows of the Q tile
-            constexpr int PB = DH + 16;
-            constexpr int CH8 = DH / 16;
-            static_assert(16 * PB <= 16 * C::ROWB, "staging stays inside the warp's rows");
-            uint8_t* wst = st + q0 * C::ROWB;
-            const float m0 = inv0 * mul, m1 = inv1 * mul;
-#pragma unroll
-            for (int nn = 0; nn < DT; ++nn) {
-                *reinterpret_cast<uint16_t*>(wst + g * PB + nn * 8 + 2 * t) = static_cast<uint16_t>(
-                    __nv_cvt_float2_to_fp8x2(make_float2(o[nn][0] * m0, o[nn][1] * m0), __NV_SATFINITE, __NV_E4M3));
-                *reinterpret_cast<uint16_t*>(wst + (g + 8) * PB + nn * 8 + 2 * t) = static_cast<uint16_t>(
-                    __nv_cvt_float2_to_fp8x2(make_float2(o[nn][2] * m1, o[nn][3] * m1), __NV_SATFINITE, __NV_E4M3));
-            }
+            // normalise, stage this warp's rows in its own rows of the Q tile (no other warp reads them; the
+            // tile is not refilled before the barrier that ends this item), store
+            const float inv0 = 1.f / sum0, inv1 = 1.f / sum1;
+            uint8_t* st = base + buf * C::SET;
+            const size_t row0 = (size_t)b * kTokens;
             __syncwarp();
-            for (int i = lane; i < 16 * CH8; i += 32) {
-                const int lr = i / CH8, c = i % CH8;
-                if (q0 + lr < kTokens)
-                    *(reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(att) + (row0 + q0 + lr) * d +
-                                               (size_t)h * DH) + c) =
-                        *reinterpret_cast<const uint4*>(wst + lr * PB + c * 16);
-            }
-        } else {
+            if constexpr (is_e4m3<TO>) {
+                // e4m3 rows of DH bytes at a pitch of DH + 16 bytes, inside the warp's own 16 rows of the Q tile
+                constexpr int PB = DH + 16;
+                constexpr int CH8 = DH / 16;
+                static_assert(16 * PB <= 16 * C::ROWB, "staging stays inside the warp's rows");
+                uint8_t* wst = st + q0 * C::ROWB;
+                const float m0 = inv0 * mul, m1 = inv1 * mul;
 #pragma unroll
-            for (int nn = 0; nn < DT; ++nn) {
-                *reinterpret_cast<uint32_t*>(st + att_off<DH>(q0 + g, nn) + 4 * t) =
-                    pack2<T>(o[nn][0] * inv0, o[nn][1] * inv0);
-                *reinterpret_cast<uint32_t*>(st + att_off<DH>(q0 + g + 8, nn) + 4 * t) =
-                    pack2<T>(o[nn][2] * inv1, o[nn][3] * inv1);
-            }
-            __syncwarp();
-            for (int i = lane; i < 16 * CH; i += 32) {
-                const int r = q0 + i / CH, c = i % CH;
-                if (r < kTokens)
-                    *(reinterpret_cast<uint4*>(att + (row0 + r) * d + (size_t)h * DH) + c) =
-                        *reinterpret_cast<const uint4*>(st + att_off<DH>(r, c));
+                for (int nn = 0; nn < DT; ++nn) {
+                    *reinterpret_cast<uint16_t*>(wst + g * PB + nn * 8 + 2 * t) = static_cast<uint16_t>(
+                        __nv_cvt_float2_to_fp8x2(make_float2(o[nn][0] * m0, o[nn][1] * m0), __NV_SATFINITE, __NV_E4M3));
+                    *reinterpret_cast<uint16_t*>(wst + (g + 8) * PB + nn * 8 + 2 * t) = static_cast<uint16_t>(
+                        __nv_cvt_float2_to_fp8x2(make_float2(o[nn][2] * m1, o[nn][3] * m1), __NV_SATFINITE, __NV_E4M3));
+                }
+                __syncwarp();
+                for (int i = lane; i < 16 * CH8; i += 32) {
+                    const int lr = i / CH8, c = i % CH8;
+                    if (q0 + lr < kTokens)
+                        *(reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(att) + (row0 + q0 + lr) * d +
+                                                   (size_t)h * DH) + c) =
+                            *reinterpret_cast<const uint4*>(wst + lr * PB + c * 16);
+                }
+            } else {
+#pragma unroll
+                for (int nn = 0; nn < DT; ++nn) {
+                    *reinterpret_cast<uint32_t*>(st + att_off<DH>(q0 + g, nn) + 4 * t) =
+                        pack2<T>(o[nn][0] * inv0, o[nn][1] * inv0);
+                    *reinterpret_cast<uint32_t*>(st + att_off<DH>(q0 + g + 8, nn) + 4 * t) =
+                        pack2<T>(o[nn][2] * inv1, o[nn][3] * inv1);
+                }
+                __syncwarp();
+                for (int i = lane; i < 16 * CH; i += 32) {
+                    const int r = q0 + i / CH, c = i % CH;
+                    if (r < kTokens)
+                        *(reinterpret_cast<uint4*>(att + (row0 + r) * d + (size_t)h * DH) + c) =
+                            *reinterpret_cast<const uint4*>(st + att_off<DH>(r, c));
+                }
             }
         }
         fence_proxy_async_smem();   // this thread's shared-memory reads and writes of the buffer come before
         __syncthreads();            // the TMA writes that refill it next
-        if (NB == 1 && tid == 0 && item + (int)gridDim.x < items) {
-            issue(item + gridDim.x, 0);
+        if (NB == 1 && tid == 0 && item + stride < items) {
+            issue(item + stride, 0);
             ++issued;
         }
     }
+    return n;
+}
+
+template <typename T, typename TO, int DH>
+__global__ void __launch_bounds__(kAttWarps * 32) attention_kernel(const __grid_constant__ CUtensorMap tmQKV,
+                                                                   TO* __restrict__ att, int B, int heads, int d,
+                                                                   float scale, float mul, uint32_t* err)
+{
+    using C = AttCfg<DH>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int NB = kAttBuffers;
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + NB * C::SET);
+    volatile uint32_t* ok_flag = reinterpret_cast<volatile uint32_t*>(full + 2);
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int i = 0; i < NB; ++i) mbar_init(&full[i], 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&tmQKV);
+    }
+    __syncthreads();
+    griddep_wait();   // qkv and att belong to the earlier kernels until they complete
+    if (tid == 0) griddep_launch();
+    int issued = 0;   // items whose loads thread 0 started (thread 0's count)
+    const int n = attention_mma_items<T, TO, DH, NB>(base, full, ok_flag, &tmQKV, att, B, heads, d, scale, mul, err,
+                                                     blockIdx.x, gridDim.x, 0, issued);
     // the loads thread 0 started have landed before the CTA leaves (only after a failed wait are any pending)
     if (tid == 0)
         for (int k = n; k < issued; ++k) mbar_wait(&full[k % NB], (k / NB) & 1, err, kErrTmaFull);
@@ -492,15 +532,12 @@ template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16
 // lane j scores keys j, j + 32 and j + 64 (q broadcast to every lane in registers, each key row read whole),
 // the softmax is a warp reduction, then lane j accumulates output dims 2j, 2j + 1 over the 65 keys (each key's
 // probability broadcast by a shuffle). att_cls [B, d] is dense; TO is T, or e4m3 of att * mul (the FP8 path).
+// One (board, head) item (a whole warp): the body of attention_cls_kernel.
 template <typename T, typename TO, int DH>
-__global__ void __launch_bounds__(256) attention_cls_kernel(const T* __restrict__ qkv, TO* __restrict__ att,
-                                                            int B, int heads, int d, float scale, float mul)
+__device__ __forceinline__ void attention_cls_item(int item, const T* __restrict__ qkv, TO* __restrict__ att,
+                                                   int heads, int d, float scale, float mul)
 {
     static_assert(DH == 64 || DH == 32, "head width 32 or 64");
-    griddep_wait();
-    griddep_launch();
-    const int item = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (item >= B * heads) return;   // whole warp
     const int lane = threadIdx.x & 31;
     const int b = item / heads, h = item - b * heads;
     const size_t ld = 3 * (size_t)d;
@@ -570,6 +607,17 @@ __global__ void __launch_bounds__(256) attention_cls_kernel(const T* __restrict_
     }
 }
 
+template <typename T, typename TO, int DH>
+__global__ void __launch_bounds__(256) attention_cls_kernel(const T* __restrict__ qkv, TO* __restrict__ att,
+                                                            int B, int heads, int d, float scale, float mul)
+{
+    griddep_wait();
+    griddep_launch();
+    const int item = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (item >= B * heads) return;   // whole warp
+    attention_cls_item<T, TO, DH>(item, qkv, att, heads, d, scale, mul);
+}
+
 // ------------------------------------------------------------------------------------------------ calibration
 // out = max(out, max |p[i]|) over i < n (out holds the f32 bits: non-negative floats order like their bits).
 // Records the ranges of the four product inputs in a 16-bit pass, from which the FP8 path's static input
@@ -592,15 +640,11 @@ __global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ p, si
 //   val = 2 * sum_k w_k q_k - 1;  pol_k = p_k, qv_k = 2 q_k - 1 on legal slots, 0 on padding
 // A row with no legal slot gets val = -1. logits [B, 2*moves] f32 (policy, then qvalue). One warp per board.
 // Policy indices outside 0..moves-1 are clamped (a bad input cannot read out of bounds).
-__global__ void __launch_bounds__(256) heads_post_kernel(const float* __restrict__ logits,
-                                                         const int64_t* __restrict__ I,
-                                                         const uint8_t* __restrict__ Mk, int B, int wide,
-                                                         int moves, float* __restrict__ pol,
-                                                         float* __restrict__ val, float* __restrict__ qv)
+__device__ __forceinline__ void heads_post_board(int b, const float* __restrict__ logits,
+                                                 const int64_t* __restrict__ I, const uint8_t* __restrict__ Mk,
+                                                 int wide, int moves, float* __restrict__ pol,
+                                                 float* __restrict__ val, float* __restrict__ qv)
 {
-    griddep_wait();
-    const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (b >= B) return;
     const int lane = threadIdx.x & 31;
     const float* lp = logits + (size_t)b * 2 * moves;
     const float* lq = lp + moves;
@@ -633,6 +677,18 @@ __global__ void __launch_bounds__(256) heads_post_kernel(const float* __restrict
     s = warp_sum(s);
     acc = warp_sum(acc);
     if (lane == 0) val[b] = s > 0.f ? (acc / s) * 2.0f - 1.0f : -1.0f;
+}
+
+__global__ void __launch_bounds__(256) heads_post_kernel(const float* __restrict__ logits,
+                                                         const int64_t* __restrict__ I,
+                                                         const uint8_t* __restrict__ Mk, int B, int wide,
+                                                         int moves, float* __restrict__ pol,
+                                                         float* __restrict__ val, float* __restrict__ qv)
+{
+    griddep_wait();
+    const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (b >= B) return;
+    heads_post_board(b, logits, I, Mk, wide, moves, pol, val, qv);
 }
 
 }  // namespace mf

@@ -60,7 +60,8 @@ def metrics(ref, got, widths, decided_gap=0.04):
             "q_mean": float(q.mean()), "val_max": float(wdl.max()), "val_mean": float(wdl.mean()),
             "prior_max": float(prior.max()), "prior_mean": float(prior.mean()),
             "top1": top1 / n, "top1_hits": top1, "top3": top3 / n, "top3_hits": top3, "rows": n,
-            "top1_clear": clear_ok / max(clear, 1), "clear_rows": clear, "top1_decided": dec_ok / max(dec, 1),
+            "top1_clear": clear_ok / clear if clear else 1.0, "clear_rows": clear,
+            "top1_decided": dec_ok / dec if dec else 1.0,
             "decided_rows": dec, "nonfinite": nonfinite, "pad_nonzero": pad, "ref_form": ref_form}
 
 
