@@ -318,10 +318,12 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ 
 }
 
 // ------------------------------------------------------------------------------------------------ four groups
-// The same arithmetic with four softmax groups of 4 warps (576 threads), each group owning one tensor-memory
-// slot (columns 128 g .. 128 g + 79) and finishing its item before it takes the next: S(n) -> softmax -> P over
-// the Q tile -> (PV(n) on the tensor cores) -> O(n) normalised and stored -> slots handed back. Four items are
-// in flight instead of two and twice as many warps hide each other's latencies. Registers are tighter (112 a
+// The same arithmetic with four softmax groups of 4 warps (576 threads), group n % 4 taking item n and finishing
+// it before it takes the next: S(n) -> softmax -> P over the Q tile -> (PV(n) on the tensor cores) -> O(n)
+// normalised and stored -> slots handed back. Four items are in flight instead of two and twice as many warps
+// hide each other's latencies. Item n's scores and output live in tensor-memory slot n % NS (NS = 5 slots of 96
+// columns, S taking 80 and O 64 of them): one more slot than groups, so the S product of a group's next item
+// runs while the group still works on its current one. Registers are tighter (112 a
 // thread), so a row's scores are read from tensor memory twice, 32 columns at a time: once for the row max, once
 // for the exponentials. The MMA thread issues whichever of the next S (its load landed, its group's slot free)
 // and the next PV (its P written) is ready first, polling with mbarrier.test_wait (which never suspends the
@@ -329,19 +331,21 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ 
 struct AttTc4Cfg {
     static constexpr int DH = 64;
     static constexpr int LS = 6;
-    static constexpr int G = 4;                              // softmax groups = tensor-memory slots
+    static constexpr int G = 4;                              // softmax groups
+    static constexpr int NS = 5;                             // tensor-memory slots
     static constexpr int KEYS = 80;
     static constexpr uint32_t Q_BYTES = 128 * 128;
     static constexpr uint32_t KV_BYTES = KEYS * 128;
     static constexpr uint32_t Q_OFF = 0, K_OFF = Q_BYTES, V_OFF = K_OFF + KV_BYTES;
     static constexpr uint32_t LOAD_SLOT = V_OFF + KV_BYTES;
     static constexpr uint32_t LOAD_BYTES = 3 * KEYS * 128;
-    static constexpr size_t SMEM = 1024 + LS * (size_t)LOAD_SLOT + 256;
+    static constexpr size_t SMEM = 1024 + LS * (size_t)LOAD_SLOT + 512;
     static constexpr int THREADS = 64 + 128 * G;
     static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr uint32_t T_STRIDE = 128;
+    static constexpr uint32_t T_STRIDE = 96;
     static_assert(LOAD_SLOT % 1024 == 0 && K_OFF % 1024 == 0 && V_OFF % 1024 == 0, "1024-byte aligned tiles");
-    static_assert(G * T_STRIDE <= TMEM_COLS && SMEM <= 232448, "resources");
+    static_assert(NS * T_STRIDE <= TMEM_COLS && T_STRIDE >= KEYS && NS > G && SMEM <= 232448, "resources");
+    static_assert((2 * LS + 3 * NS + G + 1) * 8 + 4 + 8 * G <= 512, "barriers");
 };
 
 template <typename T, typename TO>
@@ -350,16 +354,16 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
                      float scale, float mul, uint32_t* err)
 {
     using C = AttTc4Cfg;
-    constexpr int LS = C::LS, G = C::G;
+    constexpr int LS = C::LS, G = C::G, NS = C::NS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(base + LS * C::LOAD_SLOT);   // [LS] Q, K, V landed
     uint64_t* empty = full + LS;     // [LS] the load slot is finished with (its group's 4 warps)
-    uint64_t* sfull = empty + LS;    // [G] S in the group's tensor-memory slot
-    uint64_t* pready = sfull + G;    // [G] P in shared memory (4 warps)
-    uint64_t* ofull = pready + G;    // [G] O in the slot
-    uint64_t* tfree = ofull + G;     // [G] the slot is read (4 warps)
-    uint64_t* mma_done = tfree + G;
+    uint64_t* sfull = empty + LS;    // [NS] S in the tensor-memory slot
+    uint64_t* ofull = sfull + NS;    // [NS] O in the slot
+    uint64_t* tfree = ofull + NS;    // [NS] the slot is read (4 warps)
+    uint64_t* pready = tfree + NS;   // [G] the group's P in shared memory (4 warps)
+    uint64_t* mma_done = pready + G;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile uint32_t* ok = tmem_slot + 1;   // [G x 2]: the leaders' broadcasts
 
@@ -378,12 +382,12 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 4);
         }
-        for (int i = 0; i < G; ++i) {
+        for (int i = 0; i < NS; ++i) {
             mbar_init(&sfull[i], 1);
-            mbar_init(&pready[i], 4);
             mbar_init(&ofull[i], 1);
             mbar_init(&tfree[i], 4);
         }
+        for (int i = 0; i < G; ++i) mbar_init(&pready[i], 4);
         mbar_init(mma_done, 1);
         fence_barrier_init();
         tma_prefetch_desc(&tmQKV);
@@ -429,31 +433,31 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
             uint32_t idle = 0;
             while (np < my) {
                 bool progressed = false;
-                if (ns < my && ns < np + G) {
-                    const int ls = ns % LS, g = ns % G;
+                if (ns < my && ns < np + NS) {
+                    const int ls = ns % LS, ts = ns % NS;
                     if (mbar_test_wait(&full[ls], (ns / LS) & 1) &&
-                        (ns < G || mbar_test_wait(&tfree[g], (ns / G - 1) & 1))) {
+                        (ns < NS || mbar_test_wait(&tfree[ts], (ns / NS - 1) & 1))) {
                         tc_fence_after();
                         const uint32_t sb = smem_u32(base + ls * C::LOAD_SLOT);
 #pragma unroll
                         for (int k = 0; k < C::DH / 16; ++k)
-                            umma_f16(tmem + C::T_STRIDE * g, sdesc_sw128(sb + C::Q_OFF + 32u * k),
+                            umma_f16(tmem + C::T_STRIDE * ts, sdesc_sw128(sb + C::Q_OFF + 32u * k),
                                      sdesc_sw128(sb + C::K_OFF + 32u * k), idS, k > 0 ? 1u : 0u);
-                        umma_commit(&sfull[g]);
+                        umma_commit(&sfull[ts]);
                         ++ns;
                         progressed = true;
                     }
                 }
                 if (np < ns) {
-                    const int ls = np % LS, g = np % G;
+                    const int ls = np % LS, g = np % G, ts = np % NS;
                     if (mbar_test_wait(&pready[g], (np / G) & 1)) {
                         tc_fence_after();
                         const uint32_t sb = smem_u32(base + ls * C::LOAD_SLOT);
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
-                            umma_f16(tmem + C::T_STRIDE * g, sdesc_sw128(sb + C::Q_OFF + 32u * k),
+                            umma_f16(tmem + C::T_STRIDE * ts, sdesc_sw128(sb + C::Q_OFF + 32u * k),
                                      sdesc_sw128(sb + C::V_OFF + 2048u * k), idO, k > 0 ? 1u : 0u);
-                        umma_commit(&ofull[g]);
+                        umma_commit(&ofull[ts]);
                         ++np;
                         progressed = true;
                     }
@@ -480,12 +484,12 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
         const bool live = quarter < 3;                   // rows 96..127 are padding
         const bool leader = threadIdx.x == 64 + 128 * grp;
         const uint32_t bar_id = 1 + grp;
-        const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + C::T_STRIDE * grp;
         const float sl2 = scale * 1.4426950408889634f;
         for (int n = grp; n < my; n += G) {
-            const int ls = n % LS;
-            const uint32_t par = (n / G) & 1;
-            if (leader) ok[2 * grp] = mbar_wait(&sfull[grp], par, err, kErrTmemFull) ? 1u : 0u;
+            const int ls = n % LS, ts = n % NS;
+            const uint32_t par = (n / NS) & 1;   // the phase of item n's tensor-memory slot
+            const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + C::T_STRIDE * ts;
+            if (leader) ok[2 * grp] = mbar_wait(&sfull[ts], par, err, kErrTmemFull) ? 1u : 0u;
             named_barrier(bar_id, 128);
             if (!ok[2 * grp]) break;
             float p64 = 0.f, sum = 0.f;
@@ -538,7 +542,7 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&pready[grp]);
-            if (leader) ok[2 * grp + 1] = mbar_wait(&ofull[grp], par, err, kErrTmemFull) ? 1u : 0u;
+            if (leader) ok[2 * grp + 1] = mbar_wait(&ofull[ts], par, err, kErrTmemFull) ? 1u : 0u;
             named_barrier(bar_id, 128);
             if (!ok[2 * grp + 1]) break;
             if (live) {
@@ -591,7 +595,7 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
             }
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&tfree[grp]);
+                mbar_arrive(&tfree[ts]);
                 mbar_arrive(&empty[ls]);
             }
         }

@@ -425,11 +425,11 @@ static void launch_attention_dh(const CUtensorMap& map, TO* att, int B, int d, i
 }
 
 // Which attention kernel runs head width 64 (attention_tc.cuh has two tensor-memory kernels: two softmax groups
-// with a finished item pending per group, and four groups that finish each item before the next). Measured on a
-// B200: where attention writes 16-bit values the four-group kernel is fastest (2.41 ms per 1,024-position pass
-// against 2.59 for the mma.sync kernel and 2.90 for the two-group one); where it writes e4m3 (the FP8 pass) the
-// two-group kernel (9.44 against 9.57 ms per 4,096-position pass, and 9.2-9.8 for mma.sync). Forcing:
-// MAYFLY_CUDANET_ATT_TC=0 the mma.sync kernel, 1 the two-group kernel, 4 the four-group kernel.
+// with a finished item pending per group, and four groups that finish each item before the next, over five
+// tensor-memory slots). Measured on a B200, the four-group kernel is the fastest for both output types: 2.36 ms
+// per 1,024-position bf16 pass against 2.59 for the mma.sync kernel and 2.90 for the two-group one, and 8.46
+// against 8.96 ms (two-group) per 4,096-position FP8 pass. Forcing: MAYFLY_CUDANET_ATT_TC=0 the mma.sync kernel,
+// 1 the two-group kernel, 4 the four-group kernel.
 static int att_tc_env()
 {
     const char* e = std::getenv("MAYFLY_CUDANET_ATT_TC");
@@ -496,7 +496,7 @@ static void launch_attention(const CUtensorMap& map, TO* att, int B, int d, int 
     if (B < 1 || heads < 1 || d % heads) throw std::runtime_error("cudanet_b200: bad attention sizes");
     const int dh = d / heads;
     const int mode = mode_override != -2 ? mode_override : att_tc_mode();
-    const int pick = mode >= 0 ? mode : (is_e4m3<TO> ? 1 : 4);
+    const int pick = mode >= 0 ? mode : 4;
     if (dh == 64 && pick == 4) launch_attention_tc4<T, TO>(map, att, B, d, heads, mul, err, s);
     else if (dh == 64 && pick == 1) launch_attention_tc<T, TO>(map, att, B, d, heads, mul, err, s);
     else if (dh == 64) launch_attention_dh<T, TO, 64>(map, att, B, d, heads, mul, err, s);
