@@ -123,16 +123,18 @@ static CUtensorMap operand_map(const void* base, MapType type, uint64_t K, uint6
 
 // The output (and, for the residuals, the input) of a product: [M, N] with pitch ldc, 16-bit (`t16`) for
 // kEpiBias / kEpiBiasGelu, f32 for kEpiResidual / kEpiF32, e4m3 for kEpiGeluE4m3, bf16 for kEpiResidual16;
-// boxes of one staging chunk (128 rows x GemmCfg::ROW_BYTES: 64-byte rows for the GELU epilogues, the bf16
-// residual and the bias epilogue of an FP8 product, `f8`). The residuals' maps take TMA reduce-adds into X.
+// boxes of one epilogue store (GemmCfg::ROW_BYTES wide: 64-byte rows for the GELU epilogues, the bf16 residual
+// and the bias epilogue of an FP8 product, `f8`; store_rows(epi, f8) rows high). The residuals' maps take TMA
+// reduce-adds into X.
 static CUtensorMap output_map(void* base, int epi, MapType t16, int M, int N, int ldc, bool f8 = false)
 {
-    if (epi == kEpiResidual || epi == kEpiF32) return make_map(base, MapType::F32, N, M, ldc, 32, 128);
-    if (epi == kEpiGeluE4m3) return make_map(base, MapType::U8, N, M, ldc, 64, 128, true);
-    if (epi == kEpiBiasGelu) return make_map(base, t16, N, M, ldc, 32, 128, true);
-    if (epi == kEpiResidual16) return make_map(base, MapType::BF16, N, M, ldc, 32, 128, true);
-    if (epi == kEpiBias && f8 && MF_F8_BIAS_NARROW) return make_map(base, t16, N, M, ldc, 32, 128, true);
-    return make_map(base, t16, N, M, ldc, 64, 128);
+    const uint32_t rows = static_cast<uint32_t>(store_rows(epi, f8));
+    if (epi == kEpiResidual || epi == kEpiF32) return make_map(base, MapType::F32, N, M, ldc, 32, rows);
+    if (epi == kEpiGeluE4m3) return make_map(base, MapType::U8, N, M, ldc, 64, rows, true);
+    if (epi == kEpiBiasGelu) return make_map(base, t16, N, M, ldc, 32, rows, true);
+    if (epi == kEpiResidual16) return make_map(base, MapType::BF16, N, M, ldc, 32, rows, true);
+    if (epi == kEpiBias && f8 && MF_F8_BIAS_NARROW) return make_map(base, t16, N, M, ldc, 32, rows, true);
+    return make_map(base, t16, N, M, ldc, 64, rows);
 }
 
 // ------------------------------------------------------------------------------------------------ launchers
@@ -1021,7 +1023,8 @@ void Net::gemm(int epi, const CUtensorMap& ma, const void* W, bool w_f8, int M, 
     const CUtensorMap& mb = wmap(W, w_f8 ? MapType::U8 : type16(bf16()), N, K, static_cast<int>(w_box_rows(bn)));
     const auto okey = std::make_tuple(static_cast<const void*>(out), epi + (w_f8 ? 16 : 0), M, N, ldc);
     auto it = omaps_.find(okey);
-    if (it == omaps_.end()) it = omaps_.emplace(okey, output_map(out, epi, type16(bf16()), M, N, ldc, w_f8)).first;
+    if (it == omaps_.end())
+        it = omaps_.emplace(okey, output_map(out, epi, type16(bf16()), M, N, ldc, w_f8)).first;
     if (w_f8)
         launch_gemm<__nv_fp8_e4m3, __nv_bfloat16>(epi, bn, ma, mb, it->second, M, N, K, ep, err_word(), num_sms_, s);
     else if (bf16())
