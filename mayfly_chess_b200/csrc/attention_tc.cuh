@@ -318,20 +318,23 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ 
 }
 
 // ------------------------------------------------------------------------------------------------ four groups
-// The same arithmetic with four softmax groups of 4 warps (576 threads), group n % 4 taking item n and finishing
-// it before it takes the next: S(n) -> softmax -> P over the Q tile -> (PV(n) on the tensor cores) -> O(n)
-// normalised and stored -> slots handed back. Four items are in flight instead of two and twice as many warps
-// hide each other's latencies. Item n's scores and output live in tensor-memory slot n % NS (NS = 5 slots of 96
-// columns, S taking 80 and O 64 of them): one more slot than groups, so the S product of a group's next item
-// runs while the group still works on its current one. Registers are tighter (112 a
-// thread), so a row's scores are read from tensor memory twice, 32 columns at a time: once for the row max, once
-// for the exponentials. The MMA thread issues whichever of the next S (its load landed, its group's slot free)
-// and the next PV (its P written) is ready first, polling with mbarrier.test_wait (which never suspends the
-// thread on one barrier while the other is ready); it gives up after the wait limit with no progress.
+// The same arithmetic with four softmax groups, group n % 4 taking item n and finishing it before it takes the
+// next: S(n) -> softmax -> P over the Q tile -> (PV(n) on the tensor cores) -> O(n) normalised and stored ->
+// slots handed back. Four items are in flight instead of two. A group is the 3 warps whose tensor-memory lane
+// quarters hold the 65 live query rows (rows 0..95; rows 96..127 are padding, so no warp reads them): warps
+// 4g, 4g + 1, 4g + 2 of the 16 (512 threads); warp 3 issues the TMA loads, warp 7 owns tensor memory and
+// issues the MMAs, warps 11 and 15 have no role. With 16 warps a thread may hold 128 registers, so a row's 80
+// scores come out of tensor memory in one pass (three loads, one wait), and its 64 outputs in another. Item n's
+// scores and output live in tensor-memory slot n % NS (NS = 5 slots of 96 columns, S taking 80 and O 64 of
+// them): one more slot than groups, so the S product of a group's next item runs while the group still works on
+// its current one. The MMA thread issues whichever of the next S (its load landed, its slot free) and the next
+// PV (its P written) is ready first, polling with mbarrier.test_wait (which never suspends the thread on one
+// barrier while the other is ready); it gives up after the wait limit with no progress.
 struct AttTc4Cfg {
     static constexpr int DH = 64;
     static constexpr int LS = 6;
     static constexpr int G = 4;                              // softmax groups
+    static constexpr int GW = 3;                             // warps a group (lane quarters 0..2)
     static constexpr int NS = 5;                             // tensor-memory slots
     static constexpr int KEYS = 80;
     static constexpr uint32_t Q_BYTES = 128 * 128;
@@ -340,12 +343,14 @@ struct AttTc4Cfg {
     static constexpr uint32_t LOAD_SLOT = V_OFF + KV_BYTES;
     static constexpr uint32_t LOAD_BYTES = 3 * KEYS * 128;
     static constexpr size_t SMEM = 1024 + LS * (size_t)LOAD_SLOT + 512;
-    static constexpr int THREADS = 64 + 128 * G;
+    static constexpr int THREADS = 512;
+    static constexpr int LOAD_WARP = 3, MMA_WARP = 7;        // warps of lane quarter 3, which holds no live row
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr uint32_t T_STRIDE = 96;
     static_assert(LOAD_SLOT % 1024 == 0 && K_OFF % 1024 == 0 && V_OFF % 1024 == 0, "1024-byte aligned tiles");
     static_assert(NS * T_STRIDE <= TMEM_COLS && T_STRIDE >= KEYS && NS > G && SMEM <= 232448, "resources");
     static_assert((2 * LS + 3 * NS + G + 1) * 8 + 4 + 8 * G <= 512, "barriers");
+    static_assert(G * 4 * 32 == THREADS && GW * 32 > kTokens, "warp roles");
 };
 
 template <typename T, typename TO>
@@ -354,20 +359,21 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
                      float scale, float mul, uint32_t* err)
 {
     using C = AttTc4Cfg;
-    constexpr int LS = C::LS, G = C::G, NS = C::NS;
+    constexpr int LS = C::LS, G = C::G, NS = C::NS, GW = C::GW;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(base + LS * C::LOAD_SLOT);   // [LS] Q, K, V landed
-    uint64_t* empty = full + LS;     // [LS] the load slot is finished with (its group's 4 warps)
+    uint64_t* empty = full + LS;     // [LS] the load slot is finished with (its group's warps)
     uint64_t* sfull = empty + LS;    // [NS] S in the tensor-memory slot
     uint64_t* ofull = sfull + NS;    // [NS] O in the slot
-    uint64_t* tfree = ofull + NS;    // [NS] the slot is read (4 warps)
-    uint64_t* pready = tfree + NS;   // [G] the group's P in shared memory (4 warps)
+    uint64_t* tfree = ofull + NS;    // [NS] the slot is read (its group's warps)
+    uint64_t* pready = tfree + NS;   // [G] the group's P in shared memory (its warps)
     uint64_t* mma_done = pready + G;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile uint32_t* ok = tmem_slot + 1;   // [G x 2]: the leaders' broadcasts
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int quarter = warp & 3;
     const int items = B * heads;
     const int my = (int)blockIdx.x < items ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
@@ -380,19 +386,19 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
     if (threadIdx.x == 0) {
         for (int i = 0; i < LS; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 4);
+            mbar_init(&empty[i], GW);
         }
         for (int i = 0; i < NS; ++i) {
             mbar_init(&sfull[i], 1);
             mbar_init(&ofull[i], 1);
-            mbar_init(&tfree[i], 4);
+            mbar_init(&tfree[i], GW);
         }
-        for (int i = 0; i < G; ++i) mbar_init(&pready[i], 4);
+        for (int i = 0; i < G; ++i) mbar_init(&pready[i], GW);
         mbar_init(mma_done, 1);
         fence_barrier_init();
         tma_prefetch_desc(&tmQKV);
     }
-    if (warp == 1) {
+    if (warp == C::MMA_WARP) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
         tmem_relinquish();
     }
@@ -403,7 +409,7 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
     griddep_wait();
     if (threadIdx.x == 0) griddep_launch();
 
-    if (warp == 0) {
+    if (warp == C::LOAD_WARP) {
         // ---------------------------------------------------------------- TMA producer
         if (lane == 0) {
             uint32_t issued = 0, issued_par = 0;
@@ -423,7 +429,7 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
             for (int sl = 0; sl < LS; ++sl)
                 if (issued & (1u << sl)) mbar_wait(&full[sl], (issued_par >> sl) & 1, err, kErrTmaFull);
         }
-    } else if (warp == 1) {
+    } else if (warp == C::MMA_WARP) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t idS = Operand<T>::idesc(128, C::KEYS);
@@ -476,13 +482,11 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
             umma_commit(mma_done);
             mbar_wait(mma_done, 0, err, kErrTmemFull);
         }
-    } else {
+    } else if (quarter < GW) {
         // ---------------------------------------------------------------- softmax and output (four groups)
-        const int grp = (warp - 2) >> 2;
-        const int quarter = warp & 3;
+        const int grp = warp >> 2;
         const int row = quarter * 32 + lane;
-        const bool live = quarter < 3;                   // rows 96..127 are padding
-        const bool leader = threadIdx.x == 64 + 128 * grp;
+        const bool leader = threadIdx.x == 128 * grp;
         const uint32_t bar_id = 1 + grp;
         const float sl2 = scale * 1.4426950408889634f;
         for (int n = grp; n < my; n += G) {
@@ -490,43 +494,32 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
             const uint32_t par = (n / NS) & 1;   // the phase of item n's tensor-memory slot
             const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + C::T_STRIDE * ts;
             if (leader) ok[2 * grp] = mbar_wait(&sfull[ts], par, err, kErrTmemFull) ? 1u : 0u;
-            named_barrier(bar_id, 128);
+            named_barrier(bar_id, 32 * GW);
             if (!ok[2 * grp]) break;
-            float p64 = 0.f, sum = 0.f;
-            if (live) {
-                tc_fence_after();
-                uint32_t r[32];
-                // pass 1: the row max over the 65 live keys (and key 64's score, kept)
-                float m = -INFINITY, s64;
-                {
-                    uint32_t r16[16];
-                    tmem_ld_32x32b_x16(t_row + 64, r16);
-                    tmem_ld_wait();
-                    s64 = __uint_as_float(r16[0]);
-                    m = s64;
-                }
+            tc_fence_after();
+            float p64, sum;
+            {
+                // the row's 80 scores in one pass: keys 0..63, then 64.. (key 64 the last live one)
+                uint32_t r[64], r16[16];
+                tmem_ld_32x32b_x32(t_row, reinterpret_cast<uint32_t(&)[32]>(r[0]));
+                tmem_ld_32x32b_x32(t_row + 32, reinterpret_cast<uint32_t(&)[32]>(r[32]));
+                tmem_ld_32x32b_x16(t_row + 64, r16);
+                tmem_ld_wait();
+                const float s64 = __uint_as_float(r16[0]);
+                float m4[4] = {s64, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    tmem_ld_32x32b_x32(t_row + 32 * hh, r);
-                    tmem_ld_wait();
-                    float m4[4] = {m, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(r[j]));
-                    m = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-                }
-                const float mc = m * sl2;
-                // pass 2: exponentials, their sum, P (rounded to T) over the Q tile
+                for (int j = 0; j < 64; ++j) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(r[j]));
+                const float mc = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+                // exponentials, their sum, P (rounded to T) over the Q tile
                 uint8_t* pb = base + ls * C::LOAD_SLOT + C::Q_OFF;
                 float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
-                    tmem_ld_32x32b_x32(t_row + 32 * hh, r);
-                    tmem_ld_wait();
                     uint32_t pk[16];
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
-                        const float p0 = ex2_approx(fmaf(__uint_as_float(r[j]), sl2, -mc));
-                        const float p1 = ex2_approx(fmaf(__uint_as_float(r[j + 1]), sl2, -mc));
+                        const float p0 = ex2_approx(fmaf(__uint_as_float(r[32 * hh + j]), sl2, -mc));
+                        const float p1 = ex2_approx(fmaf(__uint_as_float(r[32 * hh + j + 1]), sl2, -mc));
                         pk[j / 2] = pack2<T>(p0, p1);
                         s4[(j / 2) & 3] += p0 + p1;
                     }
@@ -537,26 +530,27 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
                 }
                 p64 = ex2_approx(fmaf(s64, sl2, -mc));
                 sum = ((s4[0] + s4[1]) + (s4[2] + s4[3])) + p64;
-                fence_proxy_async_smem();   // the MMA (async proxy) reads what these generic stores wrote
-                tc_fence_before();          // and overwrites the S columns this thread has read
             }
+            fence_proxy_async_smem();   // the MMA (async proxy) reads what these generic stores wrote
+            tc_fence_before();          // and overwrites the S columns this thread has read
             __syncwarp();
             if (lane == 0) mbar_arrive(&pready[grp]);
             if (leader) ok[2 * grp + 1] = mbar_wait(&ofull[ts], par, err, kErrTmemFull) ? 1u : 0u;
-            named_barrier(bar_id, 128);
+            named_barrier(bar_id, 32 * GW);
             if (!ok[2 * grp + 1]) break;
-            if (live) {
-                tc_fence_after();
+            tc_fence_after();
+            {
                 const float inv = 1.f / sum;
                 const uint4* v64 = reinterpret_cast<const uint4*>(base + ls * C::LOAD_SLOT + C::V_OFF + 64 * 128);
                 const int item = (int)blockIdx.x + n * (int)gridDim.x;
                 const int b = item / heads, h = item - b * heads;
                 const size_t orow = (size_t)b * kTokens + row;
+                uint32_t r[64];
+                tmem_ld_32x32b_x32(t_row, reinterpret_cast<uint32_t(&)[32]>(r[0]));
+                tmem_ld_32x32b_x32(t_row + 32, reinterpret_cast<uint32_t(&)[32]>(r[32]));
+                tmem_ld_wait();
 #pragma unroll
                 for (int qq = 0; qq < 4; ++qq) {   // 16 output columns at a time
-                    uint32_t r[16];
-                    tmem_ld_32x32b_x16(t_row + 16 * qq, r);
-                    tmem_ld_wait();
                     float o[16];
 #pragma unroll
                     for (int u = 0; u < 2; ++u) {
@@ -565,9 +559,10 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             const int c = 8 * u + 2 * i;
-                            o[c] = fmaf(p64, to_f32<T>(reinterpret_cast<const T*>(&w[i])[0]), __uint_as_float(r[c])) * inv;
+                            o[c] = fmaf(p64, to_f32<T>(reinterpret_cast<const T*>(&w[i])[0]),
+                                        __uint_as_float(r[16 * qq + c])) * inv;
                             o[c + 1] = fmaf(p64, to_f32<T>(reinterpret_cast<const T*>(&w[i])[1]),
-                                            __uint_as_float(r[c + 1])) * inv;
+                                            __uint_as_float(r[16 * qq + c + 1])) * inv;
                         }
                     }
                     if (row < kTokens) {
@@ -605,7 +600,7 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+    if (warp == C::MMA_WARP) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
 }  // namespace mf
