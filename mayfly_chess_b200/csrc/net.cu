@@ -310,8 +310,11 @@ static void launch_gemm_pair_if(const CUtensorMap& ma, const CUtensorMap& mb, co
 
 // Tile choice: kPairTile (a CTA pair per 256 x 256 tile) when there are at least as many pair tiles as pairs
 // fit and the epilogue is light next to the MMAs (bias-only, f32 outputs, the residuals' TMA reductions, or
-// K >= 2048: measured on a B200, the pair kernel is faster for qkv, out and ff2 and slower for ff1, whose GELU
-// epilogue gates both CTAs of a pair), else the widest single-CTA
+// K >= 2048), or, for the 16-bit GELU epilogue, when every pair gets at least four tiles (measured on a B200 in
+// the graph pass: ff1 on pairs +1.3% positions/s for the bf16 pass at B = 1,024 and 4,096, though its eager
+// per-step time reads a little slower: the single-CTA kernel is bound by shared-memory bandwidth near two thirds
+// of the tensor rate, a pair near four fifths; the FP8 ff1, whose MMAs take half as long, stays single, its
+// GELU epilogue exposed on pairs: -1% to +0.8% across runs), else the widest single-CTA
 // tile that still gives two thirds of the SMs a tile. A launch costs ~10 us however small it is, so at small M
 // fewer, wider tiles win while most SMs are busy (measured, back-to-back launches: M = 4,160, the out product
 // 14.4 us with 132 tiles of 256 against 18.2 with 264 of 128; ff2 20.5 against 28.3); below that the weights
@@ -335,7 +338,10 @@ static int pick_bn(int M, int N, int K, int epi, int num_sms)
 {
     const int mode = tile_mode();
     const bool light = epi == kEpiBias || epi == kEpiF32 || epi == kEpiResidual || epi == kEpiResidual16 || K >= 2048;
-    if (mode == 1 || (mode == 0 && light && ((M + 255) / 256) * ((N + 255) / 256) >= num_sms / 2)) return kPairTile;
+    const int pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    const bool gelu16 = epi == kEpiBiasGelu;
+    if (mode == 1 || (mode == 0 && (light ? pair_tiles >= num_sms / 2 : gelu16 && pair_tiles >= 2 * num_sms)))
+        return kPairTile;
     const int m_tiles = (M + 127) / 128;
     for (int bn : {256, 128})
         if (3 * m_tiles * ((N + bn - 1) / bn) >= 2 * num_sms) return bn;
