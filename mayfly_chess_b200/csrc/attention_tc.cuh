@@ -540,7 +540,7 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
             if (!ok[2 * grp + 1]) break;
             tc_fence_after();
             {
-                const float inv = 1.f / sum;
+                const float inv = (is_e4m3<TO> ? mul : 1.f) / sum;   // e4m3: att * mul, folded into 1 / sum
                 const uint4* v64 = reinterpret_cast<const uint4*>(base + ls * C::LOAD_SLOT + C::V_OFF + 64 * 128);
                 const int item = (int)blockIdx.x + n * (int)gridDim.x;
                 const int b = item / heads, h = item - b * heads;
@@ -572,8 +572,7 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
                             uint32_t w[4];
 #pragma unroll
                             for (int i = 0; i < 4; ++i)
-                                w[i] = pack_e4m3x4(o[4 * i] * mul, o[4 * i + 1] * mul, o[4 * i + 2] * mul,
-                                                   o[4 * i + 3] * mul);
+                                w[i] = pack_e4m3x4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
                             dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
                         } else {
                             uint4* dst = reinterpret_cast<uint4*>(att + orow * d + (size_t)h * C::DH + 16 * qq);
