@@ -500,15 +500,18 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
             float p64, sum;
             {
                 // the row's 80 scores in one pass: keys 0..63, then 64.. (key 64 the last live one)
-                uint32_t r[64], r16[16];
-                tmem_ld_32x32b_x32(t_row, reinterpret_cast<uint32_t(&)[32]>(r[0]));
-                tmem_ld_32x32b_x32(t_row + 32, reinterpret_cast<uint32_t(&)[32]>(r[32]));
+                uint32_t ra[32], rb[32], r16[16];   // keys 0..31, 32..63, 64..79
+                tmem_ld_32x32b_x32(t_row, ra);
+                tmem_ld_32x32b_x32(t_row + 32, rb);
                 tmem_ld_32x32b_x16(t_row + 64, r16);
                 tmem_ld_wait();
                 const float s64 = __uint_as_float(r16[0]);
                 float m4[4] = {s64, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int j = 0; j < 64; ++j) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(r[j]));
+                for (int j = 0; j < 32; ++j) {
+                    m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(ra[j]));
+                    m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(rb[j]));
+                }
                 const float mc = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
                 // exponentials, their sum, P (rounded to T) over the Q tile
                 uint8_t* pb = base + ls * C::LOAD_SLOT + C::Q_OFF;
@@ -518,8 +521,9 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
                     uint32_t pk[16];
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
-                        const float p0 = ex2_approx(fmaf(__uint_as_float(r[32 * hh + j]), sl2, -mc));
-                        const float p1 = ex2_approx(fmaf(__uint_as_float(r[32 * hh + j + 1]), sl2, -mc));
+                        const uint32_t* rh = hh == 0 ? ra : rb;
+                        const float p0 = ex2_approx(fmaf(__uint_as_float(rh[j]), sl2, -mc));
+                        const float p1 = ex2_approx(fmaf(__uint_as_float(rh[j + 1]), sl2, -mc));
                         pk[j / 2] = pack2<T>(p0, p1);
                         s4[(j / 2) & 3] += p0 + p1;
                     }
@@ -545,9 +549,9 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
                 const int item = (int)blockIdx.x + n * (int)gridDim.x;
                 const int b = item / heads, h = item - b * heads;
                 const size_t orow = (size_t)b * kTokens + row;
-                uint32_t r[64];
-                tmem_ld_32x32b_x32(t_row, reinterpret_cast<uint32_t(&)[32]>(r[0]));
-                tmem_ld_32x32b_x32(t_row + 32, reinterpret_cast<uint32_t(&)[32]>(r[32]));
+                uint32_t ra[32], rb[32];   // output columns 0..31, 32..63
+                tmem_ld_32x32b_x32(t_row, ra);
+                tmem_ld_32x32b_x32(t_row + 32, rb);
                 tmem_ld_wait();
 #pragma unroll
                 for (int qq = 0; qq < 4; ++qq) {   // 16 output columns at a time
@@ -560,9 +564,9 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
                         for (int i = 0; i < 4; ++i) {
                             const int c = 8 * u + 2 * i;
                             o[c] = fmaf(p64, to_f32<T>(reinterpret_cast<const T*>(&w[i])[0]),
-                                        __uint_as_float(r[16 * qq + c])) * inv;
+                                        __uint_as_float((qq < 2 ? ra : rb)[16 * (qq & 1) + c])) * inv;
                             o[c + 1] = fmaf(p64, to_f32<T>(reinterpret_cast<const T*>(&w[i])[1]),
-                                            __uint_as_float(r[16 * qq + c + 1])) * inv;
+                                            __uint_as_float((qq < 2 ? ra : rb)[16 * (qq & 1) + c + 1])) * inv;
                         }
                     }
                     if (row < kTokens) {
