@@ -64,6 +64,9 @@
 #ifndef MF_F8_BIAS_NBUF
 #define MF_F8_BIAS_NBUF 1
 #endif
+#ifndef MF_EPI_BATCH
+#define MF_EPI_BATCH 1
+#endif
 
 namespace mf {
 
@@ -145,7 +148,11 @@ template <int BN, int EPI, bool PAIR = false, bool F8 = false> struct GemmCfg {
     // 4 x 1).
     static constexpr int EG = EPI == kEpiResidual ? ((NC % MF_REDUCE_EG == 0) ? MF_REDUCE_EG : 1)
                               : ((HEAVY || NARROW) && NC % 4 == 0) ? 4 : (NC % 2 == 0 ? 2 : 1);
-    static constexpr int NBUF = EPI == kEpiResidual ? MF_REDUCE_NBUF
+    // the FP8 bias epilogue with several chunks a group (MF_EPI_BATCH): one staging buffer per chunk, so a group
+    // writes all its chunks of a tile before one proxy fence and one barrier, then stores them
+    static constexpr bool BATCH = MF_EPI_BATCH && F8_BIAS && NC / EG > 1;
+    static constexpr int NBUF = BATCH ? NC / EG
+                                : EPI == kEpiResidual ? MF_REDUCE_NBUF
                                 : F8_BIAS ? MF_F8_BIAS_NBUF : (EG >= 2 ? 1 : 2);   // staging buffers a group
     static constexpr uint32_t A_BYTES = BM * 128;
     static constexpr uint32_t B_BYTES = B_ROWS * 128;
@@ -451,14 +458,18 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                     for (int i = 0; i < 16; ++i) q[16 * p + i] = pack2<__nv_bfloat16>(v[2 * i], v[2 * i + 1]);
                 }
             }
-            // the staging buffer (per-warp stores: this warp's rows of it) must no longer be read by its last store
+            // the staging buffer (per-warp stores: this warp's rows of it) must no longer be read by its last store;
+            // batched: once a tile, before the first chunk, for all of the group's buffers
             constexpr bool WARP_STORE = C::STORE_ROWS == 32;
-            if constexpr (WARP_STORE) {
-                if (lane == 0) bulk_wait_read<C::NBUF - 1>();
-                __syncwarp();
-            } else {
-                if (leader) bulk_wait_read<C::NBUF - 1>();
-                named_barrier(bar_id, 128);
+            if (!C::BATCH || ci == 0) {
+                constexpr int AHEAD = C::BATCH ? 0 : C::NBUF - 1;
+                if constexpr (WARP_STORE) {
+                    if (lane == 0) bulk_wait_read<AHEAD>();
+                    __syncwarp();
+                } else {
+                    if (leader) bulk_wait_read<AHEAD>();
+                    named_barrier(bar_id, 128);
+                }
             }
             constexpr int RB = C::ROW_BYTES;
             if constexpr (C::OUT_BYTES == 4) {
@@ -472,19 +483,31 @@ __device__ __forceinline__ void epilogue_loop(const SmemLayout<C>& L, const CUte
                     *reinterpret_cast<uint4*>(buf + swz<RB>(row, j)) =
                         make_uint4(q[4 * j], q[4 * j + 1], q[4 * j + 2], q[4 * j + 3]);
             }
+            if (C::BATCH && ci < CPG - 1) continue;   // batched: the fence and the stores after the last chunk
             fence_proxy_async_smem();
+            constexpr int NST = C::BATCH ? CPG : 1;   // chunks this fence covers: ci - NST + 1 .. ci
             if constexpr (WARP_STORE) {
                 __syncwarp();
                 const int wrow = row0 + quarter * 32;   // this warp's first output row
                 if (lane == 0 && wrow < M) {
-                    tma_store_2d(tmC, buf + quarter * 32 * RB, col0, wrow);
+#pragma unroll
+                    for (int k = 0; k < NST; ++k) {
+                        const int cc = grp + (ci - NST + 1 + k) * C::EG;
+                        tma_store_2d(tmC, gbuf + ((g - NST + 1 + k) % C::NBUF) * C::CHUNK_BYTES + quarter * 32 * RB,
+                                     colb + cc * C::CHUNK_COLS, wrow);
+                    }
                     bulk_commit();
                 }
             } else {
                 named_barrier(bar_id, 128);
                 if (leader) {
-                    if constexpr (C::REDUCE) tma_reduce_add_2d(tmC, buf, col0, row0);   // X += v
-                    else tma_store_2d(tmC, buf, col0, row0);
+#pragma unroll
+                    for (int k = 0; k < NST; ++k) {
+                        const int cc = grp + (ci - NST + 1 + k) * C::EG;
+                        uint8_t* sb = gbuf + ((g - NST + 1 + k) % C::NBUF) * C::CHUNK_BYTES;
+                        if constexpr (C::REDUCE) tma_reduce_add_2d(tmC, sb, colb + cc * C::CHUNK_COLS, row0);   // X += v
+                        else tma_store_2d(tmC, sb, colb + cc * C::CHUNK_COLS, row0);
+                    }
                     bulk_commit();
                 }
             }
