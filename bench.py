@@ -58,7 +58,7 @@ sys.path.insert(0, REPO)
 
 METRIC = "NN positions evaluated/sec (146M trunk, bs1024, 1/2/4/8 B200); p50 latency at bs64"
 # DRAM bytes (read + write) of one qkv launch per position, from the ncu captures in profiles/
-# (gemm_qkv_pair_bf16_b1024.md: 142.9 + 355.6 MB at B = 1,024; gemm_qkv_pair_e4m3_b1024.md: 71.5 + 355.7 MB)
+# (the qkv product's ncu captures at B = 1,024: 142.9 + 355.6 MB in bf16, 71.5 + 355.7 MB with e4m3 operands)
 QKV_TRAFFIC_PER_POS = {"bf16": (142905088 + 355564544) / 1024, "e4m3": (71474944 + 355708928) / 1024}
 CALIB_ROWS = (7936, 8192)   # positions_seed1.npz rows the e4m3 input scales are calibrated on
 POSITIONS = os.path.join(REPO, "tests", "golden", "positions_seed1.npz")
