@@ -30,6 +30,8 @@ independent evaluator per GPU, no collective on the data path (weak scaling: 1,0
              ranks); at N > 1 rank 0 also times all 8,192 alone, and efficiency = value / (N x that).
   latency_sweep  BASELINE config 3: p50 / p99 per call through CudaNet.evaluate at B = 1, 16, 64, 128, 256 and
              the weight stream's GB/s (bytes of the weights / p50).
+  ranks      at N > 1: every rank's device time of the timed region and median SM clock, and the straggler (the
+             rank with the longest time, which sets `value`).
   cpu_baseline  the CPU fp32 restatement of the reference forward (oracle/, test infrastructure) on this host's
              cores: the median of 5 calls on 64 positions after 2 warm-up calls.
 
@@ -461,9 +463,19 @@ def main():
     barrier()
     clk = clocks.stop(w0, time.monotonic())
     net.check(s)
-    dev_ms = e0.elapsed_time(e1)
-    dev_ms = max_over_ranks(dev_ms)
+    own_ms = e0.elapsed_time(e1)
+    dev_ms = max_over_ranks(own_ms)
     value = world * B * args.steps / (dev_ms / 1000.0)
+    ranks = None
+    if world > 1:
+        # every rank's device time and median SM clock, and the straggler (the rank whose time is the job's)
+        mine = torch.tensor([own_ms, float(clk.get("sm_mhz") or 0.0)], dtype=torch.float64, device="cuda")
+        every = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        rows = [t.tolist() for t in every]
+        slow = max(range(world), key=lambda r: rows[r][0])
+        ranks = {"ms": [round(r[0], 3) for r in rows], "sm_mhz": [r[1] for r in rows],
+                 "straggler": {"rank": slow, "ms": round(rows[slow][0], 3), "sm_mhz": rows[slow][1]}}
 
     # ---------------------------------------------------------------- e2e: host arrays through the C ABI
     for _ in range(2):
@@ -670,6 +682,7 @@ def main():
                  "frac_whole_pass": fl_pos * value / world / 1e12 / peak, "profile_ms": prof},
         "p50_latency_ms_bs64": sweep.get("64", {}).get("p50_ms"),
         "clocks": clk,
+        "ranks": ranks,
         "parity": parity,
         "fp8": fp8,
         "strong": strong,
