@@ -356,7 +356,7 @@ struct AttTc4Cfg {
 template <typename T, typename TO>
 __global__ void __launch_bounds__(AttTc4Cfg::THREADS, 1)
 attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__ att, int B, int heads, int d,
-                     float scale, float mul, uint32_t* err)
+                     float scale, float mul, uint32_t* err, int rev)
 {
     using C = AttTc4Cfg;
     constexpr int LS = C::LS, G = C::G, NS = C::NS, GW = C::GW;
@@ -417,7 +417,8 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
                 const int ls = n % LS, use = n / LS;
                 if (use > 0 && !mbar_wait(&empty[ls], (use - 1) & 1, err, kErrSmemEmpty)) break;
                 const int item = (int)blockIdx.x + n * (int)gridDim.x;
-                const int b = item / heads, h = item - b * heads;
+                const int bf = item / heads, h = item - bf * heads;
+                const int b = rev ? B - 1 - bf : bf;   // rev: boards in descending order
                 uint8_t* sb = base + ls * C::LOAD_SLOT;
                 mbar_arrive_expect_tx(&full[ls], C::LOAD_BYTES);
                 tma_load_2d(sb + C::Q_OFF, &tmQKV, &full[ls], h * C::DH, b * kTokens);
@@ -547,7 +548,8 @@ attention_tc4_kernel(const __grid_constant__ CUtensorMap tmQKV, TO* __restrict__
                 const float inv = (is_e4m3<TO> ? mul : 1.f) / sum;   // e4m3: att * mul, folded into 1 / sum
                 const uint4* v64 = reinterpret_cast<const uint4*>(base + ls * C::LOAD_SLOT + C::V_OFF + 64 * 128);
                 const int item = (int)blockIdx.x + n * (int)gridDim.x;
-                const int b = item / heads, h = item - b * heads;
+                const int bf = item / heads, h = item - bf * heads;
+                const int b = rev ? B - 1 - bf : bf;
                 const size_t orow = (size_t)b * kTokens + row;
                 uint32_t ra[32], rb[32];   // output columns 0..31, 32..63
                 tmem_ld_32x32b_x32(t_row, ra);

@@ -115,6 +115,7 @@ struct EpiArgs {
     const float* bias;
     const float* colscale;   // nullptr: no scaling (16-bit operands)
     float out_scale_inv;     // kEpiGeluE4m3 only
+    int rev;                 // 1: the M blocks in descending order (the output is the same)
 };
 
 // PAIR: the CTA-pair kernel, where a CTA loads BN/2 rows of W per stage and a pair covers 256 rows of M.
@@ -577,7 +578,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
             griddep_wait();
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
+                const int m_fwd = tile / n_tiles, n_blk = tile % n_tiles;
+                const int m_blk = ep.rev ? m_tiles - 1 - m_fwd : m_fwd;
                 for (int kb = 0; kb < k_iters; ++kb) {
                     if (!mbar_wait(&L.empty[stage], phase ^ 1u, err, kErrSmemEmpty)) {
                         ok = false;
@@ -645,7 +647,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
         epilogue_loop<T, EPI, C>(
             L, &tmC, tmem_base, my_tiles,
-            [&](int it) { return (((int)blockIdx.x + it * (int)gridDim.x) / n_tiles) * C::BM; },
+            [&](int it) {
+                const int m_fwd = ((int)blockIdx.x + it * (int)gridDim.x) / n_tiles;
+                return (ep.rev ? m_tiles - 1 - m_fwd : m_fwd) * C::BM;
+            },
             [&](int it) { return (((int)blockIdx.x + it * (int)gridDim.x) % n_tiles) * BN; },
             [&](int acc) { mbar_arrive(&L.tempty[acc]); }, ep, M, N, err);
     }
@@ -721,7 +726,8 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             }
             griddep_wait();
             for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
-                const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
+                const int m_fwd = tile / n_tiles, n_blk = tile % n_tiles;
+                const int m_blk = ep.rev ? m_tiles - 1 - m_fwd : m_fwd;
                 const int a_row = m_blk * 2 * C::BM + (int)rank * C::BM;
                 const int b_row = n_blk * BN + (int)rank * C::B_ROWS;
                 for (int kb = 0; kb < k_iters; ++kb) {
@@ -801,7 +807,10 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         const uint32_t tempty_lead1 = mapa_shared(smem_u32(&L.tempty[1]), 0);
         epilogue_loop<T, EPI, C>(
             L, &tmC, tmem_base, my_tiles,
-            [&](int it) { return ((pair + it * num_pairs) / n_tiles) * 2 * C::BM + (int)rank * C::BM; },
+            [&](int it) {
+                const int m_fwd = (pair + it * num_pairs) / n_tiles;
+                return (ep.rev ? m_tiles - 1 - m_fwd : m_fwd) * 2 * C::BM + (int)rank * C::BM;
+            },
             [&](int it) { return ((pair + it * num_pairs) % n_tiles) * BN; },
             [&](int acc) { mbar_arrive_cluster(acc ? tempty_lead1 : tempty_lead0); }, ep, M, N, err);
     }

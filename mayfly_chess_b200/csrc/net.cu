@@ -383,13 +383,16 @@ static void launch_gemm(int epi, int bn, const CUtensorMap& ma, const CUtensorMa
 // h = LN(x) in T (16-bit, or e4m3 of h * mul), x f32 or bf16 (XT)
 template <typename T, typename XT = float>
 static void launch_layernorm(const XT* x, const float* g, const float* b, T* h, int n, int d, int row_stride,
-                             float mul, cudaStream_t s)
+                             float mul, cudaStream_t s, int rev = 0)
 {
     const dim3 grid((n + 7) / 8), block(256);
     switch (d) {
-        case 256: launch_k(layernorm_kernel<T, 2, XT>, grid, block, 0, s, x, g, b, h, n, row_stride, 1e-5f, mul); break;
-        case 512: launch_k(layernorm_kernel<T, 4, XT>, grid, block, 0, s, x, g, b, h, n, row_stride, 1e-5f, mul); break;
-        case 1024: launch_k(layernorm_kernel<T, 8, XT>, grid, block, 0, s, x, g, b, h, n, row_stride, 1e-5f, mul); break;
+        case 256: launch_k(layernorm_kernel<T, 2, XT>, grid, block, 0, s, x, g, b, h, n, row_stride, 1e-5f, mul, rev);
+            break;
+        case 512: launch_k(layernorm_kernel<T, 4, XT>, grid, block, 0, s, x, g, b, h, n, row_stride, 1e-5f, mul, rev);
+            break;
+        case 1024: launch_k(layernorm_kernel<T, 8, XT>, grid, block, 0, s, x, g, b, h, n, row_stride, 1e-5f, mul, rev);
+            break;
         default: throw std::runtime_error("cudanet_b200: width must be 256, 512 or 1024");
     }
 }
@@ -455,7 +458,7 @@ static int att_tc_mode()
 
 template <typename T, typename TO>
 static void launch_attention_tc4(const CUtensorMap& map, TO* att, int B, int d, int heads, float mul, uint32_t* err,
-                                 cudaStream_t s)
+                                 cudaStream_t s, int rev = 0)
 {
     using C = AttTc4Cfg;
     static bool attr[64] = {};
@@ -471,7 +474,7 @@ static void launch_attention_tc4(const CUtensorMap& map, TO* att, int B, int d, 
     const int items = B * heads;
     const float scale = 1.0f / std::sqrt(static_cast<float>(C::DH));
     launch_k(attention_tc4_kernel<T, TO>, dim3(std::min(items, sms[dev])), dim3(C::THREADS), C::SMEM, s, map, att, B,
-             heads, d, scale, mul, err);
+             heads, d, scale, mul, err, rev);
 }
 
 // the tcgen05 attention (attention_tc.cuh): one CTA per SM, persistent over the (board, head) items
@@ -496,16 +499,17 @@ static void launch_attention_tc(const CUtensorMap& map, TO* att, int B, int d, i
              heads, d, scale, mul, err);
 }
 
-// att = attention(qkv) in TO (T, or e4m3 of att * mul); map from qkv_map over at least B * 65 rows
+// att = attention(qkv) in TO (T, or e4m3 of att * mul); map from qkv_map over at least B * 65 rows. rev: the
+// boards in descending order, where the kernel supports it (the four-group kernel); the output is the same.
 template <typename T, typename TO>
 static void launch_attention(const CUtensorMap& map, TO* att, int B, int d, int heads, float mul, uint32_t* err,
-                             cudaStream_t s, int mode_override = -2)
+                             cudaStream_t s, int mode_override = -2, int rev = 0)
 {
     if (B < 1 || heads < 1 || d % heads) throw std::runtime_error("cudanet_b200: bad attention sizes");
     const int dh = d / heads;
     const int mode = mode_override != -2 ? mode_override : att_tc_mode();
     const int pick = mode >= 0 ? mode : 4;
-    if (dh == 64 && pick == 4) launch_attention_tc4<T, TO>(map, att, B, d, heads, mul, err, s);
+    if (dh == 64 && pick == 4) launch_attention_tc4<T, TO>(map, att, B, d, heads, mul, err, s, rev);
     else if (dh == 64 && pick == 1) launch_attention_tc<T, TO>(map, att, B, d, heads, mul, err, s);
     else if (dh == 64) launch_attention_dh<T, TO, 64>(map, att, B, d, heads, mul, err, s);
     else if (dh == 32) launch_attention_dh<T, TO, 32>(map, att, B, d, heads, mul, err, s);
@@ -1145,14 +1149,19 @@ template <typename T> void Net::forward_t(int B, cudaStream_t s)
     mark(kPEmbed, s);
     launch_embed_ln<T>(w_, L_[0], d_in_, B, x_, h, 1.f, s);
     const bool fuse = fuse_ln() && !amax_;
+    // Each kernel of the chain walks its rows in the opposite order to the kernel that wrote its input, so it
+    // starts on what is still in L2 (the producer's last rows); the outputs do not depend on the order.
+    int dir = 0;
+    auto flip = [&] { return dir ^= 1; };
     for (int i = 0; i < a.layers; ++i) {
         const LayerW& l = L_[static_cast<size_t>(i)];
         const bool last = i + 1 == a.layers;
         mark(kPLn1, s);
-        if (i > 0 && !fuse) launch_layernorm<T>(x_, l.n1_g, l.n1_b, h, rows, d, 1, 1.f, s);
+        if (i > 0 && !fuse) launch_layernorm<T>(x_, l.n1_g, l.n1_b, h, rows, d, 1, 1.f, s, flip());
         amax(4 * i + 0, h, nd, s);
         mark(kPQkv, s);
-        gemm(kEpiBias, map_h_, l.qkv_w, false, rows, 3 * d, d, EpiArgs{l.qkv_b, nullptr, 1.f}, qkv_, 3 * d, s);
+        gemm(kEpiBias, map_h_, l.qkv_w, false, rows, 3 * d, d, EpiArgs{l.qkv_b, nullptr, 1.f, flip()}, qkv_, 3 * d,
+             s);
         mark(kPAtt, s);
         if (last && cls_only() && !amax_) {
             // the CLS rows only (cls_only): dense [B, ...] operands in att_, h_, ff_; x's CLS rows at pitch 65 d
@@ -1168,26 +1177,31 @@ template <typename T> void Net::forward_t(int B, cudaStream_t s)
             gemm(kEpiResidual, map_ff_, l.ff2_w, false, B, d, ff, EpiArgs{l.ff2_b, nullptr, 1.f}, x_, xp, s);
             continue;
         }
-        launch_attention<T, T>(map_qkv_, static_cast<T*>(att_), B, d, a.heads, 1.f, err_word(), s, att_mode_);
+        launch_attention<T, T>(map_qkv_, static_cast<T*>(att_), B, d, a.heads, 1.f, err_word(), s, att_mode_,
+                               flip());
         amax(4 * i + 1, att_, nd, s);
         mark(kPOut, s);
         if (fuse) {
+            flip();
             gemm_resln(map_att_, l.out_w, rows, d, l.out_b, l.n2_g, l.n2_b, s);   // x += out; h = LN2(x)
         } else {
-            gemm(kEpiResidual, map_att_, l.out_w, false, rows, d, d, EpiArgs{l.out_b, nullptr, 1.f}, x_, d, s);
+            gemm(kEpiResidual, map_att_, l.out_w, false, rows, d, d, EpiArgs{l.out_b, nullptr, 1.f, flip()}, x_, d,
+                 s);
             mark(kPLn2, s);
-            launch_layernorm<T>(x_, l.n2_g, l.n2_b, h, rows, d, 1, 1.f, s);
+            launch_layernorm<T>(x_, l.n2_g, l.n2_b, h, rows, d, 1, 1.f, s, flip());
         }
         amax(4 * i + 2, h, nd, s);
         mark(kPFf1, s);
-        gemm(kEpiBiasGelu, map_h_, l.ff1_w, false, rows, ff, d, EpiArgs{l.ff1_b, nullptr, 1.f}, ff_, ff, s);
+        gemm(kEpiBiasGelu, map_h_, l.ff1_w, false, rows, ff, d, EpiArgs{l.ff1_b, nullptr, 1.f, flip()}, ff_, ff, s);
         amax(4 * i + 3, ff_, nf, s);
         mark(kPFf2, s);
         if (fuse && !last) {
             const LayerW& n = L_[static_cast<size_t>(i + 1)];
+            flip();
             gemm_resln(map_ff_, l.ff2_w, rows, ff, l.ff2_b, n.n1_g, n.n1_b, s);   // x += ff; h = next LN1(x)
         } else {
-            gemm(kEpiResidual, map_ff_, l.ff2_w, false, rows, d, ff, EpiArgs{l.ff2_b, nullptr, 1.f}, x_, d, s);
+            gemm(kEpiResidual, map_ff_, l.ff2_w, false, rows, d, ff, EpiArgs{l.ff2_b, nullptr, 1.f, flip()}, x_, d,
+                 s);
         }
     }
     mark(kPCls, s);
@@ -1214,12 +1228,15 @@ void Net::forward_f8(int B, cudaStream_t s)
     T* x = reinterpret_cast<T*>(x_);
     mark(kPEmbed, s);
     launch_embed_ln<F8, T>(w_, L_[0], d_in_, B, x, h, L_[0].inv_qkv, s);
+    int dir = 0;   // the row order of each kernel, opposite to its input's producer (as in forward_t)
+    auto flip = [&] { return dir ^= 1; };
     for (int i = 0; i < a.layers; ++i) {
         const LayerW& l = L_[static_cast<size_t>(i)];
         mark(kPLn1, s);
-        if (i > 0) launch_layernorm<F8, T>(x, l.n1_g, l.n1_b, h, rows, d, 1, l.inv_qkv, s);
+        if (i > 0) launch_layernorm<F8, T>(x, l.n1_g, l.n1_b, h, rows, d, 1, l.inv_qkv, s, flip());
         mark(kPQkv, s);
-        gemm(kEpiBias, map_h_, l.qkv_w, true, rows, 3 * d, d, EpiArgs{l.qkv_b, l.qkv_cs, 1.f}, qkv_, 3 * d, s);
+        gemm(kEpiBias, map_h_, l.qkv_w, true, rows, 3 * d, d, EpiArgs{l.qkv_b, l.qkv_cs, 1.f, flip()}, qkv_, 3 * d,
+             s);
         mark(kPAtt, s);
         if (i + 1 == a.layers && cls_only()) {
             // the CLS rows only, as in forward_t
@@ -1236,15 +1253,17 @@ void Net::forward_f8(int B, cudaStream_t s)
             gemm(kEpiResidual16, map_ff_, l.ff2_w, true, B, d, ff, EpiArgs{l.ff2_b, l.ff2_cs, 1.f}, x, xp, s);
             continue;
         }
-        launch_attention<T, F8>(map_qkv_, static_cast<F8*>(att_), B, d, a.heads, l.inv_out, err_word(), s, att_mode_);
+        launch_attention<T, F8>(map_qkv_, static_cast<F8*>(att_), B, d, a.heads, l.inv_out, err_word(), s, att_mode_,
+                                flip());
         mark(kPOut, s);
-        gemm(kEpiResidual16, map_att_, l.out_w, true, rows, d, d, EpiArgs{l.out_b, l.out_cs, 1.f}, x, d, s);
+        gemm(kEpiResidual16, map_att_, l.out_w, true, rows, d, d, EpiArgs{l.out_b, l.out_cs, 1.f, flip()}, x, d, s);
         mark(kPLn2, s);
-        launch_layernorm<F8, T>(x, l.n2_g, l.n2_b, h, rows, d, 1, l.inv_ff1, s);
+        launch_layernorm<F8, T>(x, l.n2_g, l.n2_b, h, rows, d, 1, l.inv_ff1, s, flip());
         mark(kPFf1, s);
-        gemm(kEpiGeluE4m3, map_h_, l.ff1_w, true, rows, ff, d, EpiArgs{l.ff1_b, l.ff1_cs, l.inv_ff2}, ff_, ff, s);
+        gemm(kEpiGeluE4m3, map_h_, l.ff1_w, true, rows, ff, d, EpiArgs{l.ff1_b, l.ff1_cs, l.inv_ff2, flip()}, ff_, ff,
+             s);
         mark(kPFf2, s);
-        gemm(kEpiResidual16, map_ff_, l.ff2_w, true, rows, d, ff, EpiArgs{l.ff2_b, l.ff2_cs, 1.f}, x, d, s);
+        gemm(kEpiResidual16, map_ff_, l.ff2_w, true, rows, d, ff, EpiArgs{l.ff2_b, l.ff2_cs, 1.f, flip()}, x, d, s);
     }
     mark(kPCls, s);
     launch_layernorm<T, T>(x, w_.ptr<float>("ln_g"), w_.ptr<float>("ln_b"), static_cast<T*>(cls_), B, d, kTokens, 1.f,

@@ -205,16 +205,17 @@ __device__ __forceinline__ void ln_row(int i, const XT* __restrict__ x, const fl
     ln_row_store<T, V>(v, d, g, b, h + (size_t)i * d, eps, mul);
 }
 
+// rev: the rows in descending order (rows the producer of x wrote last, still in L2, come first)
 template <typename T, int V, typename XT = float>
 __global__ void __launch_bounds__(256) layernorm_kernel(const XT* __restrict__ x, const float* __restrict__ g,
                                                         const float* __restrict__ b, T* __restrict__ h, int n,
-                                                        int row_stride, float eps, float mul)
+                                                        int row_stride, float eps, float mul, int rev)
 {
     griddep_wait();
     griddep_launch();
     const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (i >= n) return;
-    ln_row<T, V, XT>(i, x, g, b, h, row_stride, eps, mul);
+    ln_row<T, V, XT>(rev ? n - 1 - i : i, x, g, b, h, row_stride, eps, mul);
 }
 
 // ------------------------------------------------------------------------------------------------ attention
