@@ -845,6 +845,7 @@ private:
     unsigned int* amax_ = nullptr;
 
     int att_mode_ = -1;   // MAYFLY_CUDANET_ATT_TC when the handle was made (-1: the evaluator's choice)
+    bool alt_order_ = true;   // alternate the row order along the kernel chain (MAYFLY_CUDANET_ORDER=fwd: off)
     std::set<int> no_graph_;   // batch sizes whose capture failed: run eagerly
 
     // profiling marks
@@ -982,6 +983,10 @@ void Net::init(const std::string& path, int device)
         const char* g = std::getenv("MAYFLY_CUDANET_GRAPH");
         use_graph_ = !(g && std::strcmp(g, "0") == 0);
         att_mode_ = att_tc_env();
+        {
+            const char* e = std::getenv("MAYFLY_CUDANET_ORDER");
+            alt_order_ = !(e && std::strcmp(e, "fwd") == 0);
+        }
         RT(cudaStreamSynchronize(stream_));
     } catch (...) {
         release();
@@ -1152,7 +1157,7 @@ template <typename T> void Net::forward_t(int B, cudaStream_t s)
     // Each kernel of the chain walks its rows in the opposite order to the kernel that wrote its input, so it
     // starts on what is still in L2 (the producer's last rows); the outputs do not depend on the order.
     int dir = 0;
-    auto flip = [&] { return dir ^= 1; };
+    auto flip = [&] { return alt_order_ ? (dir ^= 1) : 0; };
     for (int i = 0; i < a.layers; ++i) {
         const LayerW& l = L_[static_cast<size_t>(i)];
         const bool last = i + 1 == a.layers;
@@ -1229,7 +1234,7 @@ void Net::forward_f8(int B, cudaStream_t s)
     mark(kPEmbed, s);
     launch_embed_ln<F8, T>(w_, L_[0], d_in_, B, x, h, L_[0].inv_qkv, s);
     int dir = 0;   // the row order of each kernel, opposite to its input's producer (as in forward_t)
-    auto flip = [&] { return dir ^= 1; };
+    auto flip = [&] { return alt_order_ ? (dir ^= 1) : 0; };
     for (int i = 0; i < a.layers; ++i) {
         const LayerW& l = L_[static_cast<size_t>(i)];
         mark(kPLn1, s);

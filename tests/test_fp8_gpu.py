@@ -275,3 +275,22 @@ def test_fp8_against_reference(f8nets, tag):
         again = run(net, b)
         for x, y in zip(got, again):
             assert np.array_equal(x, y)
+
+
+def test_row_order_does_not_change_outputs_f8(k, f8nets, tmp_path, monkeypatch):
+    """The FP8 pass with every kernel walking its rows forward (MAYFLY_CUDANET_ORDER=fwd) gives the same bits as
+    the default, which alternates the order along each layer's chain (438 boards)."""
+    from mayfly_chess_b200 import quant
+    net, st, _ = f8nets["full"]
+    b, _ = golden_case("full_seed1_fixed")
+    want = net.evaluate(b["ids"], b["cast"], b["hm"], b["ep"], b["I"], b["M"])
+    path = str(tmp_path / "full_e4m3.cnw")
+    quant.write_e4m3(path, st, W.FULL, quant.calibrate(st, W.FULL, _calib_batch()))
+    monkeypatch.setenv("MAYFLY_CUDANET_ORDER", "fwd")
+    fwd = k.CudaNet(path)
+    try:
+        got = fwd.evaluate(b["ids"], b["cast"], b["hm"], b["ep"], b["I"], b["M"])
+    finally:
+        fwd.close()
+    for x, y in zip(want, got):
+        assert np.array_equal(x, y)

@@ -195,6 +195,26 @@ def test_batch_sizes_and_slices(nets, B):
     assert np.abs(vs - vb[:B]).max() < 1e-4
 
 
+def test_row_order_does_not_change_outputs(nets, tmp_path, monkeypatch):
+    """Every other kernel of a layer's chain walks its rows (LayerNorm rows, the products' M blocks, the attention's
+    boards) in descending order, to start on what the kernel before it left in L2. A handle made with
+    MAYFLY_CUDANET_ORDER=fwd walks them all forward; both give the same bits (438 boards: 28,470 rows, many M
+    blocks of every product)."""
+    from mayfly_chess_b200 import cudanet_py
+    b, _ = golden_case("full_seed1_fixed")
+    want = run(nets[("full", "bf16")], b)
+    path = str(tmp_path / "full_bf16.cnw")
+    W.write_cnw(path, W.random_state(W.FULL, 1), W.FULL, "bf16")
+    monkeypatch.setenv("MAYFLY_CUDANET_ORDER", "fwd")
+    fwd = cudanet_py.CudaNet(path)
+    try:
+        got = run(fwd, b)
+    finally:
+        fwd.close()
+    for x, y in zip(want, got):
+        assert np.array_equal(x, y)
+
+
 def test_begin_end_pipeline(nets):
     net = nets[("full", "bf16")]
     b1, _ = golden_case("full_seed1_b64")
